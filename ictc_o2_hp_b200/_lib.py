@@ -1,0 +1,133 @@
+"""ctypes binding of libictc_o2_b200.so, the C-ABI declared in include/ictc_o2_b200.h.
+
+This is the only place Python touches the native library.  A missing library is a
+hard error: the package has no CPU or PyTorch fallback for the kernels.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+LIBRARY = Path(__file__).resolve().parent / "_lib" / "libictc_o2_b200.so"
+
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE = range(5)
+PARITY = {"canonical": 0, "full": 1}
+NORMALIZATION = {"component": 0, "norm": 1}
+
+_c_float_p = ctypes.POINTER(ctypes.c_float)
+_i32, _i64, _size = ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
+_vp = ctypes.c_void_p
+
+# name -> (restype, argtypes); must mirror include/ictc_o2_b200.h
+SIGNATURES = {
+    "ictc_o2_last_error": (ctypes.c_char_p, []),
+    "ictc_o2_abi_version": (_i32, []),
+    "ictc_o2_tp_weight_numel": (_i32, [_i32, _i32, _i32, ctypes.POINTER(_i64)]),
+    "ictc_o2_tp_path_table": (_i32, [_i32, _i32, ctypes.POINTER(_i32), _i32,
+                                     ctypes.POINTER(_i32)]),
+    "ictc_o2_tp_forward": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _vp]),
+    "ictc_o2_tp_backward_workspace": (_i32, [_i64, _i32, _i32, _i32, _i32,
+                                             ctypes.POINTER(_size)]),
+    "ictc_o2_tp_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _size, _i64, _i32,
+                                   _i32, _i32, _i32, _vp]),
+}
+
+_lock = threading.Lock()
+_handle = None
+
+
+class NativeError(RuntimeError):
+    """A CUDA or workspace failure reported by the native library."""
+
+
+def load() -> ctypes.CDLL:
+    """Loads the library once; raises if it has not been built."""
+    global _handle
+    if _handle is not None:
+        return _handle
+    with _lock:
+        if _handle is None:
+            path = Path(os.environ.get("ICTC_O2_B200_LIBRARY", LIBRARY))
+            if not path.exists():
+                raise RuntimeError(
+                    f"{path} is missing: build it with `python -m ictc_o2_hp_b200.build` "
+                    "(the kernels have no fallback)")
+            lib = ctypes.CDLL(str(path))
+            for name, (restype, argtypes) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype, fn.argtypes = restype, argtypes
+            _handle = lib
+    return _handle
+
+
+def check(status: int, what: str) -> None:
+    if status == OK:
+        return
+    message = load().ictc_o2_last_error().decode(errors="replace")
+    text = f"{what}: {message}"
+    if status == ERR_INVALID:
+        raise ValueError(text)
+    if status == ERR_UNSUPPORTED:
+        raise NotImplementedError(text)
+    raise NativeError(text)
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def tp_weight_numel(channels: int, m_max: int, parity: str) -> int:
+    out = _i64()
+    check(load().ictc_o2_tp_weight_numel(channels, m_max, PARITY[parity], ctypes.byref(out)),
+          "tp_weight_numel")
+    return int(out.value)
+
+
+def tp_path_table(m_max: int, parity: str) -> list[tuple]:
+    lib = load()
+    count = _i32()
+    check(lib.ictc_o2_tp_path_table(m_max, PARITY[parity], None, 0, ctypes.byref(count)),
+          "tp_path_table")
+    buf = (_i32 * (23 * count.value))()
+    check(lib.ictc_o2_tp_path_table(m_max, PARITY[parity], buf, count.value,
+                                    ctypes.byref(count)), "tp_path_table")
+    rows = []
+    for p in range(count.value):
+        r = buf[23 * p:23 * (p + 1)]
+        terms = tuple(tuple(r[7 + 4 * k:11 + 4 * k]) for k in range(r[6]))
+        rows.append((r[0], r[1], r[2], r[3], r[4], r[5], terms))
+    return rows
+
+
+def tp_forward(left, right, weight, out, channels, m_max, parity, normalization):
+    rows = left.shape[0]
+    check(load().ictc_o2_tp_forward(ptr(left), ptr(right), ptr(weight), ptr(out), rows,
+                                    channels, m_max, PARITY[parity], NORMALIZATION[normalization],
+                                    stream_of(left.device)), "tp_forward")
+
+
+def tp_backward_workspace(rows, channels, m_max, parity, device: torch.device) -> int:
+    out = _size()
+    check(load().ictc_o2_tp_backward_workspace(rows, channels, m_max, PARITY[parity],
+                                               device.index or 0, ctypes.byref(out)),
+          "tp_backward_workspace")
+    return int(out.value)
+
+
+def tp_backward(left, right, weight, grad_output, grad_left, grad_right, grad_weight,
+                workspace, channels, m_max, parity, normalization):
+    rows = left.shape[0]
+    check(load().ictc_o2_tp_backward(
+        ptr(left), ptr(right), ptr(weight), ptr(grad_output), ptr(grad_left), ptr(grad_right),
+        ptr(grad_weight), ptr(workspace), workspace.numel() if workspace is not None else 0,
+        rows, channels, m_max, PARITY[parity], NORMALIZATION[normalization],
+        stream_of(left.device)), "tp_backward")

@@ -1,0 +1,65 @@
+// Shared helpers for the C-ABI launchers: status codes, the per-thread error
+// message, device properties and small device utilities.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+
+#include "ictc_o2_b200.h"
+
+namespace ictc {
+
+// Records a formatted message for ictc_o2_last_error() and returns `code`.
+int fail(int code, const char* fmt, ...);
+
+// Converts a CUDA error (launch or query) into ICTC_ERR_CUDA with its name.
+int cuda_fail(cudaError_t err, const char* what);
+
+// SM count and the current device; cached per device.
+int sm_count(int device);
+
+inline bool aligned(const void* p, uintptr_t bytes) {
+  return (reinterpret_cast<uintptr_t>(p) % bytes) == 0;
+}
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Row layout of a flat TensorProduct operand ([N, width], layout 0 of the
+// reference, triton_o2.py:110-112): [0e: C][0o: C, full only][m = 1..M:
+// copies x C x 2].
+struct TpLayout {
+  int C;
+  int64_t width;
+  int fbase;    // offset of frequency 1
+  int fstride;  // offset step between consecutive frequencies
+};
+
+inline TpLayout tp_layout(int C, int m_max, bool full) {
+  TpLayout L;
+  L.C = C;
+  L.fbase = full ? 2 * C : C;
+  L.fstride = full ? 4 * C : 2 * C;
+  L.width = static_cast<int64_t>(L.fbase) + static_cast<int64_t>(m_max) * L.fstride;
+  return L;
+}
+
+// Normalization-dependent magnitude of each path class (see o2_paths.cuh).
+struct Mags {
+  float m[4];
+};
+
+inline Mags tp_mags(int normalization) {
+  const float r = 0.70710678118654752440f;
+  Mags g;
+  if (normalization == ICTC_NORM_COMPONENT) {
+    g.m[0] = 1.0f; g.m[1] = 1.0f; g.m[2] = r; g.m[3] = r;
+  } else {
+    g.m[0] = 1.0f; g.m[1] = r; g.m[2] = r; g.m[3] = 0.5f;
+  }
+  return g;
+}
+
+}  // namespace ictc

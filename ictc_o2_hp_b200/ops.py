@@ -1,0 +1,165 @@
+"""torch.library custom ops over the C-ABI kernels, with fake (meta) kernels for
+torch.compile and autograd formulas.
+
+Replaces the reference's ``o2_forward`` / ``o2_backward`` Triton ops
+(src/ictc_o2_hp/triton_o2.py:786-966, autograd :1035-1092).  The path metadata
+tensors and global metadata registry of the reference become plain integer and
+string arguments.  Inputs must be CUDA float32: there is no CPU fallback.
+Second derivatives recompute a differentiable PyTorch formula on the GPU, as
+the reference does (triton_o2.py:969-1069).
+"""
+
+from __future__ import annotations
+
+from functools import lru_cache
+
+import torch
+from torch import Tensor
+
+from . import _lib
+from ._algebra import MAGNITUDES, TpPlan
+
+NAMESPACE = "ictc_o2_b200"
+
+
+def require_cuda_float32(what: str, *tensors: Tensor) -> None:
+    device = tensors[0].device
+    for t in tensors:
+        if t.device.type != "cuda" or t.dtype != torch.float32:
+            raise TypeError(
+                f"{what} runs only on CUDA float32 tensors (this implementation has no CPU "
+                f"or other-dtype fallback); got {t.dtype} on {t.device}")
+        if t.device != device:
+            raise ValueError(f"{what}: all operands must be on one device")
+
+
+@lru_cache(maxsize=None)
+def tp_plan(channels: int, m_max: int, parity: str, normalization: str) -> TpPlan:
+    return TpPlan(channels, m_max, parity, normalization)
+
+
+# ----------------------------------------------------------------- TensorProduct
+
+
+@torch.library.custom_op(f"{NAMESPACE}::tp_forward", mutates_args=())
+def tp_forward(left: Tensor, right: Tensor, weight: Tensor, channels: int, m_max: int,
+               parity: str, normalization: str) -> Tensor:
+    """out[N, W] of TensorProduct on flat rows (triton_o2.py:786-875)."""
+    require_cuda_float32("TensorProduct", left, right, weight)
+    left, right, weight = left.contiguous(), right.contiguous(), weight.contiguous()
+    out = torch.empty_like(left)
+    with torch.cuda.device(left.device):
+        _lib.tp_forward(left, right, weight, out, channels, m_max, parity, normalization)
+    return out
+
+
+@tp_forward.register_fake
+def _tp_forward_fake(left, right, weight, channels, m_max, parity, normalization):
+    return torch.empty_like(left)
+
+
+@torch.library.custom_op(f"{NAMESPACE}::tp_backward", mutates_args=())
+def tp_backward(left: Tensor, right: Tensor, weight: Tensor, grad_output: Tensor, channels: int,
+                m_max: int, parity: str, normalization: str) -> tuple[Tensor, Tensor, Tensor]:
+    """(dx, dy, dw) of TensorProduct (triton_o2.py:878-966)."""
+    require_cuda_float32("TensorProduct backward", left, right, weight, grad_output)
+    left, right = left.contiguous(), right.contiguous()
+    weight, grad_output = weight.contiguous(), grad_output.contiguous()
+    grad_left, grad_right = torch.empty_like(left), torch.empty_like(right)
+    grad_weight = torch.empty_like(weight)
+    with torch.cuda.device(left.device):
+        size = _lib.tp_backward_workspace(left.shape[0], channels, m_max, parity, left.device)
+        workspace = torch.empty(max(size, 1), dtype=torch.uint8, device=left.device)
+        _lib.tp_backward(left, right, weight, grad_output, grad_left, grad_right, grad_weight,
+                         workspace, channels, m_max, parity, normalization)
+    return grad_left, grad_right, grad_weight
+
+
+@tp_backward.register_fake
+def _tp_backward_fake(left, right, weight, grad_output, channels, m_max, parity, normalization):
+    return torch.empty_like(left), torch.empty_like(right), torch.empty_like(weight)
+
+
+def _tp_setup(ctx, inputs, output):
+    left, right, weight, channels, m_max, parity, normalization = inputs
+    ctx.save_for_backward(left, right, weight)
+    ctx.config = (channels, m_max, parity, normalization)
+
+
+def _tp_autograd(ctx, grad_output):
+    left, right, weight = ctx.saved_tensors
+    gx, gy, gw = tp_backward(left, right, weight, grad_output.contiguous(), *ctx.config)
+    return gx, gy, gw, None, None, None, None
+
+
+tp_forward.register_autograd(_tp_autograd, setup_context=_tp_setup)
+
+
+def torch_tp_flat(left: Tensor, right: Tensor, weight: Tensor, plan: TpPlan) -> Tensor:
+    """Differentiable PyTorch formula of the same map, used for second derivatives
+    only (the role of triton_o2.py:969-1032)."""
+    n, C = left.shape[0], plan.channels
+    offsets = plan.key_offsets()
+    mags = MAGNITUDES[plan.normalization]
+
+    def split(value):
+        blocks = {}
+        for b in plan.blocks:
+            o = offsets[b.key]
+            v = value[:, o:o + b.multiplicity * b.irrep_dimension].reshape(
+                n, b.parity_copies, C, b.irrep_dimension)
+            if b.parity_copies == 2:
+                v = torch.cat((v[:, :1], torch.stack((-v[:, 1, :, 1], v[:, 1, :, 0]), -1)[:, None]),
+                              dim=1)
+            blocks[b.key] = v
+        return blocks
+
+    first, second = split(left), split(right)
+    out = {}
+    for p in plan.paths:
+        copies = plan.block_by_key[p.key3].parity_copies
+        a, b = first[p.key1][:, :copies], second[p.key2][:, :copies]
+        comps = [None] * (1 if p.key3[0] == "scalar" else 2)
+        for i, j, k, s in p.terms:
+            term = (s * mags[p.cls]) * a[..., i] * b[..., j]
+            comps[k] = term if comps[k] is None else comps[k] + term
+        value = torch.stack(comps, -1) * weight[p.weight_start:p.weight_stop].view(
+            1, copies, C, 1)
+        out[p.key3] = value if p.key3 not in out else out[p.key3] + value
+    pieces = []
+    for b in plan.blocks:
+        v = out.get(b.key)
+        if v is None:
+            v = left.new_zeros(n, b.parity_copies, C, b.irrep_dimension)
+        if b.parity_copies == 2:
+            v = torch.cat((v[:, :1], torch.stack((v[:, 1, :, 1], -v[:, 1, :, 0]), -1)[:, None]),
+                          dim=1)
+        pieces.append(v.reshape(n, -1))
+    return torch.cat(pieces, dim=-1)
+
+
+def _tp_backward_setup(ctx, inputs, output):
+    left, right, weight, grad_output, channels, m_max, parity, normalization = inputs
+    ctx.save_for_backward(left, right, weight, grad_output)
+    ctx.config = (channels, m_max, parity, normalization)
+    ctx.set_materialize_grads(False)
+
+
+def _tp_double_backward(ctx, dd_left, dd_right, dd_weight):
+    left, right, weight, grad_output = ctx.saved_tensors
+    selected = [(i, c) for i, c in enumerate((dd_left, dd_right, dd_weight)) if c is not None]
+    if not selected:
+        return (None,) * 8
+    plan = tp_plan(*ctx.config)
+    with torch.enable_grad():
+        operands = tuple(v.detach().requires_grad_(True)
+                         for v in (left, right, weight, grad_output))
+        value = torch_tp_flat(*operands[:3], plan)
+        first = torch.autograd.grad(value, operands[:3], operands[3], create_graph=True)
+        second = torch.autograd.grad(tuple(first[i] for i, _ in selected), operands,
+                                     grad_outputs=tuple(c for _, c in selected),
+                                     allow_unused=True)
+    return (*second, None, None, None, None)
+
+
+tp_backward.register_autograd(_tp_double_backward, setup_context=_tp_backward_setup)

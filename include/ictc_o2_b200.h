@@ -1,0 +1,88 @@
+/*
+ * C ABI of the B200-native ICTC-O2 tensor-product kernels (libictc_o2_b200.so).
+ *
+ * Every entry point takes plain device pointers and sizes, launches on the
+ * given CUDA stream (NULL = legacy default stream), never aborts, and returns
+ * an ICTC status code; ictc_o2_last_error() gives a message for the calling
+ * thread.  All tensors are contiguous row-major FP32.  The library allocates
+ * no device memory in these entry points: callers pass outputs and workspace.
+ *
+ * The functions replace the reference's Triton custom ops (paths relative to
+ * the reference project root); path metadata tensors and the process-global
+ * metadata registry of the reference become (channels, m_max, parity,
+ * normalization) integers, from which the library derives its compiled tables.
+ */
+#ifndef ICTC_O2_B200_H_
+#define ICTC_O2_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ICTC_API __attribute__((visibility("default")))
+#else
+#define ICTC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  ICTC_OK = 0,
+  ICTC_ERR_INVALID = 1,      /* bad argument: size, null pointer, alignment */
+  ICTC_ERR_UNSUPPORTED = 2,  /* configuration without a compiled kernel */
+  ICTC_ERR_CUDA = 3,         /* CUDA launch or runtime error */
+  ICTC_ERR_WORKSPACE = 4     /* workspace smaller than the queried size */
+};
+
+enum { ICTC_PARITY_CANONICAL = 0, ICTC_PARITY_FULL = 1 };
+enum { ICTC_NORM_COMPONENT = 0, ICTC_NORM_NORM = 1 };
+
+/* Message describing the last non-OK status returned on this thread. */
+ICTC_API const char* ictc_o2_last_error(void);
+
+/* Library ABI version (major * 100 + minor). */
+ICTC_API int32_t ictc_o2_abi_version(void);
+
+/* ---------------------------------------------------------------- TensorProduct
+ * Flat channel-major operands of width W = C * (2 * m_max + 1) * (full ? 2 : 1),
+ * layout [0e: C][0o: C (full)][m = 1..m_max: copy (1 or 2) x C x 2]
+ * (reference: src/ictc_o2_hp/api.py:43-54, triton_o2.py:1169-1201).
+ */
+
+/* Packed weight length (reference: fast_o2.py:152-167, native_o2.py:101-117). */
+ICTC_API int32_t ictc_o2_tp_weight_numel(int32_t channels, int32_t m_max, int32_t parity,
+                                int64_t* numel);
+
+/* Compiled path table, for host-side consistency checks: for each block path,
+ * 7 + 4 * 4 int32 = {in1 slot, in2 slot, out slot, class, unit offset, copied,
+ * nterms, then 4 x (i, j, k, sign)}.  `count` receives the path count. */
+ICTC_API int32_t ictc_o2_tp_path_table(int32_t m_max, int32_t parity, int32_t* table,
+                              int32_t capacity_paths, int32_t* count);
+
+/* out[N, W] = TP(left, right; weight).  Replaces the o2_forward custom op
+ * (reference: src/ictc_o2_hp/triton_o2.py:786-875). */
+ICTC_API int32_t ictc_o2_tp_forward(const float* left, const float* right, const float* weight,
+                           float* output, int64_t rows, int32_t channels, int32_t m_max,
+                           int32_t parity, int32_t normalization, void* stream);
+
+/* Workspace bytes needed by ictc_o2_tp_backward on `device` for these sizes. */
+ICTC_API int32_t ictc_o2_tp_backward_workspace(int64_t rows, int32_t channels, int32_t m_max,
+                                      int32_t parity, int32_t device, size_t* bytes);
+
+/* Full first-order VJP: grad_left, grad_right [N, W] and grad_weight [numel]
+ * (deterministic fixed-order reduction over rows).  Replaces the o2_backward
+ * custom op (reference: src/ictc_o2_hp/triton_o2.py:878-966); N = 0 writes a
+ * zero grad_weight (triton_o2.py:890-891). */
+ICTC_API int32_t ictc_o2_tp_backward(const float* left, const float* right, const float* weight,
+                            const float* grad_output, float* grad_left, float* grad_right,
+                            float* grad_weight, void* workspace, size_t workspace_bytes,
+                            int64_t rows, int32_t channels, int32_t m_max, int32_t parity,
+                            int32_t normalization, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ICTC_O2_B200_H_ */
