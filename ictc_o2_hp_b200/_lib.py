@@ -27,6 +27,7 @@ _vp = ctypes.c_void_p
 SIGNATURES = {
     "ictc_o2_last_error": (ctypes.c_char_p, []),
     "ictc_o2_abi_version": (_i32, []),
+    "ictc_o2_device_error": (_i32, [ctypes.POINTER(_i32)]),
     "ictc_o2_tp_weight_numel": (_i32, [_i32, _i32, _i32, ctypes.POINTER(_i64)]),
     "ictc_o2_tp_path_table": (_i32, [_i32, _i32, ctypes.POINTER(_i32), _i32,
                                      ctypes.POINTER(_i32)]),
@@ -83,6 +84,13 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 def stream_of(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def device_error() -> int:
+    """Reads and clears the kernels' device-side error flag (0 = none)."""
+    code = _i32()
+    check(load().ictc_o2_device_error(ctypes.byref(code)), "device_error")
+    return int(code.value)
 
 
 def tp_weight_numel(channels: int, m_max: int, parity: str) -> int:

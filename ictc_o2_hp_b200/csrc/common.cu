@@ -35,8 +35,44 @@ int sm_count(int device) {
   return cache[device];
 }
 
+int allow_smem(const void* kernel, size_t bytes) {
+  static std::mutex mu;
+  static const void* seen[256] = {};
+  static size_t granted[256] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  int slot = -1;
+  for (int i = 0; i < 256; ++i) {
+    if (seen[i] == kernel) {
+      if (granted[i] >= bytes) return ICTC_OK;
+      slot = i;
+      break;
+    }
+    if (seen[i] == nullptr) {
+      slot = i;
+      break;
+    }
+  }
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(bytes));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+  if (slot >= 0) {
+    seen[slot] = kernel;
+    granted[slot] = bytes;
+  }
+  return ICTC_OK;
+}
+
 }  // namespace ictc
 
 extern "C" const char* ictc_o2_last_error(void) { return ictc::g_message; }
+
+extern "C" int32_t ictc_o2_device_error(int32_t* code) {
+  if (code == nullptr) return ictc::fail(ICTC_ERR_INVALID, "code is null");
+  int value = 0;
+  const int st = ictc::tp_take_device_error(&value);
+  if (st != ICTC_OK) return st;
+  *code = value;
+  return ICTC_OK;
+}
 
 extern "C" int32_t ictc_o2_abi_version(void) { return 100; }

@@ -21,6 +21,13 @@ int cuda_fail(cudaError_t err, const char* what);
 // SM count and the current device; cached per device.
 int sm_count(int device);
 
+// Reads and clears the device error flag of the TensorProduct kernels on the
+// current device (nonzero: a bounded wait ran out).
+int tp_take_device_error(int* code);
+
+// Opts a kernel into `bytes` of dynamic shared memory (cached per kernel).
+int allow_smem(const void* kernel, size_t bytes);
+
 inline bool aligned(const void* p, uintptr_t bytes) {
   return (reinterpret_cast<uintptr_t>(p) % bytes) == 0;
 }

@@ -167,11 +167,30 @@ constexpr PathTable build_table(int m_max, bool full) {
   return tab;
 }
 
+// A permutation of the paths of a table.
+struct PathOrder {
+  int idx[kMaxPaths] = {};
+};
+
+// Paths grouped by first-input slot (stable): in the adjoint the gradient of a
+// first-input slot is complete once its group is done, which shortens register
+// live ranges.
+constexpr PathOrder by_first_input(const PathTable& t) {
+  PathOrder o{};
+  int n = 0;
+  for (int slot = 0; slot <= 2 * kMaxOrder + 1; ++slot)
+    for (int p = 0; p < t.n; ++p)
+      if (t.p[p].in1 == slot) o.idx[n++] = p;
+  return o;
+}
+
 template <int M, bool FULL>
 struct Paths {
   static constexpr PathTable table = build_table(M, FULL);
   static constexpr int n = table.n;
   static constexpr int slots = 2 * M + 2;
+  static constexpr PathOrder vjp = by_first_input(table);
+  static constexpr int chunks = (n + 3) / 4;  // float4 chunks of per-thread weights
 };
 
 // Compile-time loop: f(std::integral_constant<int, I>) for I in [0, N).

@@ -9,30 +9,41 @@
 // warps (lanes 0-15: copy 0, lanes 16-31: copy 1) and run the same frequency-
 // output paths in lockstep; only the scalar-output paths (world 0) diverge.
 //
-// A warp keeps the same channel group for its whole life (the grid holds a
-// multiple of `groups` warps), so its path weights stay in registers in the
-// forward pass and its weight-gradient accumulators stay in registers in the
-// backward pass.  The weight gradient is reduced deterministically: each warp
-// slot writes one partial row, then a second kernel sums the slots in a fixed
-// order (reference: two-stage FP32 reduction, triton_o2.py:744-780, 948-959).
+// A warp keeps the same channel group for its whole life, so its path weights
+// stay in registers in the forward pass and its weight-gradient accumulators
+// stay in registers in the backward pass.  The weight gradient is reduced
+// deterministically: every warp "slot" writes one partial row, then a second
+// kernel sums the slots in a fixed order (reference: two-stage FP32 reduction,
+// triton_o2.py:744-780, 948-959).
+//
+// Two kernel families share this per-row arithmetic:
+//   * staged: persistent CTAs (one per SM) that stream blocks of whole rows into
+//     shared memory with bulk asynchronous copies (TMA) through an mbarrier ring,
+//     so HBM latency hides behind the arithmetic of earlier rows;
+//   * direct: plain coalesced global loads, for operands that are not 16-byte
+//     aligned or rows wider than one CTA.
 #include <cuda_runtime.h>
 
 #include <cstring>
+#include <initializer_list>
 
 #include "common.cuh"
 #include "o2_paths.cuh"
+#include "tma.cuh"
 
 namespace ictc {
 
 namespace {
 
-constexpr int kThreads = 128;  // 4 warps per CTA
-#ifndef ICTC_FENCE_EVERY
-#define ICTC_FENCE_EVERY 8
-#endif
-constexpr int kFenceEvery = ICTC_FENCE_EVERY;
+constexpr int kDirectThreads = 128;  // 4 warps per CTA (direct kernels)
+constexpr int kStagedWarps = 8;      // max warps of a staged CTA
+constexpr size_t kStagedSmemBudget = 220 * 1024;
+constexpr int kBarrierBytes = 128;   // mbarrier area at the start of dynamic smem
+constexpr int kMaxStages = 4;
 
-__device__ __forceinline__ float2 ld2(const float* p, bool vec2) {
+// ------------------------------------------------------------ memory helpers
+
+__device__ __forceinline__ float2 ldg2(const float* p, bool vec2) {
   if (vec2) return __ldg(reinterpret_cast<const float2*>(p));
   return make_float2(__ldg(p), __ldg(p + 1));
 }
@@ -55,16 +66,33 @@ __device__ __forceinline__ void st2(float* p, float a, float b, bool vec2) {
   }
 }
 
+// Source of a row's values: global memory (read-only path) or a shared-memory
+// copy of the row.
+struct GlobalRow {
+  const float* p;
+  bool vec2;
+  __device__ __forceinline__ float ld(int i) const { return __ldg(p + i); }
+  __device__ __forceinline__ float2 ld2(int i) const { return ldg2(p + i, vec2); }
+};
+
+struct SharedRow {
+  const float* p;
+  __device__ __forceinline__ float ld(int i) const { return p[i]; }
+  __device__ __forceinline__ float2 ld2(int i) const {
+    return *reinterpret_cast<const float2*>(p + i);
+  }
+};
+
 // Slot vector of channel c in world q, in the canonical basis: the odd copy
 // (r0, r1) is read as (-r1, r0) (reference fast_o2.py:61-66).
-template <int M, bool FULL>
-__device__ __forceinline__ void load_slots(const float* __restrict__ row, const TpLayout& L,
-                                           int c, int q, bool vec2, float (&v)[2 * M + 2]) {
-  v[0] = __ldg(row + c);
-  v[1] = FULL ? __ldg(row + L.C + c) : 0.0f;
+template <int M, bool FULL, class Row>
+__device__ __forceinline__ void load_slots(const Row& row, const TpLayout& L, int c, int q,
+                                           float (&v)[2 * M + 2]) {
+  v[0] = row.ld(c);
+  v[1] = FULL ? row.ld(L.C + c) : 0.0f;
 #pragma unroll
   for (int m = 1; m <= M; ++m) {
-    const float2 r = ld2(row + L.fbase + (m - 1) * L.fstride + 2 * (q * L.C + c), vec2);
+    const float2 r = row.ld2(L.fbase + (m - 1) * L.fstride + 2 * (q * L.C + c));
     v[2 * m] = q ? -r.y : r.x;
     v[2 * m + 1] = q ? r.x : r.y;
   }
@@ -85,6 +113,8 @@ __device__ __forceinline__ void store_slots(float* __restrict__ row, const TpLay
     st2(p, q ? v[2 * m + 1] : v[2 * m], q ? -v[2 * m] : v[2 * m + 1], vec2);
   }
 }
+
+// ------------------------------------------------------------ path arithmetic
 
 // Index of the weight used by path I for channel c in world q.
 template <int M, bool FULL, int I>
@@ -122,12 +152,13 @@ __device__ __forceinline__ void mac(float& acc, float x, float y) {
 // Forward contribution of path I: o[out + k] += w * sum_terms sign * a_i * b_j.
 template <int M, bool FULL, int I>
 __device__ __forceinline__ void path_forward(const float* a, const float* b, float* o, float w) {
-  constexpr ChanPath cp = Paths<M, FULL>::table.p[I];
+  using P = Paths<M, FULL>;
+  constexpr ChanPath cp = P::table.p[I];
   float s[2];
   static_for<cp.nt>([&](auto T) {
-    constexpr Term t = Paths<M, FULL>::table.p[I].t[T];
-    mac<first_term<M, FULL, I, T, 0>(), t.s>(s[t.k], a[Paths<M, FULL>::table.p[I].in1 + t.i],
-                                              b[Paths<M, FULL>::table.p[I].in2 + t.j]);
+    constexpr Term t = P::table.p[I].t[T];
+    mac<first_term<M, FULL, I, T, 0>(), t.s>(s[t.k], a[P::table.p[I].in1 + t.i],
+                                              b[P::table.p[I].in2 + t.j]);
   });
   o[cp.out] = fmaf(w, s[0], o[cp.out]);
   if constexpr (slot_dim(cp.out) == 2) o[cp.out + 1] = fmaf(w, s[1], o[cp.out + 1]);
@@ -136,13 +167,14 @@ __device__ __forceinline__ void path_forward(const float* a, const float* b, flo
 // First-order adjoint of path I for one row: dx, dy and the weight-gradient
 // accumulator.  Three algebraically equal factorizations; the cheapest for the
 // path's shape is chosen at compile time:
-//   form 0:  s_k = sum a b,  acc += g.s,  dx_i += (w g_k) b_j,  dy_j += (w g_k) a_i
+//   form 0:   s_k = sum a b,  acc += g.s,  dx_i += (w g_k) b_j,  dy_j += (w g_k) a_i
 //   form 1/2: t_i = sum b_j g_k,  u_j = sum a_i g_k,  dx += w t,  dy += w u,
 //             acc += a.t (form 1) or b.u (form 2)
 template <int M, bool FULL, int I>
 __device__ __forceinline__ void path_vjp(const float* a, const float* b, const float* g,
                                          float* dx, float* dy, float& acc, float w) {
-  constexpr ChanPath cp = Paths<M, FULL>::table.p[I];
+  using P = Paths<M, FULL>;
+  constexpr ChanPath cp = P::table.p[I];
   constexpr int d1 = slot_dim(cp.in1), d2 = slot_dim(cp.in2), d3 = slot_dim(cp.out);
   constexpr int cost0 = 2 * d3 + 3 * cp.nt;
   constexpr int cost1 = 2 * cp.nt + 2 * d1 + d2;
@@ -150,9 +182,9 @@ __device__ __forceinline__ void path_vjp(const float* a, const float* b, const f
   if constexpr (cost0 <= cost1 && cost0 <= cost2) {
     float s[2];
     static_for<cp.nt>([&](auto T) {
-      constexpr Term t = Paths<M, FULL>::table.p[I].t[T];
-      mac<first_term<M, FULL, I, T, 0>(), t.s>(s[t.k], a[Paths<M, FULL>::table.p[I].in1 + t.i],
-                                                b[Paths<M, FULL>::table.p[I].in2 + t.j]);
+      constexpr Term t = P::table.p[I].t[T];
+      mac<first_term<M, FULL, I, T, 0>(), t.s>(s[t.k], a[P::table.p[I].in1 + t.i],
+                                                b[P::table.p[I].in2 + t.j]);
     });
     float wg[2];
     acc = fmaf(g[cp.out], s[0], acc);
@@ -162,19 +194,19 @@ __device__ __forceinline__ void path_vjp(const float* a, const float* b, const f
       wg[1] = w * g[cp.out + 1];
     }
     static_for<cp.nt>([&](auto T) {
-      constexpr Term t = Paths<M, FULL>::table.p[I].t[T];
-      constexpr int i1 = Paths<M, FULL>::table.p[I].in1 + t.i;
-      constexpr int i2 = Paths<M, FULL>::table.p[I].in2 + t.j;
+      constexpr Term t = P::table.p[I].t[T];
+      constexpr int i1 = P::table.p[I].in1 + t.i;
+      constexpr int i2 = P::table.p[I].in2 + t.j;
       mac<false, t.s>(dx[i1], wg[t.k], b[i2]);
       mac<false, t.s>(dy[i2], wg[t.k], a[i1]);
     });
   } else {
     float tv[2], uv[2];
     static_for<cp.nt>([&](auto T) {
-      constexpr Term t = Paths<M, FULL>::table.p[I].t[T];
-      constexpr int i1 = Paths<M, FULL>::table.p[I].in1 + t.i;
-      constexpr int i2 = Paths<M, FULL>::table.p[I].in2 + t.j;
-      constexpr int i3 = Paths<M, FULL>::table.p[I].out + t.k;
+      constexpr Term t = P::table.p[I].t[T];
+      constexpr int i1 = P::table.p[I].in1 + t.i;
+      constexpr int i2 = P::table.p[I].in2 + t.j;
+      constexpr int i3 = P::table.p[I].out + t.k;
       mac<first_term<M, FULL, I, T, 1>(), t.s>(tv[t.i], b[i2], g[i3]);
       mac<first_term<M, FULL, I, T, 2>(), t.s>(uv[t.j], a[i1], g[i3]);
     });
@@ -188,132 +220,347 @@ __device__ __forceinline__ void path_vjp(const float* a, const float* b, const f
   }
 }
 
+// Loads the register-resident path weights of (channel c, world q), magnitude
+// folded in.  Unused entries (scalar-output paths in world 1) are zero.
 template <int M, bool FULL>
-__global__ void __launch_bounds__(kThreads)
-    tp_forward_kernel(const float* __restrict__ x, const float* __restrict__ y,
-                      const float* __restrict__ w, float* __restrict__ out, int64_t rows,
-                      TpLayout L, Mags mags, int groups, int64_t nwarps, int64_t slots,
-                      bool vec2) {
+__device__ __forceinline__ void load_weights(const float* __restrict__ w, const TpLayout& L,
+                                             const Mags& mags, int c, int q, bool active,
+                                             float (&wr)[Paths<M, FULL>::n]) {
   using P = Paths<M, FULL>;
-  constexpr int S = 2 * M + 2;
-  constexpr int CPW = FULL ? 16 : 32;
-  const int lane = threadIdx.x & 31;
-  const int q = FULL ? (lane >> 4) : 0;
-  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  if (gw >= nwarps) return;
-  const int c_raw = static_cast<int>(gw % groups) * CPW + (FULL ? (lane & 15) : lane);
-  const bool active = c_raw < L.C;
-  const int c = active ? c_raw : 0;
-
-  // Path weights of this channel and world, with the path magnitude folded in.
-  float wr[P::n];
   static_for<P::n>([&](auto I) {
     constexpr ChanPath cp = P::table.p[I];
     const bool used = active && (!FULL || cp.copied || q == 0);
     wr[I] = used ? __ldg(w + weight_index<M, FULL, I>(L.C, c, q)) * mags.m[cp.cls] : 0.0f;
   });
+}
 
+// Forward of one (row, channel, world): o = sum over paths.
+template <int M, bool FULL>
+__device__ __forceinline__ void row_forward(const float (&a)[2 * M + 2],
+                                            const float (&b)[2 * M + 2],
+                                            const float (&wr)[Paths<M, FULL>::n], int q,
+                                            float (&o)[2 * M + 2]) {
+  using P = Paths<M, FULL>;
+#pragma unroll
+  for (int s = 0; s < 2 * M + 2; ++s) o[s] = 0.0f;
+  static_for<P::n>([&](auto I) {
+    if (FULL && !P::table.p[I].copied && q != 0) return;  // scalar outputs: world 0 only
+    path_forward<M, FULL, I>(a, b, o, wr[I]);
+  });
+}
+
+// VJP of one (row, channel, world).  Paths run grouped by first-input slot
+// (Paths::vjp); the magnitude-scaled weights of this thread sit in that order as
+// float4 chunks: chunk k of thread t at wsrc[k * T + t] (see prescale_kernel).
+template <int M, bool FULL>
+__device__ __forceinline__ void row_vjp(const float (&a)[2 * M + 2], const float (&b)[2 * M + 2],
+                                        const float (&g)[2 * M + 2], const float4* wsrc, int T,
+                                        int t, int q, float (&dx)[2 * M + 2],
+                                        float (&dy)[2 * M + 2],
+                                        float (&acc)[Paths<M, FULL>::n]) {
+  using P = Paths<M, FULL>;
+#pragma unroll
+  for (int s = 0; s < 2 * M + 2; ++s) {
+    dx[s] = 0.0f;
+    dy[s] = 0.0f;
+  }
+  float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  static_for<P::n>([&](auto K) {
+    constexpr int I = P::vjp.idx[K];
+    if constexpr (K % 4 == 0) w4 = wsrc[(K / 4) * T + t];
+    if (FULL && !P::table.p[I].copied && q != 0) return;  // scalar outputs: world 0 only
+    const float wv = K % 4 == 0 ? w4.x : (K % 4 == 1 ? w4.y : (K % 4 == 2 ? w4.z : w4.w));
+    path_vjp<M, FULL, I>(a, b, g, dx, dy, acc[K], wv);
+  });
+  if (FULL) {
+    // World 1 reaches the scalars through scalar x frequency paths.
+    dx[0] += __shfl_xor_sync(0xffffffffu, dx[0], 16);
+    dx[1] += __shfl_xor_sync(0xffffffffu, dx[1], 16);
+    dy[0] += __shfl_xor_sync(0xffffffffu, dy[0], 16);
+    dy[1] += __shfl_xor_sync(0xffffffffu, dy[1], 16);
+  }
+}
+
+// Writes the weight-gradient accumulators of one thread (in Paths::vjp order)
+// to its partial row.
+template <int M, bool FULL>
+__device__ __forceinline__ void store_partial(float* __restrict__ dst, const TpLayout& L,
+                                              const Mags& mags, int c, int q,
+                                              const float (&acc)[Paths<M, FULL>::n]) {
+  using P = Paths<M, FULL>;
+  static_for<P::n>([&](auto K) {
+    constexpr int I = P::vjp.idx[K];
+    constexpr ChanPath cp = P::table.p[I];
+    if (FULL && !cp.copied && q != 0) return;
+    dst[weight_index<M, FULL, I>(L.C, c, q)] = acc[K] * mags.m[cp.cls];
+  });
+}
+
+// Lane -> (channel, world) of a warp that owns channel group `group`.
+template <bool FULL>
+struct LaneMap {
+  int q, c;
+  bool active;
+  __device__ __forceinline__ LaneMap(int group, int lane, int C) {
+    constexpr int CPW = FULL ? 16 : 32;
+    q = FULL ? (lane >> 4) : 0;
+    const int raw = group * CPW + (FULL ? (lane & 15) : lane);
+    active = raw < C;
+    c = active ? raw : 0;  // inactive lanes compute on channel 0 and store nothing
+  }
+};
+
+// ------------------------------------------------------------ direct kernels
+
+template <int M, bool FULL>
+__global__ void __launch_bounds__(kDirectThreads)
+    tp_forward_direct(const float* __restrict__ x, const float* __restrict__ y,
+                      const float* __restrict__ w, float* __restrict__ out, int64_t rows,
+                      TpLayout L, Mags mags, int groups, int64_t nwarps, int64_t slots,
+                      bool vec2) {
+  constexpr int S = 2 * M + 2;
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (gw >= nwarps) return;
+  const LaneMap<FULL> lm(static_cast<int>(gw % groups), lane, L.C);
+  float wr[Paths<M, FULL>::n];
+  load_weights<M, FULL>(w, L, mags, lm.c, lm.q, lm.active, wr);
   for (int64_t row = gw / groups; row < rows; row += slots) {
     float a[S], b[S], o[S];
-    load_slots<M, FULL>(x + row * L.width, L, c, q, vec2, a);
-    load_slots<M, FULL>(y + row * L.width, L, c, q, vec2, b);
-#pragma unroll
-    for (int s = 0; s < S; ++s) o[s] = 0.0f;
-    static_for<P::n>([&](auto I) {
-      if (FULL && !P::table.p[I].copied && q != 0) return;  // scalar outputs: world 0 only
-      path_forward<M, FULL, I>(a, b, o, wr[I]);
-    });
-    if (active) store_slots<M, FULL>(out + row * L.width, L, c, q, vec2, o);
+    load_slots<M, FULL>(GlobalRow{x + row * L.width, vec2}, L, lm.c, lm.q, a);
+    load_slots<M, FULL>(GlobalRow{y + row * L.width, vec2}, L, lm.c, lm.q, b);
+    row_forward<M, FULL>(a, b, wr, lm.q, o);
+    if (lm.active) store_slots<M, FULL>(out + row * L.width, L, lm.c, lm.q, vec2, o);
   }
 }
 
 template <int M, bool FULL>
-__global__ void __launch_bounds__(kThreads)
-    tp_backward_kernel(const float* __restrict__ x, const float* __restrict__ y,
-                       const float* __restrict__ ws, const float* __restrict__ go,
+__global__ void __launch_bounds__(kDirectThreads)
+    tp_backward_direct(const float* __restrict__ x, const float* __restrict__ y,
+                       const float4* __restrict__ ws, const float* __restrict__ go,
                        float* __restrict__ gx, float* __restrict__ gy,
                        float* __restrict__ partial, int64_t numel, int64_t rows, TpLayout L,
                        Mags mags, int groups, int64_t nwarps, int64_t slots, bool vec2) {
   using P = Paths<M, FULL>;
   constexpr int S = 2 * M + 2;
-  constexpr int CPW = FULL ? 16 : 32;
   const int lane = threadIdx.x & 31;
-  const int q = FULL ? (lane >> 4) : 0;
   const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (gw >= nwarps) return;  // whole warps only: nwarps counts warps
-  const int c_raw = static_cast<int>(gw % groups) * CPW + (FULL ? (lane & 15) : lane);
-  const bool active = c_raw < L.C;
-  const int c = active ? c_raw : 0;
+  const LaneMap<FULL> lm(static_cast<int>(gw % groups), lane, L.C);
   const int64_t slot = gw / groups;
-
   float acc[P::n];
 #pragma unroll
   for (int i = 0; i < P::n; ++i) acc[i] = 0.0f;
-
   for (int64_t row = slot; row < rows; row += slots) {
     float a[S], b[S], g[S], dx[S], dy[S];
-    load_slots<M, FULL>(x + row * L.width, L, c, q, vec2, a);
-    load_slots<M, FULL>(y + row * L.width, L, c, q, vec2, b);
+    load_slots<M, FULL>(GlobalRow{x + row * L.width, vec2}, L, lm.c, lm.q, a);
+    load_slots<M, FULL>(GlobalRow{y + row * L.width, vec2}, L, lm.c, lm.q, b);
     // The output twist (v0, v1) -> (v1, -v0) has the adjoint g -> (-g1, g0),
     // which is the same map as the input read.
-    load_slots<M, FULL>(go + row * L.width, L, c, q, vec2, g);
-#pragma unroll
-    for (int s = 0; s < S; ++s) {
-      dx[s] = 0.0f;
-      dy[s] = 0.0f;
-    }
-    static_for<P::n>([&](auto I) {
-      if (FULL && !P::table.p[I].copied && q != 0) return;  // scalar outputs: world 0 only
-      const float wv = ld_stream(ws + weight_index<M, FULL, I>(L.C, c, q));
-      path_vjp<M, FULL, I>(a, b, g, dx, dy, acc[I], wv);
-      // Scheduling fence: keeps the weight loads of later paths from being
-      // issued early, which would raise register pressure past the budget.
-      if constexpr (I % kFenceEvery == kFenceEvery - 1) asm volatile("" ::: "memory");
-    });
-    if (FULL) {
-      // World 1 reaches the scalars through scalar x frequency paths.
-      dx[0] += __shfl_xor_sync(0xffffffffu, dx[0], 16);
-      dx[1] += __shfl_xor_sync(0xffffffffu, dx[1], 16);
-      dy[0] += __shfl_xor_sync(0xffffffffu, dy[0], 16);
-      dy[1] += __shfl_xor_sync(0xffffffffu, dy[1], 16);
-    }
-    if (active) {
-      store_slots<M, FULL>(gx + row * L.width, L, c, q, vec2, dx);
-      store_slots<M, FULL>(gy + row * L.width, L, c, q, vec2, dy);
+    load_slots<M, FULL>(GlobalRow{go + row * L.width, vec2}, L, lm.c, lm.q, g);
+    row_vjp<M, FULL>(a, b, g, ws, groups * 32, static_cast<int>(gw % groups) * 32 + lane, lm.q,
+                     dx, dy, acc);
+    if (lm.active) {
+      store_slots<M, FULL>(gx + row * L.width, L, lm.c, lm.q, vec2, dx);
+      store_slots<M, FULL>(gy + row * L.width, L, lm.c, lm.q, vec2, dy);
     }
   }
-
-  if (active) {
-    float* dst = partial + slot * numel;
-    static_for<P::n>([&](auto I) {
-      constexpr ChanPath cp = P::table.p[I];
-      if (FULL && !cp.copied && q != 0) return;
-      dst[weight_index<M, FULL, I>(L.C, c, q)] = acc[I] * mags.m[cp.cls];
-    });
-  }
+  if (lm.active) store_partial<M, FULL>(partial + slot * numel, L, mags, lm.c, lm.q, acc);
 }
 
-// Class of each weight unit (a unit is `channels` consecutive weights).
-struct UnitClasses {
-  unsigned char cls[2 * kMaxPaths];
+// ------------------------------------------------------------ staged kernels
+//
+// A CTA of R * groups warps; warp (r, g) handles row r of each stage and channel
+// group g.  A stage holds NT tensors of R consecutive rows (contiguous in HBM, one
+// bulk copy each).  Thread 0 issues copies: `stages` blocks up front, then it
+// refills the stage consumed one iteration earlier once every warp has released
+// it.  Blocks of rows are dealt round-robin over the persistent grid.
+
+struct StageRing {
+  uint64_t* full;
+  uint64_t* empty;
+  float* buf;
 };
 
-UnitClasses unit_classes(int m_max, bool full) {
-  const PathTable t = build_table(m_max, full);
-  UnitClasses u{};
-  for (int p = 0; p < t.n; ++p) {
-    u.cls[t.p[p].unit] = static_cast<unsigned char>(t.p[p].cls);
-    if (t.p[p].copied) u.cls[t.p[p].unit + 1] = static_cast<unsigned char>(t.p[p].cls);
-  }
-  return u;
+// Barriers live in the first kBarrierBytes of `smem`; stage buffers start at
+// `base + kBarrierBytes` (base = smem, or past data placed in front of them).
+__device__ __forceinline__ StageRing stage_ring(unsigned char* smem, unsigned char* base,
+                                                int stages) {
+  StageRing ring;
+  ring.full = reinterpret_cast<uint64_t*>(smem);
+  ring.empty = ring.full + stages;
+  ring.buf = reinterpret_cast<float*>(base + kBarrierBytes);
+  return ring;
 }
 
-// ws[i] = w[i] * magnitude of its path, so the row loop needs no extra multiply.
-__global__ void prescale_kernel(const float* __restrict__ w, float* __restrict__ ws, int64_t numel,
-                                int C, UnitClasses uc, Mags mags) {
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < numel;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    ws[i] = w[i] * mags.m[uc.cls[i / C]];
+template <int NT>
+__device__ __forceinline__ void issue_stage(const StageRing& ring, int s, int64_t block, int R,
+                                            int64_t rows, int64_t W, const float* const* src) {
+  const int64_t row0 = block * R;
+  const int64_t nr = rows - row0 < R ? rows - row0 : R;
+  const uint32_t bytes = static_cast<uint32_t>(nr * W * 4);
+  float* dst = ring.buf + static_cast<int64_t>(s) * NT * R * W;
+  mbar_arrive_expect_tx(&ring.full[s], NT * bytes);
+#pragma unroll
+  for (int t = 0; t < NT; ++t) bulk_g2s(dst + t * R * W, src[t] + row0 * W, bytes, &ring.full[s]);
+}
+
+// Pipeline driver: calls body(stage_base, row) for every row of this CTA's
+// blocks (row < rows), with the whole stage resident in shared memory.
+template <int NT, class Body>
+__device__ __forceinline__ void staged_loop(unsigned char* smem, unsigned char* base, int stages,
+                                            int R, int64_t rows, int64_t W,
+                                            const float* const* src, Body&& body) {
+  const StageRing ring = stage_ring(smem, base, stages);
+  const int nwarps = blockDim.x >> 5;
+  const int r = (threadIdx.x >> 5) / (nwarps / R);
+  const int64_t nblocks = (rows + R - 1) / R;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&ring.full[s], 1);
+      mbar_init(&ring.empty[s], nwarps);
+    }
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      const int64_t block = blockIdx.x + static_cast<int64_t>(s) * gridDim.x;
+      if (block < nblocks) issue_stage<NT>(ring, s, block, R, rows, W, src);
+    }
+  }
+  int64_t it = 0;
+  bool ok = true;
+  for (int64_t block = blockIdx.x; block < nblocks && ok; block += gridDim.x, ++it) {
+    const int s = static_cast<int>(it % stages);
+    ok = mbar_wait(&ring.full[s], static_cast<uint32_t>((it / stages) & 1), 1);
+    if (!ok) break;
+    const int64_t row = block * R + r;
+    if (row < rows) body(ring.buf + static_cast<int64_t>(s) * NT * R * W + r * W, row);
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&ring.empty[s]);
+    if (threadIdx.x == 0 && it > 0) {
+      // refill the stage of iteration it - 1 with the block of iteration it - 1 + stages
+      const int64_t prev = it - 1;
+      const int ps = static_cast<int>(prev % stages);
+      const int64_t next = block + static_cast<int64_t>(stages - 1) * gridDim.x;
+      if (next < nblocks) {
+        ok = mbar_wait(&ring.empty[ps], static_cast<uint32_t>((prev / stages) & 1), 2);
+        if (ok) issue_stage<NT>(ring, ps, next, R, rows, W, src);
+      }
+    }
+  }
+  if (!ok && threadIdx.x == 0) {
+    // a wait ran out: let copies already issued land before the CTA exits
+    for (int s = 0; s < stages; ++s) mbar_wait(&ring.full[s], 0, 3);
+  }
+}
+
+template <int M, bool FULL>
+__global__ void __launch_bounds__(kStagedWarps * 32, 1)
+    tp_forward_staged(const float* __restrict__ x, const float* __restrict__ y,
+                      const float* __restrict__ w, float* __restrict__ out, int64_t rows,
+                      TpLayout L, Mags mags, int groups, int R, int stages) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int S = 2 * M + 2;
+  const int warp = threadIdx.x >> 5;
+  const LaneMap<FULL> lm(warp % groups, threadIdx.x & 31, L.C);
+  float wr[Paths<M, FULL>::n];
+  load_weights<M, FULL>(w, L, mags, lm.c, lm.q, lm.active, wr);
+  const float* src[2] = {x, y};
+  const int64_t W = L.width;
+  staged_loop<2>(smem, smem, stages, R, rows, W, src, [&](const float* stage, int64_t row) {
+    float a[S], b[S], o[S];
+    load_slots<M, FULL>(SharedRow{stage}, L, lm.c, lm.q, a);
+    load_slots<M, FULL>(SharedRow{stage + R * W}, L, lm.c, lm.q, b);
+    row_forward<M, FULL>(a, b, wr, lm.q, o);
+    if (lm.active) store_slots<M, FULL>(out + row * W, L, lm.c, lm.q, true, o);
+  });
+}
+
+template <int M, bool FULL>
+__global__ void __launch_bounds__(kStagedWarps * 32, 1)
+    tp_backward_staged(const float* __restrict__ x, const float* __restrict__ y,
+                       const float4* __restrict__ ws, const float* __restrict__ go,
+                       float* __restrict__ gx, float* __restrict__ gy,
+                       float* __restrict__ partial, int64_t numel, int64_t rows, TpLayout L,
+                       Mags mags, int groups, int R, int stages, int weights_in_smem) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  using P = Paths<M, FULL>;
+  constexpr int S = 2 * M + 2;
+  const int warp = threadIdx.x >> 5;
+  const int r = warp / groups;
+  const int T = groups * 32;
+  const int t = (warp % groups) * 32 + (threadIdx.x & 31);
+  const LaneMap<FULL> lm(warp % groups, threadIdx.x & 31, L.C);
+  // Weights: copied once into shared memory when they fit next to the stages.
+  const size_t wbytes = static_cast<size_t>(P::chunks) * T * sizeof(float4);
+  const float4* wsrc = ws;
+  unsigned char* ring_base = smem;
+  if (weights_in_smem) {
+    uint64_t* wbar = reinterpret_cast<uint64_t*>(smem) + 2 * kMaxStages;
+    float4* wsm = reinterpret_cast<float4*>(smem + kBarrierBytes);
+    if (threadIdx.x == 0) {
+      mbar_init(wbar, 1);
+      fence_mbarrier_init();
+      mbar_arrive_expect_tx(wbar, static_cast<uint32_t>(wbytes));
+      bulk_g2s(wsm, ws, static_cast<uint32_t>(wbytes), wbar);
+    }
+    __syncthreads();
+    if (!mbar_wait(wbar, 0, 4)) return;
+    wsrc = wsm;
+    ring_base = smem + wbytes;  // barriers stay at smem; stages follow the weights
+  }
+  float acc[P::n];
+#pragma unroll
+  for (int i = 0; i < P::n; ++i) acc[i] = 0.0f;
+  const float* src[3] = {x, y, go};
+  const int64_t W = L.width;
+  staged_loop<3>(smem, ring_base, stages, R, rows, W, src, [&](const float* stage, int64_t row) {
+    float a[S], b[S], g[S], dx[S], dy[S];
+    load_slots<M, FULL>(SharedRow{stage}, L, lm.c, lm.q, a);
+    load_slots<M, FULL>(SharedRow{stage + R * W}, L, lm.c, lm.q, b);
+    load_slots<M, FULL>(SharedRow{stage + 2 * R * W}, L, lm.c, lm.q, g);
+    row_vjp<M, FULL>(a, b, g, wsrc, T, t, lm.q, dx, dy, acc);
+    if (lm.active) {
+      store_slots<M, FULL>(gx + row * W, L, lm.c, lm.q, true, dx);
+      store_slots<M, FULL>(gy + row * W, L, lm.c, lm.q, true, dy);
+    }
+  });
+  if (lm.active) {
+    const int64_t slot = static_cast<int64_t>(blockIdx.x) * R + r;
+    store_partial<M, FULL>(partial + slot * numel, L, mags, lm.c, lm.q, acc);
+  }
+}
+
+// ------------------------------------------------------------ small kernels
+
+// Magnitude-scaled weights in the per-thread order of row_vjp: chunk k of thread
+// t (channel group t / 32, lane t % 32) holds the weights of paths vjp[4k..4k+3]
+// for that lane's (channel, world), at ws[k * T + t]; unused entries are zero.
+template <int M, bool FULL>
+__global__ void prescale_kernel(const float* __restrict__ w, float4* __restrict__ ws,
+                                TpLayout L, Mags mags, int groups) {
+  using P = Paths<M, FULL>;
+  const int T = groups * 32;
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
+    const LaneMap<FULL> lm(t / 32, t % 32, L.C);
+    static_for<P::chunks>([&](auto k) {
+      float v[4];
+      static_for<4>([&](auto e) {
+        constexpr int pos = 4 * k + e;
+        if constexpr (pos < P::n) {
+          constexpr int I = P::vjp.idx[pos];
+          constexpr ChanPath cp = P::table.p[I];
+          const bool used = lm.active && (!FULL || cp.copied || lm.q == 0);
+          v[e] = used ? w[weight_index<M, FULL, I>(L.C, lm.c, lm.q)] * mags.m[cp.cls] : 0.0f;
+        } else {
+          v[e] = 0.0f;
+        }
+      });
+      ws[k * T + t] = make_float4(v[0], v[1], v[2], v[3]);
+    });
+  }
 }
 
 // dw[i] = sum over slots of partial[slot][i], in a fixed order: thread (r, col)
@@ -347,18 +594,17 @@ __global__ void zero_kernel(float* __restrict__ dst, int64_t n) {
 
 // ------------------------------------------------------------------ dispatch
 
-struct Launch {
-  int groups;
-  int64_t slots;
-  int64_t nwarps;
-  int64_t blocks;
-};
-
-using ForwardFn = void (*)(const float*, const float*, const float*, float*, int64_t, TpLayout,
-                           Mags, int, int64_t, int64_t, bool);
-using BackwardFn = void (*)(const float*, const float*, const float*, const float*, float*,
-                            float*, float*, int64_t, int64_t, TpLayout, Mags, int, int64_t,
-                            int64_t, bool);
+using ForwardDirectFn = void (*)(const float*, const float*, const float*, float*, int64_t,
+                                 TpLayout, Mags, int, int64_t, int64_t, bool);
+using BackwardDirectFn = void (*)(const float*, const float*, const float4*, const float*,
+                                  float*, float*, float*, int64_t, int64_t, TpLayout, Mags, int,
+                                  int64_t, int64_t, bool);
+using ForwardStagedFn = void (*)(const float*, const float*, const float*, float*, int64_t,
+                                 TpLayout, Mags, int, int, int);
+using BackwardStagedFn = void (*)(const float*, const float*, const float4*, const float*,
+                                  float*, float*, float*, int64_t, int64_t, TpLayout, Mags, int,
+                                  int, int, int);
+using PrescaleFn = void (*)(const float*, float4*, TpLayout, Mags, int);
 
 // ICTC_ONLY_ORDER=m builds one order only (quick register/spill checks).
 #ifdef ICTC_ONLY_ORDER
@@ -367,30 +613,33 @@ constexpr bool compiled_order(int m) { return m == ICTC_ONLY_ORDER; }
 constexpr bool compiled_order(int) { return true; }
 #endif
 
+struct Kernels {
+  ForwardDirectFn fwd_direct;
+  BackwardDirectFn bwd_direct;
+  ForwardStagedFn fwd_staged;
+  BackwardStagedFn bwd_staged;
+  PrescaleFn prescale;
+  int chunks;  // float4 weight chunks per thread (Paths::chunks)
+};
+
 template <int M, bool FULL>
-constexpr ForwardFn forward_ptr() {
-  if constexpr (compiled_order(M)) return &tp_forward_kernel<M, FULL>;
-  else return nullptr;
-}
-template <int M, bool FULL>
-constexpr BackwardFn backward_ptr() {
-  if constexpr (compiled_order(M)) return &tp_backward_kernel<M, FULL>;
-  else return nullptr;
+constexpr Kernels kernels_for() {
+  if constexpr (compiled_order(M)) {
+    return Kernels{&tp_forward_direct<M, FULL>, &tp_backward_direct<M, FULL>,
+                   &tp_forward_staged<M, FULL>, &tp_backward_staged<M, FULL>,
+                   &prescale_kernel<M, FULL>, Paths<M, FULL>::chunks};
+  } else {
+    return Kernels{nullptr, nullptr, nullptr, nullptr, nullptr, 0};
+  }
 }
 
 template <int... Ms>
-constexpr auto make_forward_table(std::integer_sequence<int, Ms...>) {
-  struct T { ForwardFn f[2][sizeof...(Ms)]; };
-  return T{{{forward_ptr<Ms, false>()...}, {forward_ptr<Ms, true>()...}}};
-}
-template <int... Ms>
-constexpr auto make_backward_table(std::integer_sequence<int, Ms...>) {
-  struct T { BackwardFn f[2][sizeof...(Ms)]; };
-  return T{{{backward_ptr<Ms, false>()...}, {backward_ptr<Ms, true>()...}}};
+constexpr auto make_table(std::integer_sequence<int, Ms...>) {
+  struct T { Kernels k[2][sizeof...(Ms)]; };
+  return T{{{kernels_for<Ms, false>()...}, {kernels_for<Ms, true>()...}}};
 }
 
-const auto kForward = make_forward_table(std::make_integer_sequence<int, kMaxOrder + 1>{});
-const auto kBackward = make_backward_table(std::make_integer_sequence<int, kMaxOrder + 1>{});
+const auto kKernels = make_table(std::make_integer_sequence<int, kMaxOrder + 1>{});
 
 int validate(int64_t rows, int32_t channels, int32_t m_max, int32_t parity,
              int32_t normalization) {
@@ -415,36 +664,110 @@ int64_t weight_numel(int C, int m_max, bool full) {
   return static_cast<int64_t>(build_table(m_max, full).units) * C;
 }
 
-// Workspace: [magnitude-scaled weights, padded to 256 B][slots x numel partials].
-size_t scaled_weight_floats(int64_t numel) { return static_cast<size_t>(ceil_div(numel, 64) * 64); }
-size_t backward_workspace_bytes(int64_t slots, int64_t numel) {
-  return (scaled_weight_floats(numel) + static_cast<size_t>(slots) * static_cast<size_t>(numel)) *
-         sizeof(float);
+int current_device(int* device) {
+  const cudaError_t e = cudaGetDevice(device);
+  return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "cudaGetDevice");
 }
 
-// Grid shape: a multiple of `groups` warps so that every warp keeps one channel
+// Direct grid: a multiple of `groups` warps so that every warp keeps one channel
 // group; `slots` warps share each group and split the rows round-robin.
-int plan(const void* kernel, int64_t rows, int C, bool full, Launch* out) {
-  int device = 0;
-  cudaError_t e = cudaGetDevice(&device);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+struct DirectPlan {
+  int groups;
+  int64_t slots, nwarps, blocks;
+};
+
+int plan_direct(const void* kernel, int device, int64_t rows, int C, bool full, DirectPlan* out) {
   int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0);
+  const cudaError_t e =
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kDirectThreads, 0);
   if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-  const int cpw = full ? 16 : 32;
-  out->groups = static_cast<int>(ceil_div(C, cpw));
-  const int64_t resident = static_cast<int64_t>(sm_count(device)) * (per_sm > 0 ? per_sm : 1) *
-                           (kThreads / 32);
+  out->groups = static_cast<int>(ceil_div(C, full ? 16 : 32));
+  const int64_t resident =
+      static_cast<int64_t>(sm_count(device)) * (per_sm > 0 ? per_sm : 1) * (kDirectThreads / 32);
   int64_t slots = resident / out->groups;
   if (slots < 1) slots = 1;
   if (slots > rows) slots = rows > 0 ? rows : 1;
   out->slots = slots;
   out->nwarps = slots * out->groups;
-  out->blocks = ceil_div(out->nwarps * 32, kThreads);
+  out->blocks = ceil_div(out->nwarps * 32, kDirectThreads);
   return ICTC_OK;
 }
 
+// Staged grid: one persistent CTA per SM of R * groups warps (R rows per stage).
+// With `weight_bytes` > 0 the weights go to shared memory in front of the stages
+// when at least three stages still fit.
+struct StagedPlan {
+  bool ok, weights_in_smem;
+  int groups, R, warps, stages;
+  int64_t grid;
+  size_t smem;
+};
+
+StagedPlan plan_staged(int device, int64_t rows, const TpLayout& L, bool full, int tensors,
+                       size_t weight_bytes) {
+  StagedPlan p{};
+  p.groups = static_cast<int>(ceil_div(L.C, full ? 16 : 32));
+  if (p.groups > kStagedWarps || L.width % 4 != 0 || rows == 0) return p;
+  p.R = kStagedWarps / p.groups;
+  p.warps = p.R * p.groups;
+  const size_t stage_bytes = static_cast<size_t>(tensors) * p.R * L.width * sizeof(float);
+  if (weight_bytes > 0 && kStagedSmemBudget > kBarrierBytes + weight_bytes) {
+    const int fit =
+        static_cast<int>((kStagedSmemBudget - kBarrierBytes - weight_bytes) / stage_bytes);
+    if (fit >= 3) {
+      p.weights_in_smem = true;
+      p.stages = fit < kMaxStages ? fit : kMaxStages;
+      p.smem = kBarrierBytes + weight_bytes + static_cast<size_t>(p.stages) * stage_bytes;
+    }
+  }
+  if (!p.weights_in_smem) {
+    const int fit = static_cast<int>((kStagedSmemBudget - kBarrierBytes) / stage_bytes);
+    p.stages = fit < kMaxStages ? fit : kMaxStages;
+    if (p.stages < 2) return p;
+    p.smem = kBarrierBytes + static_cast<size_t>(p.stages) * stage_bytes;
+  }
+  const int64_t nblocks = ceil_div(rows, p.R);
+  p.grid = sm_count(device);
+  if (p.grid > nblocks) p.grid = nblocks;
+  p.ok = true;
+  return p;
+}
+
+bool aligned16(std::initializer_list<const void*> ptrs) {
+  for (const void* p : ptrs)
+    if (!aligned(p, 16)) return false;
+  return true;
+}
+
+// Backward workspace: [per-thread float4 weight chunks][slots x numel partials].
+size_t weight_chunk_bytes(const Kernels& k, int C, bool full) {
+  const int64_t T = ceil_div(C, full ? 16 : 32) * 32;
+  return static_cast<size_t>(k.chunks) * static_cast<size_t>(T) * sizeof(float4);
+}
+
+int64_t backward_slots(int device, const Kernels& k, int64_t rows, const TpLayout& L, bool full,
+                       int* status) {
+  DirectPlan d{};
+  *status = plan_direct(reinterpret_cast<const void*>(k.bwd_direct), device, rows, L.C, full, &d);
+  const StagedPlan s = plan_staged(device, rows, L, full, 3, weight_chunk_bytes(k, L.C, full));
+  const int64_t staged = s.ok ? s.grid * s.R : 0;
+  return d.slots > staged ? d.slots : staged;
+}
+
 }  // namespace
+
+int tp_take_device_error(int* code) {
+  int value = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  e = cudaMemcpyFromSymbol(&value, g_ictc_device_error, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "read device error flag");
+  const int zero = 0;
+  e = cudaMemcpyToSymbol(g_ictc_device_error, &zero, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "clear device error flag");
+  *code = value;
+  return ICTC_OK;
+}
 
 }  // namespace ictc
 
@@ -497,16 +820,27 @@ extern "C" int32_t ictc_o2_tp_forward(const float* left, const float* right, con
     return fail(ICTC_ERR_INVALID, "tensor pointers must be 4-byte aligned");
   const bool full = parity == ICTC_PARITY_FULL;
   const TpLayout L = tp_layout(channels, m_max, full);
-  const bool vec2 = (L.width % 2 == 0) && aligned(left, 8) && aligned(right, 8) &&
-                    aligned(output, 8);
-  ForwardFn fn = kForward.f[full ? 1 : 0][m_max];
-  Launch g;
-  st = plan(reinterpret_cast<const void*>(fn), rows, channels, full, &g);
-  if (st != ICTC_OK) return st;
+  const Kernels& k = kKernels.k[full ? 1 : 0][m_max];
+  const Mags mags = tp_mags(normalization);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  fn<<<static_cast<unsigned>(g.blocks), kThreads, 0, s>>>(left, right, weight, output, rows, L,
-                                                           tp_mags(normalization), g.groups,
-                                                           g.nwarps, g.slots, vec2);
+  int device = 0;
+  if ((st = current_device(&device)) != ICTC_OK) return st;
+  const StagedPlan sp = plan_staged(device, rows, L, full, 2, 0);
+  if (sp.ok && aligned16({left, right, output})) {
+    if ((st = allow_smem(reinterpret_cast<const void*>(k.fwd_staged), sp.smem)) != ICTC_OK)
+      return st;
+    k.fwd_staged<<<static_cast<unsigned>(sp.grid), sp.warps * 32, sp.smem, s>>>(
+        left, right, weight, output, rows, L, mags, sp.groups, sp.R, sp.stages);
+  } else {
+    const bool vec2 = (L.width % 2 == 0) && aligned(left, 8) && aligned(right, 8) &&
+                      aligned(output, 8);
+    DirectPlan g;
+    st = plan_direct(reinterpret_cast<const void*>(k.fwd_direct), device, rows, channels, full,
+                     &g);
+    if (st != ICTC_OK) return st;
+    k.fwd_direct<<<static_cast<unsigned>(g.blocks), kDirectThreads, 0, s>>>(
+        left, right, weight, output, rows, L, mags, g.groups, g.nwarps, g.slots, vec2);
+  }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tp_forward launch");
   return ICTC_OK;
@@ -517,20 +851,25 @@ extern "C" int32_t ictc_o2_tp_backward_workspace(int64_t rows, int32_t channels,
   if (bytes == nullptr) return fail(ICTC_ERR_INVALID, "bytes is null");
   int st = validate(rows, channels, m_max, parity, ICTC_NORM_COMPONENT);
   if (st != ICTC_OK) return st;
+  if (rows == 0) {
+    *bytes = 0;
+    return ICTC_OK;
+  }
   int prev = 0;
-  cudaError_t e = cudaGetDevice(&prev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if ((st = current_device(&prev)) != ICTC_OK) return st;
   if (device != prev) {
-    e = cudaSetDevice(device);
+    const cudaError_t e = cudaSetDevice(device);
     if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
   }
   const bool full = parity == ICTC_PARITY_FULL;
-  Launch g;
-  st = plan(reinterpret_cast<const void*>(kBackward.f[full ? 1 : 0][m_max]), rows, channels,
-            full, &g);
+  const TpLayout L = tp_layout(channels, m_max, full);
+  const int64_t slots =
+      backward_slots(device, kKernels.k[full ? 1 : 0][m_max], rows, L, full, &st);
   if (device != prev) cudaSetDevice(prev);
   if (st != ICTC_OK) return st;
-  *bytes = rows == 0 ? 0 : backward_workspace_bytes(g.slots, weight_numel(channels, m_max, full));
+  const int64_t numel = weight_numel(channels, m_max, full);
+  *bytes = weight_chunk_bytes(kKernels.k[full ? 1 : 0][m_max], channels, full) +
+           static_cast<size_t>(slots) * numel * sizeof(float);
   return ICTC_OK;
 }
 
@@ -547,8 +886,8 @@ extern "C" int32_t ictc_o2_tp_backward(const float* left, const float* right, co
   const int64_t numel = weight_numel(channels, m_max, full);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (rows == 0) {
-    zero_kernel<<<static_cast<unsigned>(ceil_div(numel, 256) < 1024 ? ceil_div(numel, 256) : 1024),
-                  256, 0, s>>>(grad_weight, numel);
+    const int64_t blocks = ceil_div(numel, 256) < 1024 ? ceil_div(numel, 256) : 1024;
+    zero_kernel<<<static_cast<unsigned>(blocks > 0 ? blocks : 1), 256, 0, s>>>(grad_weight, numel);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "zero launch");
   }
@@ -556,32 +895,50 @@ extern "C" int32_t ictc_o2_tp_backward(const float* left, const float* right, co
     return fail(ICTC_ERR_INVALID, "null tensor pointer");
   if (!aligned(left, 4) || !aligned(right, 4) || !aligned(weight, 4) ||
       !aligned(grad_output, 4) || !aligned(grad_left, 4) || !aligned(grad_right, 4) ||
-      !aligned(grad_weight, 4) || !aligned(workspace, 4))
-    return fail(ICTC_ERR_INVALID, "tensor pointers must be 4-byte aligned");
+      !aligned(grad_weight, 4) || !aligned(workspace, 16))
+    return fail(ICTC_ERR_INVALID, "tensor pointers must be 4-byte aligned (workspace 16)");
   const TpLayout L = tp_layout(channels, m_max, full);
-  const bool vec2 = (L.width % 2 == 0) && aligned(left, 8) && aligned(right, 8) &&
-                    aligned(grad_output, 8) && aligned(grad_left, 8) && aligned(grad_right, 8);
-  BackwardFn fn = kBackward.f[full ? 1 : 0][m_max];
-  Launch g;
-  st = plan(reinterpret_cast<const void*>(fn), rows, channels, full, &g);
-  if (st != ICTC_OK) return st;
-  const size_t need = backward_workspace_bytes(g.slots, numel);
+  const Kernels& k = kKernels.k[full ? 1 : 0][m_max];
+  int device = 0;
+  if ((st = current_device(&device)) != ICTC_OK) return st;
+  const size_t wbytes = weight_chunk_bytes(k, channels, full);
+  const StagedPlan sp = plan_staged(device, rows, L, full, 3, wbytes);
+  const bool staged = sp.ok && aligned16({left, right, grad_output, grad_left, grad_right});
+  DirectPlan dp{};
+  if (!staged) {
+    st = plan_direct(reinterpret_cast<const void*>(k.bwd_direct), device, rows, channels, full,
+                     &dp);
+    if (st != ICTC_OK) return st;
+  }
+  const int64_t slots = staged ? sp.grid * sp.R : dp.slots;
+  const size_t need = wbytes + static_cast<size_t>(slots) * numel * sizeof(float);
   if (workspace_bytes < need)
     return fail(ICTC_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, need);
-  float* scaled = static_cast<float*>(workspace);
-  float* partial = scaled + scaled_weight_floats(numel);
+  float4* chunks = static_cast<float4*>(workspace);
+  float* partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + wbytes);
   const Mags mags = tp_mags(normalization);
-  prescale_kernel<<<static_cast<unsigned>(ceil_div(numel, 256) < 1024 ? ceil_div(numel, 256) : 1024),
-                    256, 0, s>>>(weight, scaled, numel, channels, unit_classes(m_max, full), mags);
+  const int groups = static_cast<int>(ceil_div(channels, full ? 16 : 32));
+  k.prescale<<<static_cast<unsigned>(ceil_div(groups * 32, 256)), 256, 0, s>>>(weight, chunks, L,
+                                                                               mags, groups);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "prescale launch");
-  fn<<<static_cast<unsigned>(g.blocks), kThreads, 0, s>>>(
-      left, right, scaled, grad_output, grad_left, grad_right, partial, numel, rows, L,
-      mags, g.groups, g.nwarps, g.slots, vec2);
+  if (staged) {
+    if ((st = allow_smem(reinterpret_cast<const void*>(k.bwd_staged), sp.smem)) != ICTC_OK)
+      return st;
+    k.bwd_staged<<<static_cast<unsigned>(sp.grid), sp.warps * 32, sp.smem, s>>>(
+        left, right, chunks, grad_output, grad_left, grad_right, partial, numel, rows, L, mags,
+        sp.groups, sp.R, sp.stages, sp.weights_in_smem ? 1 : 0);
+  } else {
+    const bool vec2 = (L.width % 2 == 0) && aligned(left, 8) && aligned(right, 8) &&
+                      aligned(grad_output, 8) && aligned(grad_left, 8) && aligned(grad_right, 8);
+    k.bwd_direct<<<static_cast<unsigned>(dp.blocks), kDirectThreads, 0, s>>>(
+        left, right, chunks, grad_output, grad_left, grad_right, partial, numel, rows, L, mags,
+        dp.groups, dp.nwarps, dp.slots, vec2);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tp_backward launch");
   reduce_slots_kernel<<<static_cast<unsigned>(ceil_div(numel, 32)), 256, 0, s>>>(
-      partial, grad_weight, numel, g.slots);
+      partial, grad_weight, numel, slots);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "reduce launch");
   return ICTC_OK;

@@ -45,6 +45,12 @@ ICTC_API const char* ictc_o2_last_error(void);
 /* Library ABI version (major * 100 + minor). */
 ICTC_API int32_t ictc_o2_abi_version(void);
 
+/* Synchronizes with the current device, then reads and clears the kernels'
+ * device-side error flag: 0 = none; nonzero = a bounded wait inside a kernel ran
+ * out and that kernel stopped early (its outputs are invalid).  No counterpart in
+ * the reference, whose Triton kernels have no waits. */
+ICTC_API int32_t ictc_o2_device_error(int32_t* code);
+
 /* ---------------------------------------------------------------- TensorProduct
  * Flat channel-major operands of width W = C * (2 * m_max + 1) * (full ? 2 : 1),
  * layout [0e: C][0o: C (full)][m = 1..m_max: copy (1 or 2) x C x 2]
