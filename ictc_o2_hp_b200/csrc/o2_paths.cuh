@@ -172,16 +172,25 @@ struct PathOrder {
   int idx[kMaxPaths] = {};
 };
 
-// Paths grouped by first-input slot (stable): in the adjoint the gradient of a
-// first-input slot is complete once its group is done, which shortens register
-// live ranges.
+// Kernel execution order: paths with a frequency output (run by both parity
+// worlds) first, then the scalar-output paths (world 0 only, one divergent
+// region in full parity); inside each part, grouped by first-input slot, which
+// shortens register live ranges in the adjoint.
 constexpr PathOrder by_first_input(const PathTable& t) {
   PathOrder o{};
   int n = 0;
-  for (int slot = 0; slot <= 2 * kMaxOrder + 1; ++slot)
-    for (int p = 0; p < t.n; ++p)
-      if (t.p[p].in1 == slot) o.idx[n++] = p;
+  for (int part = 0; part < 2; ++part)
+    for (int slot = 0; slot <= 2 * kMaxOrder + 1; ++slot)
+      for (int p = 0; p < t.n; ++p)
+        if (t.p[p].in1 == slot && (t.p[p].out >= 2) == (part == 0)) o.idx[n++] = p;
   return o;
+}
+
+// Number of leading entries of by_first_input() with a frequency output.
+constexpr int frequency_output_paths(const PathTable& t) {
+  int n = 0;
+  for (int p = 0; p < t.n; ++p) n += t.p[p].out >= 2 ? 1 : 0;
+  return n;
 }
 
 template <int M, bool FULL>
@@ -190,6 +199,7 @@ struct Paths {
   static constexpr int n = table.n;
   static constexpr int slots = 2 * M + 2;
   static constexpr PathOrder vjp = by_first_input(table);
+  static constexpr int nfreq = frequency_output_paths(table);
   static constexpr int chunks = (n + 3) / 4;  // float4 chunks of per-thread weights
 };
 

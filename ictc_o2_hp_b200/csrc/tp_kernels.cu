@@ -24,6 +24,7 @@
 //     aligned or rows wider than one CTA.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <initializer_list>
 
@@ -75,12 +76,42 @@ struct GlobalRow {
   __device__ __forceinline__ float2 ld2(int i) const { return ldg2(p + i, vec2); }
 };
 
+// Explicit ld.shared (a generic load of shared memory costs more and waits on the
+// long scoreboard); volatile keeps them after the mbarrier wait that publishes
+// the stage.
 struct SharedRow {
-  const float* p;
-  __device__ __forceinline__ float ld(int i) const { return p[i]; }
-  __device__ __forceinline__ float2 ld2(int i) const {
-    return *reinterpret_cast<const float2*>(p + i);
+  uint32_t base;  // shared-window byte address of the row
+  __device__ __forceinline__ explicit SharedRow(const float* p)
+      : base(static_cast<uint32_t>(__cvta_generic_to_shared(p))) {}
+  __device__ __forceinline__ float ld(int i) const {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(base + 4u * i));
+    return v;
   }
+  __device__ __forceinline__ float2 ld2(int i) const {
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(base + 4u * i));
+    return v;
+  }
+};
+
+// Per-thread float4 weight chunks (see prescale_kernel) in shared or global memory.
+struct SharedChunks {
+  uint32_t base;  // byte address of chunk 0 of this thread
+  int stride;     // bytes between chunks of one thread
+  __device__ __forceinline__ float4 ld(int k) const {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(base + static_cast<uint32_t>(k * stride)));
+    return v;
+  }
+};
+
+struct GlobalChunks {
+  const float4* p;  // chunk 0 of this thread
+  int T;            // float4 stride between chunks
+  __device__ __forceinline__ float4 ld(int k) const { return __ldg(p + k * T); }
 };
 
 // Slot vector of channel c in world q, in the canonical basis: the odd copy
@@ -234,7 +265,8 @@ __device__ __forceinline__ void load_weights(const float* __restrict__ w, const 
   });
 }
 
-// Forward of one (row, channel, world): o = sum over paths.
+// Forward of one (row, channel, world): o = sum over paths, in Paths::vjp order
+// (the scalar-output paths of world 0 form one divergent region).
 template <int M, bool FULL>
 __device__ __forceinline__ void row_forward(const float (&a)[2 * M + 2],
                                             const float (&b)[2 * M + 2],
@@ -243,20 +275,23 @@ __device__ __forceinline__ void row_forward(const float (&a)[2 * M + 2],
   using P = Paths<M, FULL>;
 #pragma unroll
   for (int s = 0; s < 2 * M + 2; ++s) o[s] = 0.0f;
-  static_for<P::n>([&](auto I) {
-    if (FULL && !P::table.p[I].copied && q != 0) return;  // scalar outputs: world 0 only
+  auto step = [&](auto K) {
+    constexpr int I = P::vjp.idx[K];
     path_forward<M, FULL, I>(a, b, o, wr[I]);
-  });
+  };
+  static_for<P::nfreq>(step);
+  if (!FULL || q == 0) {
+    static_for<P::n - P::nfreq>([&](auto J) { step(std::integral_constant<int, P::nfreq + J>{}); });
+  }
 }
 
-// VJP of one (row, channel, world).  Paths run grouped by first-input slot
-// (Paths::vjp); the magnitude-scaled weights of this thread sit in that order as
-// float4 chunks: chunk k of thread t at wsrc[k * T + t] (see prescale_kernel).
-template <int M, bool FULL>
+// VJP of one (row, channel, world).  Paths run in Paths::vjp order (frequency-
+// output paths, then the world-0 scalar-output paths); the magnitude-scaled
+// weights of this thread sit in that order as float4 chunks (prescale_kernel).
+template <int M, bool FULL, class Chunks>
 __device__ __forceinline__ void row_vjp(const float (&a)[2 * M + 2], const float (&b)[2 * M + 2],
-                                        const float (&g)[2 * M + 2], const float4* wsrc, int T,
-                                        int t, int q, float (&dx)[2 * M + 2],
-                                        float (&dy)[2 * M + 2],
+                                        const float (&g)[2 * M + 2], const Chunks& wsrc, int q,
+                                        float (&dx)[2 * M + 2], float (&dy)[2 * M + 2],
                                         float (&acc)[Paths<M, FULL>::n]) {
   using P = Paths<M, FULL>;
 #pragma unroll
@@ -265,13 +300,16 @@ __device__ __forceinline__ void row_vjp(const float (&a)[2 * M + 2], const float
     dy[s] = 0.0f;
   }
   float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  static_for<P::n>([&](auto K) {
+  auto step = [&](auto K) {
     constexpr int I = P::vjp.idx[K];
-    if constexpr (K % 4 == 0) w4 = wsrc[(K / 4) * T + t];
-    if (FULL && !P::table.p[I].copied && q != 0) return;  // scalar outputs: world 0 only
+    if constexpr (K % 4 == 0) w4 = wsrc.ld(K / 4);
     const float wv = K % 4 == 0 ? w4.x : (K % 4 == 1 ? w4.y : (K % 4 == 2 ? w4.z : w4.w));
     path_vjp<M, FULL, I>(a, b, g, dx, dy, acc[K], wv);
-  });
+  };
+  static_for<P::nfreq>(step);
+  if (!FULL || q == 0) {  // scalar-output paths: world 0 only
+    static_for<P::n - P::nfreq>([&](auto J) { step(std::integral_constant<int, P::nfreq + J>{}); });
+  }
   if (FULL) {
     // World 1 reaches the scalars through scalar x frequency paths.
     dx[0] += __shfl_xor_sync(0xffffffffu, dx[0], 16);
@@ -358,8 +396,8 @@ __global__ void __launch_bounds__(kDirectThreads)
     // The output twist (v0, v1) -> (v1, -v0) has the adjoint g -> (-g1, g0),
     // which is the same map as the input read.
     load_slots<M, FULL>(GlobalRow{go + row * L.width, vec2}, L, lm.c, lm.q, g);
-    row_vjp<M, FULL>(a, b, g, ws, groups * 32, static_cast<int>(gw % groups) * 32 + lane, lm.q,
-                     dx, dy, acc);
+    const GlobalChunks chunks{ws + static_cast<int>(gw % groups) * 32 + lane, groups * 32};
+    row_vjp<M, FULL>(a, b, g, chunks, lm.q, dx, dy, acc);
     if (lm.active) {
       store_slots<M, FULL>(gx + row * L.width, L, lm.c, lm.q, vec2, dx);
       store_slots<M, FULL>(gy + row * L.width, L, lm.c, lm.q, vec2, dy);
@@ -471,9 +509,85 @@ __global__ void __launch_bounds__(kStagedWarps * 32, 1)
   const int64_t W = L.width;
   staged_loop<2>(smem, smem, stages, R, rows, W, src, [&](const float* stage, int64_t row) {
     float a[S], b[S], o[S];
-    load_slots<M, FULL>(SharedRow{stage}, L, lm.c, lm.q, a);
-    load_slots<M, FULL>(SharedRow{stage + R * W}, L, lm.c, lm.q, b);
+    load_slots<M, FULL>(SharedRow(stage), L, lm.c, lm.q, a);
+    load_slots<M, FULL>(SharedRow(stage + R * W), L, lm.c, lm.q, b);
     row_forward<M, FULL>(a, b, wr, lm.q, o);
+    if (lm.active) store_slots<M, FULL>(out + row * W, L, lm.c, lm.q, true, o);
+  });
+}
+
+// Forward with the path weights in shared memory instead of registers: with
+// register use capped at 128, CTAs of 16 warps (two rows per stage) fit on an SM,
+// twice the warps of the register-weight variant.  The weights are laid out as
+// per-thread float4 chunks (thread t, chunk k at [k * T + t], Paths::vjp order)
+// by the warps of row slot 0 at kernel start.
+constexpr int kWideWarps = 16;
+
+template <int M, bool FULL>
+constexpr size_t wide_forward_smem() {
+  // worst case over channel counts: 256 threads per row, R * W <= 512 (2M + 1)
+  return kBarrierBytes + static_cast<size_t>(Paths<M, FULL>::chunks) * 256 * 16 +
+         2 * 2 * static_cast<size_t>(FULL ? 512 : 256) * (2 * M + 1) * 4;
+}
+
+template <int M, bool FULL>
+constexpr bool wide_forward_fits() { return wide_forward_smem<M, FULL>() <= kStagedSmemBudget; }
+
+template <int M, bool FULL>
+__global__ void __launch_bounds__(kWideWarps * 32, 1)
+    tp_forward_wide(const float* __restrict__ x, const float* __restrict__ y,
+                    const float* __restrict__ w, float* __restrict__ out, int64_t rows,
+                    TpLayout L, Mags mags, int groups, int R, int stages) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  using P = Paths<M, FULL>;
+  constexpr int S = 2 * M + 2;
+  const int warp = threadIdx.x >> 5;
+  const int T = groups * 32;
+  const int t = (warp % groups) * 32 + (threadIdx.x & 31);
+  const LaneMap<FULL> lm(warp % groups, threadIdx.x & 31, L.C);
+  float4* wsm = reinterpret_cast<float4*>(smem + kBarrierBytes);
+  if (warp < groups) {
+    static_for<P::chunks>([&](auto k) {
+      float v[4];
+      static_for<4>([&](auto e) {
+        constexpr int pos = 4 * k + e;
+        if constexpr (pos < P::n) {
+          constexpr int I = P::vjp.idx[pos];
+          constexpr ChanPath cp = P::table.p[I];
+          const bool used = lm.active && (!FULL || cp.copied || lm.q == 0);
+          v[e] = used ? __ldg(w + weight_index<M, FULL, I>(L.C, lm.c, lm.q)) * mags.m[cp.cls]
+                      : 0.0f;
+        } else {
+          v[e] = 0.0f;
+        }
+      });
+      wsm[k * T + t] = make_float4(v[0], v[1], v[2], v[3]);
+    });
+  }
+  __syncthreads();
+  const SharedChunks chunks{static_cast<uint32_t>(__cvta_generic_to_shared(wsm + t)),
+                            T * static_cast<int>(sizeof(float4))};
+  const size_t wbytes = static_cast<size_t>(P::chunks) * T * sizeof(float4);
+  const float* src[2] = {x, y};
+  const int64_t W = L.width;
+  staged_loop<2>(smem, smem + wbytes, stages, R, rows, W, src, [&](const float* stage, int64_t row) {
+    float a[S], b[S], o[S];
+    load_slots<M, FULL>(SharedRow(stage), L, lm.c, lm.q, a);
+    load_slots<M, FULL>(SharedRow(stage + R * W), L, lm.c, lm.q, b);
+#pragma unroll
+    for (int i = 0; i < S; ++i) o[i] = 0.0f;
+    float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    auto step = [&](auto K) {
+      constexpr int I = P::vjp.idx[K];
+      if constexpr (K % 4 == 0) w4 = chunks.ld(K / 4);
+      const float wv = K % 4 == 0 ? w4.x : (K % 4 == 1 ? w4.y : (K % 4 == 2 ? w4.z : w4.w));
+      path_forward<M, FULL, I>(a, b, o, wv);
+    };
+    static_for<P::nfreq>(step);
+    if (!FULL || lm.q == 0) {
+      static_for<P::n - P::nfreq>(
+          [&](auto J) { step(std::integral_constant<int, P::nfreq + J>{}); });
+    }
     if (lm.active) store_slots<M, FULL>(out + row * W, L, lm.c, lm.q, true, o);
   });
 }
@@ -495,8 +609,24 @@ __global__ void __launch_bounds__(kStagedWarps * 32, 1)
   const LaneMap<FULL> lm(warp % groups, threadIdx.x & 31, L.C);
   // Weights: copied once into shared memory when they fit next to the stages.
   const size_t wbytes = static_cast<size_t>(P::chunks) * T * sizeof(float4);
-  const float4* wsrc = ws;
-  unsigned char* ring_base = smem;
+  float acc[P::n];
+#pragma unroll
+  for (int i = 0; i < P::n; ++i) acc[i] = 0.0f;
+  const float* src[3] = {x, y, go};
+  const int64_t W = L.width;
+  auto body = [&](const auto& chunks) {
+    return [&](const float* stage, int64_t row) {
+      float a[S], b[S], g[S], dx[S], dy[S];
+      load_slots<M, FULL>(SharedRow(stage), L, lm.c, lm.q, a);
+      load_slots<M, FULL>(SharedRow(stage + R * W), L, lm.c, lm.q, b);
+      load_slots<M, FULL>(SharedRow(stage + 2 * R * W), L, lm.c, lm.q, g);
+      row_vjp<M, FULL>(a, b, g, chunks, lm.q, dx, dy, acc);
+      if (lm.active) {
+        store_slots<M, FULL>(gx + row * W, L, lm.c, lm.q, true, dx);
+        store_slots<M, FULL>(gy + row * W, L, lm.c, lm.q, true, dy);
+      }
+    };
+  };
   if (weights_in_smem) {
     uint64_t* wbar = reinterpret_cast<uint64_t*>(smem) + 2 * kMaxStages;
     float4* wsm = reinterpret_cast<float4*>(smem + kBarrierBytes);
@@ -508,25 +638,14 @@ __global__ void __launch_bounds__(kStagedWarps * 32, 1)
     }
     __syncthreads();
     if (!mbar_wait(wbar, 0, 4)) return;
-    wsrc = wsm;
-    ring_base = smem + wbytes;  // barriers stay at smem; stages follow the weights
+    const SharedChunks chunks{static_cast<uint32_t>(__cvta_generic_to_shared(wsm + t)),
+                              T * static_cast<int>(sizeof(float4))};
+    // stages follow the weights
+    staged_loop<3>(smem, smem + wbytes, stages, R, rows, W, src, body(chunks));
+  } else {
+    const GlobalChunks chunks{ws + t, T};
+    staged_loop<3>(smem, smem, stages, R, rows, W, src, body(chunks));
   }
-  float acc[P::n];
-#pragma unroll
-  for (int i = 0; i < P::n; ++i) acc[i] = 0.0f;
-  const float* src[3] = {x, y, go};
-  const int64_t W = L.width;
-  staged_loop<3>(smem, ring_base, stages, R, rows, W, src, [&](const float* stage, int64_t row) {
-    float a[S], b[S], g[S], dx[S], dy[S];
-    load_slots<M, FULL>(SharedRow{stage}, L, lm.c, lm.q, a);
-    load_slots<M, FULL>(SharedRow{stage + R * W}, L, lm.c, lm.q, b);
-    load_slots<M, FULL>(SharedRow{stage + 2 * R * W}, L, lm.c, lm.q, g);
-    row_vjp<M, FULL>(a, b, g, wsrc, T, t, lm.q, dx, dy, acc);
-    if (lm.active) {
-      store_slots<M, FULL>(gx + row * W, L, lm.c, lm.q, true, dx);
-      store_slots<M, FULL>(gy + row * W, L, lm.c, lm.q, true, dy);
-    }
-  });
   if (lm.active) {
     const int64_t slot = static_cast<int64_t>(blockIdx.x) * R + r;
     store_partial<M, FULL>(partial + slot * numel, L, mags, lm.c, lm.q, acc);
@@ -614,6 +733,7 @@ constexpr bool compiled_order(int) { return true; }
 #endif
 
 struct Kernels {
+  ForwardStagedFn fwd_wide;  // null when the weights do not fit in shared memory
   ForwardDirectFn fwd_direct;
   BackwardDirectFn bwd_direct;
   ForwardStagedFn fwd_staged;
@@ -625,11 +745,13 @@ struct Kernels {
 template <int M, bool FULL>
 constexpr Kernels kernels_for() {
   if constexpr (compiled_order(M)) {
-    return Kernels{&tp_forward_direct<M, FULL>, &tp_backward_direct<M, FULL>,
+    ForwardStagedFn wide = nullptr;
+    if constexpr (wide_forward_fits<M, FULL>()) wide = &tp_forward_wide<M, FULL>;
+    return Kernels{wide, &tp_forward_direct<M, FULL>, &tp_backward_direct<M, FULL>,
                    &tp_forward_staged<M, FULL>, &tp_backward_staged<M, FULL>,
                    &prescale_kernel<M, FULL>, Paths<M, FULL>::chunks};
   } else {
-    return Kernels{nullptr, nullptr, nullptr, nullptr, nullptr, 0};
+    return Kernels{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0};
   }
 }
 
@@ -704,23 +826,25 @@ struct StagedPlan {
 };
 
 StagedPlan plan_staged(int device, int64_t rows, const TpLayout& L, bool full, int tensors,
-                       size_t weight_bytes) {
+                       size_t weight_bytes, int max_warps = kStagedWarps, int max_stages = kMaxStages,
+                       bool weights_required = false) {
   StagedPlan p{};
   p.groups = static_cast<int>(ceil_div(L.C, full ? 16 : 32));
-  if (p.groups > kStagedWarps || L.width % 4 != 0 || rows == 0) return p;
-  p.R = kStagedWarps / p.groups;
+  if (p.groups > max_warps || L.width % 4 != 0 || rows == 0) return p;
+  p.R = max_warps / p.groups;
   p.warps = p.R * p.groups;
   const size_t stage_bytes = static_cast<size_t>(tensors) * p.R * L.width * sizeof(float);
   if (weight_bytes > 0 && kStagedSmemBudget > kBarrierBytes + weight_bytes) {
     const int fit =
         static_cast<int>((kStagedSmemBudget - kBarrierBytes - weight_bytes) / stage_bytes);
-    if (fit >= 3) {
+    if (fit >= (weights_required ? 2 : 3)) {
       p.weights_in_smem = true;
-      p.stages = fit < kMaxStages ? fit : kMaxStages;
+      p.stages = fit < max_stages ? fit : max_stages;
       p.smem = kBarrierBytes + weight_bytes + static_cast<size_t>(p.stages) * stage_bytes;
     }
   }
   if (!p.weights_in_smem) {
+    if (weights_required) return p;
     const int fit = static_cast<int>((kStagedSmemBudget - kBarrierBytes) / stage_bytes);
     p.stages = fit < kMaxStages ? fit : kMaxStages;
     if (p.stages < 2) return p;
@@ -825,8 +949,25 @@ extern "C" int32_t ictc_o2_tp_forward(const float* left, const float* right, con
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int device = 0;
   if ((st = current_device(&device)) != ICTC_OK) return st;
-  const StagedPlan sp = plan_staged(device, rows, L, full, 2, 0);
-  if (sp.ok && aligned16({left, right, output})) {
+  // The forward's arithmetic per byte is low enough that the direct kernel (12
+  // resident warps per SM, L1-cached loads) outruns the staged ring at every
+  // measured shape; the staged and wide variants stay selectable for experiments.
+  const char* variant = getenv("ICTC_TP_FORWARD");
+  const bool al16 = aligned16({left, right, output});
+  const bool want_wide = variant && strcmp(variant, "wide") == 0;
+  const bool want_staged = variant && strcmp(variant, "staged") == 0;
+  const StagedPlan wp =
+      (want_wide && k.fwd_wide)
+          ? plan_staged(device, rows, L, full, 2, weight_chunk_bytes(k, channels, full),
+                        kWideWarps, 2, true)
+          : StagedPlan{};
+  const StagedPlan sp = want_staged ? plan_staged(device, rows, L, full, 2, 0) : StagedPlan{};
+  if (wp.ok && al16) {
+    if ((st = allow_smem(reinterpret_cast<const void*>(k.fwd_wide), wp.smem)) != ICTC_OK)
+      return st;
+    k.fwd_wide<<<static_cast<unsigned>(wp.grid), wp.warps * 32, wp.smem, s>>>(
+        left, right, weight, output, rows, L, mags, wp.groups, wp.R, wp.stages);
+  } else if (sp.ok && al16) {
     if ((st = allow_smem(reinterpret_cast<const void*>(k.fwd_staged), sp.smem)) != ICTC_OK)
       return st;
     k.fwd_staged<<<static_cast<unsigned>(sp.grid), sp.warps * 32, sp.smem, s>>>(

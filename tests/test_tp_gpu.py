@@ -232,3 +232,26 @@ def test_tuple_and_component_major_layouts(cuda_device):
     assert torch.equal(got, ref)
     cm = comp(comp._to_component_major(x), comp._to_component_major(y))
     assert torch.equal(comp._to_channel_major(cm), ref)
+
+
+@pytest.mark.parametrize("variant", ["staged", "wide"])
+def test_forward_variants_agree(variant, cuda_device, monkeypatch):
+    """The staged and wide forward kernels (selectable with ICTC_TP_FORWARD)
+    give the same values as the default direct kernel."""
+    from ictc_o2_hp_b200 import TensorProduct
+    torch.manual_seed(7)
+    for channels, m_max, parity in ((128, 6, "full"), (32, 2, "canonical"), (48, 3, "full")):
+        tp = TensorProduct(channels, m_max, parity=parity).to(cuda_device)
+        x = torch.randn(333, tp.representation_dimension, device=cuda_device)
+        y = torch.randn_like(x)
+        with torch.no_grad():
+            ref = tp(x, y)
+            monkeypatch.setenv("ICTC_TP_FORWARD", variant)
+            got = tp(x, y)
+            monkeypatch.delenv("ICTC_TP_FORWARD")
+        assert O.max_error(got.cpu().numpy(), ref.cpu().numpy()) < 1e-6
+
+
+def test_no_device_error_flag(cuda_device):
+    from ictc_o2_hp_b200 import _lib
+    assert _lib.device_error() == 0
