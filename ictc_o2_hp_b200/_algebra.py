@@ -242,3 +242,65 @@ def iter_entries(blocks: Iterable[RepresentationBlock], channels: int):
             yield block.key, copy, cursor + copy * channels * block.irrep_dimension, \
                 block.irrep_dimension
         cursor += block.multiplicity * block.irrep_dimension
+
+
+# --------------------------------------------------------------------------- uvu
+
+
+@dataclass(frozen=True)
+class UvuEntry:
+    """One representation copy (reference: uvu_o2.py:14-18)."""
+
+    key: O2Key
+    copy: int
+    offset: int
+    dim: int
+
+
+def uvu_representation(channels: int, order: int, parity: str):
+    """(blocks, entries, width) of one uvu operand (uvu_o2.py:27-41)."""
+    if parity not in ("canonical", "full"):
+        raise ValueError("parity must be canonical or full")
+    blocks = (canonical_blocks if parity == "canonical" else full_parity_blocks)(order, channels)
+    entries, cursor = [], 0
+    for block in blocks:
+        for copy in range(block.parity_copies):
+            entries.append(UvuEntry(block.key, copy,
+                                    cursor + copy * channels * block.irrep_dimension,
+                                    block.irrep_dimension))
+        cursor += block.multiplicity * block.irrep_dimension
+    return blocks, tuple(entries), cursor
+
+
+_J = np.array([[0.0, -1.0], [1.0, 0.0]])
+
+
+def _copy_basis(entry: UvuEntry) -> np.ndarray:
+    return _J if entry.copy else np.eye(entry.dim)
+
+
+def uvu_paths(entries_in1, entries_in2, normalization: str, path_normalization: str,
+              channels_in2: int):
+    """Paths (i, j, k) ordered by output entry, first entry, second entry and their
+    padded coefficients c[p, k, a, b] in float64 (uvu_o2.py:121-145)."""
+    paths, coefficients = [], []
+    for k, out in enumerate(entries_in1):
+        start = len(paths)
+        for i, first in enumerate(entries_in1):
+            for j, second in enumerate(entries_in2):
+                if out.key not in valid_output_keys(first.key, second.key):
+                    continue
+                cg = cg_tensor(first.key, second.key, out.key, normalization)
+                cg = np.einsum("abk,ai,bj,lk->ijl", cg, _copy_basis(first),
+                               _copy_basis(second), _copy_basis(out).T)
+                padded = np.zeros((2, 2, 2))
+                padded[:out.dim, :first.dim, :second.dim] = np.transpose(cg, (2, 0, 1))
+                paths.append((i, j, k))
+                coefficients.append(padded)
+        count = len(paths) - start
+        if path_normalization != "none":
+            scale = math.sqrt(channels_in2 * count)
+            for p in range(start, len(paths)):
+                coefficients[p] = coefficients[p] / scale
+    coef = np.stack(coefficients) if coefficients else np.zeros((0, 2, 2, 2))
+    return tuple(paths), coef

@@ -36,6 +36,14 @@ SIGNATURES = {
                                              ctypes.POINTER(_size)]),
     "ictc_o2_tp_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _size, _i64, _i32,
                                    _i32, _i32, _i32, _vp]),
+    "ictc_o2_uvu_table": (_i32, [_i32] * 8 + [ctypes.POINTER(_i32), _i64,
+                                              ctypes.POINTER(_i64)]),
+    "ictc_o2_uvu_workspace": (_i32, [_i32] * 8 + [_i32, _i64, _i32, ctypes.POINTER(_size),
+                                                  ctypes.POINTER(_size)]),
+    "ictc_o2_uvu_forward": (_i32, [_vp, _vp, _vp, _vp, _i64] + [_i32] * 8 +
+                            [_i32, _vp, _vp, _size, _vp]),
+    "ictc_o2_uvu_backward": (_i32, [_vp] * 7 + [_i64] + [_i32] * 8 +
+                             [_i32, _i32, _vp, _vp, _size, _vp]),
 }
 
 _lock = threading.Lock()
@@ -139,3 +147,42 @@ def tp_backward(left, right, weight, grad_output, grad_left, grad_right, grad_we
         ptr(grad_weight), ptr(workspace), workspace.numel() if workspace is not None else 0,
         rows, channels, m_max, PARITY[parity], NORMALIZATION[normalization],
         stream_of(left.device)), "tp_backward")
+
+
+# ------------------------------------------------------------------------ uvu
+# config = (channels, channels_in2, m_max, parity, m_max_in2, parity_in2,
+#           normalization, path_normalization) as ints
+
+
+def uvu_table(config) -> "np.ndarray":
+    import numpy as np
+    lib = load()
+    words = _i64()
+    check(lib.ictc_o2_uvu_table(*config, None, 0, ctypes.byref(words)), "uvu_table")
+    buf = np.zeros(words.value, dtype=np.int32)
+    check(lib.ictc_o2_uvu_table(*config, buf.ctypes.data_as(ctypes.POINTER(_i32)), words.value,
+                                ctypes.byref(words)), "uvu_table")
+    return buf
+
+
+def uvu_workspace(config, shared: bool, rows: int, device: torch.device) -> tuple[int, int]:
+    fwd, bwd = _size(), _size()
+    check(load().ictc_o2_uvu_workspace(*config, int(shared), rows, device.index or 0,
+                                       ctypes.byref(fwd), ctypes.byref(bwd)), "uvu_workspace")
+    return int(fwd.value), int(bwd.value)
+
+
+def uvu_forward(left, right, weight, out, config, shared, table, workspace):
+    check(load().ictc_o2_uvu_forward(
+        ptr(left), ptr(right), ptr(weight), ptr(out), left.shape[0], *config, int(shared),
+        ptr(table), ptr(workspace), workspace.numel() if workspace is not None else 0,
+        stream_of(left.device)), "uvu_forward")
+
+
+def uvu_backward(left, right, weight, grad_output, gx, gy, gw, config, shared, needed, table,
+                 workspace):
+    check(load().ictc_o2_uvu_backward(
+        ptr(left), ptr(right), ptr(weight), ptr(grad_output), ptr(gx), ptr(gy), ptr(gw),
+        left.shape[0], *config, int(shared), int(needed), ptr(table), ptr(workspace),
+        workspace.numel() if workspace is not None else 0, stream_of(left.device)),
+        "uvu_backward")

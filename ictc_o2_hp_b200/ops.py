@@ -163,3 +163,98 @@ def _tp_double_backward(ctx, dd_left, dd_right, dd_weight):
 
 
 tp_backward.register_autograd(_tp_double_backward, setup_context=_tp_backward_setup)
+
+
+# ---------------------------------------------------------------------- uvu ops
+
+
+@torch.library.custom_op(f"{NAMESPACE}::uvu_forward", mutates_args=())
+def uvu_forward(left: Tensor, right: Tensor, weight: Tensor, table: Tensor, config: list[int],
+                shared: bool) -> Tensor:
+    """out[N, width1] of UvuTensorProduct (reference uvu_triton.py:235-275)."""
+    require_cuda_float32("UvuTensorProduct", left, right, weight)
+    left, right, weight = left.contiguous(), right.contiguous(), weight.contiguous()
+    out = torch.empty_like(left)
+    with torch.cuda.device(left.device):
+        fwd, _ = _lib.uvu_workspace(config, shared, left.shape[0], left.device)
+        workspace = torch.empty(max(fwd, 16), dtype=torch.uint8, device=left.device)
+        _lib.uvu_forward(left, right, weight, out, config, shared, table, workspace)
+    return out
+
+
+@uvu_forward.register_fake
+def _uvu_forward_fake(left, right, weight, table, config, shared):
+    return torch.empty_like(left)
+
+
+@torch.library.custom_op(f"{NAMESPACE}::uvu_backward", mutates_args=())
+def uvu_backward(left: Tensor, right: Tensor, weight: Tensor, grad_output: Tensor, table: Tensor,
+                 config: list[int], shared: bool, needed: int
+                 ) -> tuple[Tensor, Tensor, Tensor]:
+    """(gx, gy, gw) for the roles in `needed` (1 = x, 2 = y, 4 = w); absent roles
+    are empty (reference uvu_triton.py:287-404)."""
+    require_cuda_float32("UvuTensorProduct backward", left, right, weight, grad_output)
+    left, right = left.contiguous(), right.contiguous()
+    weight, grad_output = weight.contiguous(), grad_output.contiguous()
+    gx = torch.empty_like(left) if needed & 1 else left.new_empty(0)
+    gy = torch.empty_like(right) if needed & 2 else right.new_empty(0)
+    gw = torch.empty_like(weight) if needed & 4 else weight.new_empty(0)
+    with torch.cuda.device(left.device):
+        _, bwd = _lib.uvu_workspace(config, shared, left.shape[0], left.device)
+        workspace = torch.empty(max(bwd, 16), dtype=torch.uint8, device=left.device)
+        _lib.uvu_backward(left, right, weight, grad_output, gx if needed & 1 else None,
+                          gy if needed & 2 else None, gw if needed & 4 else None, config, shared,
+                          needed, table, workspace)
+    return gx, gy, gw
+
+
+@uvu_backward.register_fake
+def _uvu_backward_fake(left, right, weight, grad_output, table, config, shared, needed):
+    return (torch.empty_like(left) if needed & 1 else left.new_empty(0),
+            torch.empty_like(right) if needed & 2 else right.new_empty(0),
+            torch.empty_like(weight) if needed & 4 else weight.new_empty(0))
+
+
+def _uvu_setup(ctx, inputs, output):
+    left, right, weight, table, config, shared = inputs
+    ctx.save_for_backward(left, right, weight, table)
+    ctx.config, ctx.shared = config, shared
+
+
+def _uvu_autograd(ctx, grad_output):
+    left, right, weight, table = ctx.saved_tensors
+    flags = ctx.needs_input_grad[:3]
+    needed = sum(int(f) << i for i, f in enumerate(flags))
+    if needed == 0:
+        return None, None, None, None, None, None
+    gx, gy, gw = uvu_backward(left, right, weight, grad_output.contiguous(), table, ctx.config,
+                              ctx.shared, needed)
+    return (gx if flags[0] else None, gy if flags[1] else None, gw if flags[2] else None,
+            None, None, None)
+
+
+uvu_forward.register_autograd(_uvu_autograd, setup_context=_uvu_setup)
+
+
+def torch_uvu_flat(left: Tensor, right: Tensor, weight: Tensor, entries_in1, entries_in2,
+                   paths, coefficients: Tensor, channels: int, channels_in2: int,
+                   shared: bool) -> Tensor:
+    """Differentiable PyTorch formula of the uvu map (the role of the reference's
+    torch_uvu_forward, uvu_o2.py:50-73); used for second derivatives only."""
+    rows = left.shape[0]
+    values = [None] * len(entries_in1)
+    for p, (i, j, k) in enumerate(paths):
+        a, b, out = entries_in1[i], entries_in2[j], entries_in1[k]
+        x = left[:, a.offset:a.offset + channels * a.dim].reshape(rows, channels, a.dim)
+        y = right[:, b.offset:b.offset + channels_in2 * b.dim].reshape(rows, channels_in2, b.dim)
+        start = p * channels * channels_in2
+        w = weight[..., start:start + channels * channels_in2]
+        if shared:
+            projected = torch.einsum("uv,nvj->nuj", w.reshape(channels, channels_in2), y)
+        else:
+            projected = torch.einsum("nuv,nvj->nuj", w.reshape(rows, channels, channels_in2), y)
+        cg = coefficients[p, :out.dim, :a.dim, :b.dim]
+        contribution = torch.einsum("nui,nuj,kij->nuk", x, projected, cg)
+        values[k] = contribution if values[k] is None else values[k] + contribution
+    return torch.cat([value.reshape(rows, channels * entry.dim)
+                      for entry, value in zip(entries_in1, values)], dim=-1)

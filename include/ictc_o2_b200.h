@@ -87,6 +87,58 @@ ICTC_API int32_t ictc_o2_tp_backward(const float* left, const float* right, cons
                             int64_t rows, int32_t channels, int32_t m_max, int32_t parity,
                             int32_t normalization, void* stream);
 
+/* ------------------------------------------------------------ UvuTensorProduct
+ * First input / output: C channels per representation copy, flat
+ * [copy, channel, component] blocks; second input: V channels per copy
+ * (reference: src/ictc_o2_hp/uvu_o2.py:27-41, 76-156).  Configuration arguments,
+ * shared by the entry points below:
+ *   channels (C), channels_in2 (V), m_max, parity, m_max_in2, parity_in2,
+ *   normalization, path_normalization (0 = none, 1 = element/path; they coincide
+ *   for this API, uvu_o2.py:138-144).
+ * The path table is built by the library (ictc_o2_uvu_table); the caller copies
+ * it once to the device and passes that pointer, the role of the reference's
+ * path_info / coefficients buffers (uvu_triton.py:39-67). */
+
+/* Packed path table (int32 words, coefficients stored as float bits): a 16-word
+ * header {n_in1, n_in2, n_paths, C, V, width1, width2, 0, then the word offsets
+ * of the sections below and the total words}, then (offset, dim) per entry of
+ * each input, (i, j, k, 0) per path, 8 coefficients c[k][a][b] per path, and the
+ * paths ordered by first and by second entry; each section starts on a 16-byte
+ * boundary.  With table == NULL only `words` is written. */
+ICTC_API int32_t ictc_o2_uvu_table(int32_t channels, int32_t channels_in2, int32_t m_max,
+                                   int32_t parity, int32_t m_max_in2, int32_t parity_in2,
+                                   int32_t normalization, int32_t path_normalization,
+                                   int32_t* table, int64_t capacity_words, int64_t* words);
+
+/* Workspace bytes of the forward and backward entry points (device `device`). */
+ICTC_API int32_t ictc_o2_uvu_workspace(int32_t channels, int32_t channels_in2, int32_t m_max,
+                                       int32_t parity, int32_t m_max_in2, int32_t parity_in2,
+                                       int32_t normalization, int32_t path_normalization,
+                                       int32_t shared, int64_t rows, int32_t device,
+                                       size_t* forward_bytes, size_t* backward_bytes);
+
+/* out[N, width1].  weight: [weight_numel] when shared, else [N, weight_numel].
+ * Replaces the uvu forward / forward_into ops (reference: uvu_triton.py:235-284). */
+ICTC_API int32_t ictc_o2_uvu_forward(const float* left, const float* right, const float* weight,
+                                     float* output, int64_t rows, int32_t channels,
+                                     int32_t channels_in2, int32_t m_max, int32_t parity,
+                                     int32_t m_max_in2, int32_t parity_in2,
+                                     int32_t normalization, int32_t path_normalization,
+                                     int32_t shared, const void* device_table, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
+/* VJP; `needed` is the role mask 1 = grad_left, 2 = grad_right, 4 = grad_weight
+ * (the reference's `needed`, uvu_triton.py:18-36, 287-414).  grad_weight is
+ * [weight_numel] (shared, summed over rows in a fixed order) or [N, weight_numel]. */
+ICTC_API int32_t ictc_o2_uvu_backward(const float* left, const float* right, const float* weight,
+                                      const float* grad_output, float* grad_left,
+                                      float* grad_right, float* grad_weight, int64_t rows,
+                                      int32_t channels, int32_t channels_in2, int32_t m_max,
+                                      int32_t parity, int32_t m_max_in2, int32_t parity_in2,
+                                      int32_t normalization, int32_t path_normalization,
+                                      int32_t shared, int32_t needed, const void* device_table,
+                                      void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
