@@ -44,6 +44,11 @@ SIGNATURES = {
                             [_i32, _vp, _vp, _size, _vp]),
     "ictc_o2_uvu_backward": (_i32, [_vp] * 7 + [_i64] + [_i32] * 8 +
                              [_i32, _i32, _vp, _vp, _size, _vp]),
+    "ictc_o2_radial_workspace": (_i32, [_i32] * 8 + [_i64, _i32, ctypes.POINTER(_size),
+                                                     ctypes.POINTER(_size)]),
+    "ictc_o2_radial_forward": (_i32, [_vp] * 6 + [_i64] + [_i32] * 8 + [_vp, _vp, _size, _vp]),
+    "ictc_o2_radial_backward": (_i32, [_vp] * 11 + [_i64] + [_i32] * 8 +
+                                [_i32, _vp, _vp, _size, _vp]),
 }
 
 _lock = threading.Lock()
@@ -186,3 +191,30 @@ def uvu_backward(left, right, weight, grad_output, gx, gy, gw, config, shared, n
         left.shape[0], *config, int(shared), int(needed), ptr(table), ptr(workspace),
         workspace.numel() if workspace is not None else 0, stream_of(left.device)),
         "uvu_backward")
+
+
+# --------------------------------------------------------------------- radial
+# rconfig = (channels, m_max, parity, m_max_in2, parity_in2, normalization,
+#            path_normalization, hidden) as ints
+
+
+def radial_workspace(rconfig, rows: int, device: torch.device) -> tuple[int, int]:
+    fwd, bwd = _size(), _size()
+    check(load().ictc_o2_radial_workspace(*rconfig, rows, device.index or 0, ctypes.byref(fwd),
+                                          ctypes.byref(bwd)), "radial_workspace")
+    return int(fwd.value), int(bwd.value)
+
+
+def radial_forward(left, angular, hidden, alpha, bias, out, rconfig, table, workspace):
+    check(load().ictc_o2_radial_forward(
+        ptr(left), ptr(angular), ptr(hidden), ptr(alpha), ptr(bias), ptr(out), left.shape[0],
+        *rconfig, ptr(table), ptr(workspace), workspace.numel(), stream_of(left.device)),
+        "radial_forward")
+
+
+def radial_backward(left, angular, hidden, alpha, bias, grad_output, gx, gy, gh, ga, gb, rconfig,
+                    needed, table, workspace):
+    check(load().ictc_o2_radial_backward(
+        ptr(left), ptr(angular), ptr(hidden), ptr(alpha), ptr(bias), ptr(grad_output), ptr(gx),
+        ptr(gy), ptr(gh), ptr(ga), ptr(gb), left.shape[0], *rconfig, int(needed), ptr(table),
+        ptr(workspace), workspace.numel(), stream_of(left.device)), "radial_backward")

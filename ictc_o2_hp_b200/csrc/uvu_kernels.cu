@@ -20,21 +20,12 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "rowtile.cuh"
 #include "uvu_table.cuh"
 
 namespace ictc {
 
 namespace {
-
-struct UvuDev {
-  const int2* in1;
-  const int2* in2;
-  const int4* paths;
-  const float* coef;
-  const int* by_i;
-  const int* by_j;
-  int n1, n2, np;
-};
 
 UvuDev uvu_dev(const void* table, const UvuLayout& l) {
   const int* w = static_cast<const int*>(table);
@@ -67,10 +58,6 @@ __device__ __forceinline__ void cp_async_wait() {
 
 // ------------------------------------------------------------ shared weights
 
-constexpr int kRT = 32;    // rows per rowtile CTA
-constexpr int kUT = 128;   // u per rowtile CTA
-constexpr int kVC = 32;    // v per weight tile
-
 // wt[p][v][u] (u padded to Up) <- w[p][u][v]
 __global__ void transpose_weights(const float* __restrict__ w, float* __restrict__ wt, int P,
                                   int U, int Up, int V) {
@@ -82,155 +69,6 @@ __global__ void transpose_weights(const float* __restrict__ w, float* __restrict
     const int v = static_cast<int>(pv % V);
     const int64_t p = pv / V;
     wt[idx] = u < U ? w[(p * U + u) * V + v] : 0.0f;
-  }
-}
-
-// MODE 0: forward (operand x, output entries k, paths in table order = by k).
-// MODE 1: dx (operand g, output entries i, paths by_i).
-template <int MODE>
-__global__ void __launch_bounds__(256)
-    uvu_rowtile(const float* __restrict__ opnd, const float* __restrict__ y,
-                const float* __restrict__ wt, float* __restrict__ out, int64_t rows, int U,
-                int Up, int V, int W1, int W2, UvuDev t) {
-  extern __shared__ __align__(16) float sm[];
-  float* ytile = sm;                        // [W2][32]  (column-major: 4 rows per float4)
-  float* wtile = sm + static_cast<size_t>(W2) * kRT;  // [2][32 v][128 u]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int uq = warp * 4 + (lane & 3);  // 0..31
-  const int rq = lane >> 2;              // 0..7
-  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRT;
-  const int ub = blockIdx.y * kUT;
-  const int u0 = ub + uq * 4;
-
-  for (int idx = threadIdx.x; idx < kRT * W2; idx += blockDim.x) {
-    const int c = idx % W2, r = idx / W2;
-    const int64_t row = row0 + r;
-    ytile[c * kRT + r] = row < rows ? __ldg(y + row * W2 + c) : 0.0f;
-  }
-
-  const int nvc = (V + kVC - 1) / kVC;
-  const int ntiles = t.np * nvc;
-  auto path_at = [&](int pos) { return MODE == 0 ? pos : t.by_i[pos]; };
-  auto issue = [&](int T, int buf) {
-    const int p = path_at(T / nvc);
-    const int v0 = (T % nvc) * kVC;
-    float* dst = wtile + buf * (kVC * kUT);
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      const int q = threadIdx.x + s * 256;  // float4 index in the tile
-      const int vr = q >> 5, c4 = q & 31;
-      const int v = v0 + vr, u = ub + c4 * 4;
-      const bool valid = v < V && u < Up;
-      const float* src = valid ? wt + (static_cast<int64_t>(p) * V + v) * Up + u : wt;
-      cp_async16(dst + vr * kUT + c4 * 4, src, valid);
-    }
-  };
-
-  float acc[4][4][2];
-  float proj[4][4][2];
-#pragma unroll
-  for (int r = 0; r < 4; ++r)
-#pragma unroll
-    for (int q = 0; q < 4; ++q) acc[r][q][0] = acc[r][q][1] = proj[r][q][0] = proj[r][q][1] = 0.f;
-
-  if (ntiles > 0) issue(0, 0);
-  cp_async_commit();
-  __syncthreads();  // y tile visible
-  for (int T = 0; T < ntiles; ++T) {
-    if (T + 1 < ntiles) issue(T + 1, (T + 1) & 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const int pos = T / nvc, vc = T % nvc;
-    const int p = path_at(pos);
-    const int4 pt = t.paths[p];  // i, j, k
-    const int2 ej = t.in2[pt.y];
-    const int db = ej.y;
-    const float* wb = wtile + (T & 1) * (kVC * kUT) + uq * 4;
-    const int vn = min(kVC, V - vc * kVC);
-    if (db == 2) {
-      for (int vv = 0; vv < vn; ++vv) {
-        const float4 w4 = *reinterpret_cast<const float4*>(wb + vv * kUT);
-        const int col = ej.x + (vc * kVC + vv) * 2;
-        const float4 y0 = *reinterpret_cast<const float4*>(ytile + col * kRT + rq * 4);
-        const float4 y1 = *reinterpret_cast<const float4*>(ytile + (col + 1) * kRT + rq * 4);
-        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
-        const float ya[4] = {y0.x, y0.y, y0.z, y0.w};
-        const float yb[4] = {y1.x, y1.y, y1.z, y1.w};
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            proj[r][q][0] = fmaf(ya[r], wv[q], proj[r][q][0]);
-            proj[r][q][1] = fmaf(yb[r], wv[q], proj[r][q][1]);
-          }
-      }
-    } else {
-      for (int vv = 0; vv < vn; ++vv) {
-        const float4 w4 = *reinterpret_cast<const float4*>(wb + vv * kUT);
-        const int col = ej.x + (vc * kVC + vv);
-        const float4 y0 = *reinterpret_cast<const float4*>(ytile + col * kRT + rq * 4);
-        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
-        const float ya[4] = {y0.x, y0.y, y0.z, y0.w};
-#pragma unroll
-        for (int r = 0; r < 4; ++r)
-#pragma unroll
-          for (int q = 0; q < 4; ++q) proj[r][q][0] = fmaf(ya[r], wv[q], proj[r][q][0]);
-      }
-    }
-    if (vc == nvc - 1) {
-      // coupling with the row operand: x_i (forward) or g_k (dx)
-      const int2 eo = t.in1[MODE == 0 ? pt.x : pt.z];  // operand entry
-      const float* cf = t.coef + 8 * p;
-      float c[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) c[e] = __ldg(cf + e);
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int64_t row = row0 + rq * 4 + r;
-        const bool rv = row < rows;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int u = u0 + q;
-          float o0 = 0.f, o1 = 0.f;
-          if (rv && u < U) {
-            const float* src = opnd + row * W1 + eo.x + u * eo.y;
-            o0 = __ldg(src);
-            o1 = eo.y == 2 ? __ldg(src + 1) : 0.f;
-          }
-          const float p0 = proj[r][q][0], p1 = proj[r][q][1];
-          if (MODE == 0) {  // out[kc] += c[kc][a][b] x[a] p[b]
-            acc[r][q][0] += c[0] * o0 * p0 + c[1] * o0 * p1 + c[2] * o1 * p0 + c[3] * o1 * p1;
-            acc[r][q][1] += c[4] * o0 * p0 + c[5] * o0 * p1 + c[6] * o1 * p0 + c[7] * o1 * p1;
-          } else {  // dx[a] += c[kc][a][b] g[kc] p[b]
-            acc[r][q][0] += c[0] * o0 * p0 + c[1] * o0 * p1 + c[4] * o1 * p0 + c[5] * o1 * p1;
-            acc[r][q][1] += c[2] * o0 * p0 + c[3] * o0 * p1 + c[6] * o1 * p0 + c[7] * o1 * p1;
-          }
-          proj[r][q][0] = proj[r][q][1] = 0.f;
-        }
-      }
-      const int key = MODE == 0 ? pt.z : pt.x;
-      const bool last = pos + 1 == t.np ||
-                        (MODE == 0 ? t.paths[path_at(pos + 1)].z : t.paths[path_at(pos + 1)].x) != key;
-      if (last) {
-        const int2 ek = t.in1[key];
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const int64_t row = row0 + rq * 4 + r;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int u = u0 + q;
-            if (row < rows && u < U) {
-              float* dst = out + row * W1 + ek.x + u * ek.y;
-              dst[0] = acc[r][q][0];
-              if (ek.y == 2) dst[1] = acc[r][q][1];
-            }
-            acc[r][q][0] = acc[r][q][1] = 0.f;
-          }
-        }
-      }
-    }
-    __syncthreads();  // buffer T & 1 is refilled at T + 2
   }
 }
 
@@ -633,10 +471,6 @@ UvuTableH table_of(const UvuConfig& c) {
   return build_uvu_table(c.U, c.V, c.m1, c.full1, c.m2, c.full2, c.component, c.path_norm);
 }
 
-size_t uvu_rowtile_smem(int W2) {
-  return static_cast<size_t>(W2) * kRT * 4 + 2 * kVC * kUT * 4;
-}
-
 int64_t dw_chunks(int device, int64_t rows, int P, int U, int V) {
   const int64_t tiles = static_cast<int64_t>(P) * ((U + 127) / 128) * ((V + 31) / 32);
   int64_t chunks = (2 * sm_count(device) + tiles - 1) / tiles;
@@ -776,12 +610,14 @@ extern "C" int32_t ictc_o2_uvu_forward(const float* left, const float* right, co
     if (!aligned(workspace, 16)) return fail(ICTC_ERR_INVALID, "workspace must be 16-byte aligned");
     float* wt = static_cast<float*>(workspace);
     transpose_weights<<<1024, 256, 0, s>>>(weight, wt, l.np, c.U, Up, c.V);
-    const size_t smem = uvu_rowtile_smem(W2);
+    const size_t smem = rowtile_smem(kUvuFwd, W2, W2);
     if (smem > 220 * 1024) return fail(ICTC_ERR_UNSUPPORTED, "second input too wide (%d)", W2);
-    if ((st = allow_smem(reinterpret_cast<const void*>(&uvu_rowtile<0>), smem)) != ICTC_OK)
+    if ((st = allow_smem(reinterpret_cast<const void*>(&rowtile<kUvuFwd>), smem)) != ICTC_OK)
       return st;
     const dim3 grid(static_cast<unsigned>(ceil_div(rows, kRT)), (c.U + kUT - 1) / kUT);
-    uvu_rowtile<0><<<grid, 256, smem, s>>>(left, right, wt, output, rows, c.U, Up, c.V, W1, W2, t);
+    RowtileArgs ra{left, nullptr, right, nullptr, wt, nullptr, output, nullptr, rows,
+                   c.U, Up, c.V, W1, W2, W2, t};
+    rowtile<kUvuFwd><<<grid, 256, smem, s>>>(ra);
   }
   e = cudaGetLastError();
   return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "uvu forward launch");
@@ -844,13 +680,14 @@ extern "C" int32_t ictc_o2_uvu_backward(const float* left, const float* right, c
   float* partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + wt_bytes);
   if (needed & 1) {
     transpose_weights<<<1024, 256, 0, s>>>(weight, wt, l.np, c.U, Up, c.V);
-    const size_t smem = uvu_rowtile_smem(W2);
+    const size_t smem = rowtile_smem(kUvuDx, W2, W2);
     if (smem > 220 * 1024) return fail(ICTC_ERR_UNSUPPORTED, "second input too wide (%d)", W2);
-    if ((st = allow_smem(reinterpret_cast<const void*>(&uvu_rowtile<1>), smem)) != ICTC_OK)
+    if ((st = allow_smem(reinterpret_cast<const void*>(&rowtile<kUvuDx>), smem)) != ICTC_OK)
       return st;
     const dim3 grid(static_cast<unsigned>(ceil_div(rows, kRT)), (c.U + kUT - 1) / kUT);
-    uvu_rowtile<1><<<grid, 256, smem, s>>>(grad_output, right, wt, grad_left, rows, c.U, Up, c.V,
-                                           W1, W2, t);
+    RowtileArgs ra{grad_output, nullptr, right, nullptr, wt, nullptr, grad_left, nullptr, rows,
+                   c.U, Up, c.V, W1, W2, W2, t};
+    rowtile<kUvuDx><<<grid, 256, smem, s>>>(ra);
   }
   if (needed & 2) {
     const size_t smem = 128 * kDpStride * sizeof(float) > 4 * 64 * 32 * sizeof(float)

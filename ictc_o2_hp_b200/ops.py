@@ -258,3 +258,94 @@ def torch_uvu_flat(left: Tensor, right: Tensor, weight: Tensor, entries_in1, ent
         values[k] = contribution if values[k] is None else values[k] + contribution
     return torch.cat([value.reshape(rows, channels * entry.dim)
                       for entry, value in zip(entries_in1, values)], dim=-1)
+
+
+# -------------------------------------------------------------------- radial ops
+
+
+@torch.library.custom_op(f"{NAMESPACE}::radial_forward", mutates_args=())
+def radial_forward(left: Tensor, angular: Tensor, hidden: Tensor, alpha: Tensor, bias: Tensor,
+                   table: Tensor, rconfig: list[int], has_bias: bool) -> Tensor:
+    """uvu(left, angular, hidden @ alpha^T + bias) with the edge weights regenerated
+    on chip (reference radial_streamed.py:81-99)."""
+    require_cuda_float32("RadialUvuTensorProduct", left, angular, hidden, alpha)
+    left, angular = left.contiguous(), angular.contiguous()
+    hidden, alpha = hidden.contiguous(), alpha.contiguous()
+    bias = bias.contiguous() if has_bias else None
+    out = torch.empty_like(left)
+    with torch.cuda.device(left.device):
+        fwd, _ = _lib.radial_workspace(rconfig, left.shape[0], left.device)
+        workspace = torch.empty(max(fwd, 16), dtype=torch.uint8, device=left.device)
+        _lib.radial_forward(left, angular, hidden, alpha, bias, out, rconfig, table, workspace)
+    return out
+
+
+@radial_forward.register_fake
+def _radial_forward_fake(left, angular, hidden, alpha, bias, table, rconfig, has_bias):
+    return torch.empty_like(left)
+
+
+@torch.library.custom_op(f"{NAMESPACE}::radial_backward", mutates_args=())
+def radial_backward(left: Tensor, angular: Tensor, hidden: Tensor, alpha: Tensor, bias: Tensor,
+                    grad_output: Tensor, table: Tensor, rconfig: list[int], has_bias: bool,
+                    needed: int) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """(g_left, g_angular, g_hidden, g_alpha, g_bias) for the role mask `needed`
+    (1, 2, 4, 8, 16); absent roles are empty (reference radial_streamed.py:109-139)."""
+    require_cuda_float32("RadialUvuTensorProduct backward", left, angular, hidden, alpha,
+                         grad_output)
+    left, angular = left.contiguous(), angular.contiguous()
+    hidden, alpha, grad_output = hidden.contiguous(), alpha.contiguous(), grad_output.contiguous()
+    if not has_bias:
+        needed &= ~16
+    bias_c = bias.contiguous() if has_bias else None
+    # left and angular gradients come from one kernel; alpha's buffer is scratch for bias
+    want_xy = bool(needed & 3)
+    gx = torch.empty_like(left) if want_xy else left.new_empty(0)
+    gy = torch.empty_like(angular) if want_xy else angular.new_empty(0)
+    gh = torch.empty_like(hidden) if needed & 4 else hidden.new_empty(0)
+    ga = torch.empty_like(alpha) if needed & 24 else alpha.new_empty(0)
+    gb = torch.empty_like(bias) if needed & 16 else alpha.new_empty(0)
+    kernel_mask = needed | (3 if want_xy else 0) | (8 if needed & 16 else 0)
+    with torch.cuda.device(left.device):
+        _, bwd = _lib.radial_workspace(rconfig, left.shape[0], left.device)
+        workspace = torch.empty(max(bwd, 16), dtype=torch.uint8, device=left.device)
+        _lib.radial_backward(left, angular, hidden, alpha, bias_c, grad_output,
+                             gx if want_xy else None, gy if want_xy else None,
+                             gh if needed & 4 else None, ga if needed & 24 else None,
+                             gb if needed & 16 else None, rconfig, kernel_mask, table, workspace)
+    return (gx if needed & 1 else left.new_empty(0), gy if needed & 2 else angular.new_empty(0),
+            gh, ga if needed & 8 else alpha.new_empty(0), gb)
+
+
+@radial_backward.register_fake
+def _radial_backward_fake(left, angular, hidden, alpha, bias, grad_output, table, rconfig,
+                          has_bias, needed):
+    if not has_bias:
+        needed &= ~16
+    return (torch.empty_like(left) if needed & 1 else left.new_empty(0),
+            torch.empty_like(angular) if needed & 2 else angular.new_empty(0),
+            torch.empty_like(hidden) if needed & 4 else hidden.new_empty(0),
+            torch.empty_like(alpha) if needed & 8 else alpha.new_empty(0),
+            torch.empty_like(bias) if needed & 16 else alpha.new_empty(0))
+
+
+def _radial_setup(ctx, inputs, output):
+    left, angular, hidden, alpha, bias, table, rconfig, has_bias = inputs
+    ctx.save_for_backward(left, angular, hidden, alpha, bias, table)
+    ctx.rconfig, ctx.has_bias = rconfig, has_bias
+
+
+def _radial_autograd(ctx, grad_output):
+    left, angular, hidden, alpha, bias, table = ctx.saved_tensors
+    flags = list(ctx.needs_input_grad[:5])
+    if not ctx.has_bias:
+        flags[4] = False
+    needed = sum(int(f) << i for i, f in enumerate(flags))
+    if needed == 0:
+        return (None,) * 8
+    grads = radial_backward(left, angular, hidden, alpha, bias, grad_output.contiguous(), table,
+                            ctx.rconfig, ctx.has_bias, needed)
+    return (*(g if f else None for g, f in zip(grads, flags)), None, None, None)
+
+
+radial_forward.register_autograd(_radial_autograd, setup_context=_radial_setup)

@@ -139,6 +139,48 @@ ICTC_API int32_t ictc_o2_uvu_backward(const float* left, const float* right, con
                                       int32_t shared, int32_t needed, const void* device_table,
                                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------ RadialUvuTensorProduct
+ * out = uvu(left, angular, hidden @ alpha^T + bias) with a V = 1 per-edge uvu
+ * (reference: src/ictc_o2_hp/radial_uvu.py:21-66, radial_streamed.py:37-146).
+ * Shapes: left [N, width1], angular [N, width2], hidden [N, H], alpha [P*C, H],
+ * bias [P*C] or NULL.  The edge weights are regenerated on chip and never
+ * written.  Configuration: channels (C <= 128), m_max, parity, m_max_in2,
+ * parity_in2, normalization, path_normalization, hidden (H); the device table
+ * is ictc_o2_uvu_table(channels, 1, ...) copied to the device. */
+
+ICTC_API int32_t ictc_o2_radial_workspace(int32_t channels, int32_t m_max, int32_t parity,
+                                          int32_t m_max_in2, int32_t parity_in2,
+                                          int32_t normalization, int32_t path_normalization,
+                                          int32_t hidden, int64_t rows, int32_t device,
+                                          size_t* forward_bytes, size_t* backward_bytes);
+
+/* Replaces radial_stream_forward (reference: radial_streamed.py:81-99). */
+ICTC_API int32_t ictc_o2_radial_forward(const float* left, const float* angular,
+                                        const float* radial_hidden, const float* alpha,
+                                        const float* bias, float* output, int64_t rows,
+                                        int32_t channels, int32_t m_max, int32_t parity,
+                                        int32_t m_max_in2, int32_t parity_in2,
+                                        int32_t normalization, int32_t path_normalization,
+                                        int32_t hidden, const void* device_table,
+                                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Replaces radial_stream_backward (reference: radial_streamed.py:109-139).  Role
+ * mask: 1 left, 2 angular, 4 hidden, 8 alpha, 16 bias; left and angular
+ * gradients are produced together (both buffers required if either is), and
+ * grad_alpha is required whenever the bias gradient is.  dalpha and dbias are
+ * summed over edges in a fixed order. */
+ICTC_API int32_t ictc_o2_radial_backward(const float* left, const float* angular,
+                                         const float* radial_hidden, const float* alpha,
+                                         const float* bias, const float* grad_output,
+                                         float* grad_left, float* grad_angular,
+                                         float* grad_hidden, float* grad_alpha,
+                                         float* grad_bias, int64_t rows, int32_t channels,
+                                         int32_t m_max, int32_t parity, int32_t m_max_in2,
+                                         int32_t parity_in2, int32_t normalization,
+                                         int32_t path_normalization, int32_t hidden,
+                                         int32_t needed, const void* device_table,
+                                         void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
