@@ -1,23 +1,31 @@
 #!/usr/bin/env python
-"""Benchmark of the fused TensorProduct forward + VJP on B200 (the BASELINE metric).
+"""Benchmark of the B200 tensor-product kernels on the BASELINE configurations.
 
-One step = TensorProduct(128, 6, parity='full') forward and full VJP (dx, dy, dw)
-with a ones cotangent over N = 65,536 rows per GPU (config 2 of the benchmark
-recipe; seeded init, iid N(0, 1) inputs).  With N > 1 GPUs (torchrun, one process
-per GPU) every rank runs its own 65,536-row shard and dw is all-reduced over NCCL
-(weak scaling); `value` is rows of all ranks / max-over-ranks step time.
+Default workload (the BASELINE metric): TensorProduct(128, 6, parity='full')
+forward and full VJP (dx, dy, dw) with a ones cotangent over N = 65,536 rows per
+GPU (config 2; seeded init, iid N(0, 1) inputs).  With N > 1 GPUs (torchrun, one
+process per GPU) every rank runs its own 65,536-row shard and dw is all-reduced
+over NCCL (weak scaling); `value` = rows of all ranks / max-over-ranks step time.
 
-Prints one JSON line with the metric, the roofline of the dominant kernel, an
-end-to-end figure through the public API with host buffers, clocks sampled during
-the timed region, and (rank 0, N = 1) the CPU oracle timed on the host cores.
-`--impl reference` times the reference algorithm's CPU restatement (the oracle
-port) on the host cores instead.
+Other workloads (``--workload``): ``uvu`` = UvuTensorProduct(128, 32, 3) shared
+weights over 131,072 rows per GPU (config 4); ``radial`` = the config-5 message-
+passing layer, 1,048,576 edges in total sharded over the ranks (strong scaling),
+Bessel(8) x cosine-cutoff radial basis -> MLP 8->64->64 (SiLU) -> fused affine +
+V=1 uvu (C=64, m_max=3, full, angular harmonics up to 3), forward and VJP through
+the whole radial network, one all-reduce of every parameter gradient.
+
+Prints one JSON line: the metric, the roofline of the dominant kernel, an
+end-to-end figure through the public API with host buffers (H2D of the inputs and
+D2H of the results every step), clocks sampled during the timed region, and (rank
+0, N = 1) the CPU oracle timed on the host cores.  ``--impl reference`` times the
+reference algorithm's CPU restatement (the oracle port) on the host cores instead.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -29,31 +37,61 @@ ROOT = Path(__file__).resolve().parent
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
-METRIC = "fwd+VJP rows/s, TensorProduct C128 m6 full N=65536; % HBM peak; 1–8 GPU"
-A100_PUBLISHED_ROWS_PER_S = 65536 / 30.087e-3  # complete_matrix.csv:383
-CHANNELS, M_MAX, PARITY = 128, 6, "full"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+# Scalar FP32 FFMA throughput measured on this pool's B200 (profiles/fp32_peak.md).
+FP32_PEAK_TFLOPS = 72.9
+
+METRICS = {
+    "tp": "fwd+VJP rows/s, TensorProduct C128 m6 full N=65536; % HBM peak; 1–8 GPU",
+    "uvu": "fwd+VJP rows/s, UvuTensorProduct C128 V32 m3 full shared weights N=131072",
+    "radial": "fwd+VJP edges/s, RadialUvuTensorProduct C64 m3 radial MLP 8-64-64, E=1048576",
+}
+# A100 published fwd+VJP for config 2 (benchmarks/eqx/results/complete_matrix.csv:383)
+A100_TP_ROWS_PER_S = 65536 / 30.087e-3
 
 
 # ------------------------------------------------------------------ CPU baseline
 
 def _cpu_worker(task):
-    """Oracle fwd + VJP (float32) on `rows` seeded rows; returns seconds."""
-    rows, seed = task
+    """Oracle fwd + VJP (float32) on `rows` seeded rows of a workload; returns s."""
+    workload, rows, seed = task
     import numpy as np
     from oracle import o2_oracle as O
-    oracle = O.TpOracle(CHANNELS, M_MAX, PARITY)
     rng = np.random.default_rng(seed)
-    x = rng.standard_normal((rows, oracle.width), dtype=np.float32)
-    y = rng.standard_normal((rows, oracle.width), dtype=np.float32)
-    w = (rng.standard_normal(oracle.weight_numel) * 0.02).astype(np.float32)
-    g = np.ones_like(x)
-    start = time.perf_counter()
-    oracle.vjp(x, y, w, g)
+    if workload == "tp":
+        oracle = O.TpOracle(128, 6, "full")
+        x = rng.standard_normal((rows, oracle.width), dtype=np.float32)
+        y = rng.standard_normal((rows, oracle.width), dtype=np.float32)
+        w = (rng.standard_normal(oracle.weight_numel) * 0.02).astype(np.float32)
+        g = np.ones_like(x)
+        start = time.perf_counter()
+        oracle.vjp(x, y, w, g)
+    elif workload == "uvu":
+        oracle = O.UvuOracle(128, 32, 3)
+        x = rng.standard_normal((rows, oracle.width1), dtype=np.float32)
+        y = rng.standard_normal((rows, oracle.width2), dtype=np.float32)
+        w = (rng.standard_normal(oracle.weight_numel) / np.sqrt(32)).astype(np.float32)
+        g = np.ones_like(x)
+        start = time.perf_counter()
+        oracle.vjp(x, y, w, g, shared=True)
+    else:
+        uvu = O.UvuOracle(64, 1, 3, "full", "canonical")
+        radial = O.RadialOracle(uvu)
+        x = rng.standard_normal((rows, uvu.width1), dtype=np.float32)
+        y = rng.standard_normal((rows, uvu.width2), dtype=np.float32)
+        h = rng.standard_normal((rows, 64), dtype=np.float32)
+        a = (rng.standard_normal((uvu.weight_numel, 64)) / 8).astype(np.float32)
+        g = np.ones_like(x)
+        start = time.perf_counter()
+        radial.vjp(x, y, h, a, g)
     return time.perf_counter() - start
 
 
-def cpu_rows_per_second(rows_per_worker: int, steps: int, warmup: int) -> dict:
+def _pin_single_thread():
+    os.environ["OMP_NUM_THREADS"] = "1"
+
+
+def cpu_units_per_second(workload: str, rows_per_worker: int, steps: int, warmup: int) -> dict:
     """Times the CPU oracle on all host cores (one spawned process per core)."""
     import multiprocessing as mp
     cores = os.cpu_count() or 1
@@ -61,19 +99,18 @@ def cpu_rows_per_second(rows_per_worker: int, steps: int, warmup: int) -> dict:
     values = []
     with ctx.Pool(cores, initializer=_pin_single_thread) as pool:
         for step in range(warmup + steps):
-            tasks = [(rows_per_worker, 1000 * step + i) for i in range(cores)]
+            tasks = [(workload, rows_per_worker, 1000 * step + i) for i in range(cores)]
             elapsed = max(pool.map(_cpu_worker, tasks))
             if step >= warmup:
                 values.append(rows_per_worker * cores / elapsed)
-    return {"value": statistics.median(values), "unit": "rows/s", "cores": cores,
-            "kind": "port",
+    unit = "edges/s" if workload == "radial" else "rows/s"
+    return {"value": statistics.median(values), "unit": unit, "cores": cores, "kind": "port",
             "sample": f"{rows_per_worker} rows x {cores} processes per step (float32 numpy "
-                      f"oracle, TensorProduct({CHANNELS},{M_MAX},{PARITY!r}) fwd+VJP, ones "
-                      f"cotangent), median of {steps} steps"}
+                      f"oracle of the reference algorithm, {workload} fwd+VJP), median of "
+                      f"{steps} steps"}
 
 
-def _pin_single_thread():
-    os.environ["OMP_NUM_THREADS"] = "1"
+CPU_ROWS = {"tp": 1024, "uvu": 16, "radial": 256}
 
 
 # ------------------------------------------------------------------ clocks
@@ -88,6 +125,7 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu_index = gpu_index
         self.proc = None
+        self.lines = []
 
     def __enter__(self):
         try:
@@ -100,7 +138,6 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -108,13 +145,13 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            self.lines = [line for line in out.splitlines() if line.strip()]
         return False
 
     def summary(self) -> dict:
         sm, mx, reasons = [], [], set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in getattr(self, "lines", []):
+        for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -132,14 +169,226 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-# ------------------------------------------------------------------ GPU arm
-
 def peaks() -> tuple[dict, str]:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         return json.loads(path.read_text()), "measured"
     return dict(FALLBACK_PEAKS), "fallback"
 
+
+# ------------------------------------------------------------------ workloads
+
+class TpWorkload:
+    """Config 2: TensorProduct(128, 6, 'full') fwd + VJP, 65,536 rows per GPU."""
+
+    name, scaling, unit = "tp", "weak", "rows/s"
+
+    def __init__(self, args, device, rank, world):
+        import torch
+        from ictc_o2_hp_b200 import TensorProduct, ops
+        self.ops, self.torch, self.world = ops, torch, world
+        self.rows = args.rows or 65536
+        torch.manual_seed(0)
+        self.tp = TensorProduct(128, 6, parity="full").to(device)
+        self.W = self.tp.representation_dimension
+        gen = torch.Generator(device=device)
+        gen.manual_seed(1000 + rank)
+        self.x = torch.randn(self.rows, self.W, device=device, generator=gen)
+        self.y = torch.randn(self.rows, self.W, device=device, generator=gen)
+        self.g = torch.ones(self.rows, self.W, device=device)
+        self.units = self.rows
+        self.launches = 4  # forward; backward prescale, main, slot reduction
+
+    def step(self, x=None, y=None, g=None):
+        torch = self.torch
+        x = (self.x if x is None else x).detach().requires_grad_(True)
+        y = (self.y if y is None else y).detach().requires_grad_(True)
+        out = self.tp(x, y)
+        dx, dy, dw = torch.autograd.grad(out, (x, y, self.tp.weight),
+                                         self.g if g is None else g)
+        if self.world > 1:
+            torch.distributed.all_reduce(dw)
+        return out, dx, dy, dw
+
+    def kernels(self, time_op):
+        ops, w = self.ops, self.tp.weight.detach()
+        fwd = time_op(lambda: ops.tp_forward(self.x, self.y, w, 128, 6, "full", "component"))
+        bwd = time_op(lambda: ops.tp_backward(self.x, self.y, w, self.g, 128, 6, "full",
+                                              "component"))
+        return {"tp_forward": (fwd, 12 * self.W * self.rows),
+                "tp_backward": (bwd, 20 * self.W * self.rows)}, "hbm"
+
+    def host_inputs(self):
+        return (self.x, self.y, self.g)
+
+    def config(self):
+        return {"workload": f"TensorProduct(128, 6, parity='full') forward + VJP (dx, dy, dw), "
+                            f"{self.rows} rows per GPU, ones cotangent",
+                "rows_per_gpu": self.rows, "width": self.W,
+                "weight_numel": self.tp.weight.numel(),
+                "l2": f"inputs larger than L2 (each operand {self.rows * self.W * 4 / 1e6:.0f} MB)",
+                "parallelism": f"row shards on {self.world} GPU(s), one NCCL all_reduce of dw"}
+
+    def step_bytes(self):
+        return 32 * self.W * self.rows
+
+
+class UvuWorkload:
+    """Config 4 (shared weights): UvuTensorProduct(128, 32, 3) fwd + VJP."""
+
+    name, scaling, unit = "uvu", "weak", "rows/s"
+
+    def __init__(self, args, device, rank, world):
+        import torch
+        from ictc_o2_hp_b200 import UvuTensorProduct, ops
+        self.ops, self.torch, self.world = ops, torch, world
+        self.rows = args.rows or 131072
+        torch.manual_seed(0)
+        self.tp = UvuTensorProduct(128, 32, 3).to(device)
+        with torch.no_grad():
+            self.tp.weight.copy_(torch.randn(self.tp.weight_numel, device=device) / 32 ** 0.5)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(2000 + rank)
+        self.x = torch.randn(self.rows, self.tp.input1_dimension, device=device, generator=gen)
+        self.y = torch.randn(self.rows, self.tp.input2_dimension, device=device, generator=gen)
+        self.g = torch.ones(self.rows, self.tp.input1_dimension, device=device)
+        self.units = self.rows
+        self.launches = 6
+        e2 = self.tp.entries_in2
+        self.fma_per_row = sum(128 * 32 * e2[j].dim for (_, j, _) in self.tp.paths)
+
+    def step(self, x=None, y=None, g=None):
+        torch = self.torch
+        x = (self.x if x is None else x).detach().requires_grad_(True)
+        y = (self.y if y is None else y).detach().requires_grad_(True)
+        out = self.tp(x, y)
+        dx, dy, dw = torch.autograd.grad(out, (x, y, self.tp.weight),
+                                         self.g if g is None else g)
+        if self.world > 1:
+            torch.distributed.all_reduce(dw)
+        return out, dx, dy, dw
+
+    def kernels(self, time_op):
+        ops, tp = self.ops, self.tp
+        w = tp.weight.detach()
+        fwd = time_op(lambda: ops.uvu_forward(self.x, self.y, w, tp._table, tp._config, True))
+        bwd = time_op(lambda: ops.uvu_backward(self.x, self.y, w, self.g, tp._table, tp._config,
+                                               True, 7))
+        flops = 2 * self.fma_per_row * self.rows
+        return {"uvu_forward": (fwd, flops), "uvu_backward": (bwd, 3 * flops)}, "fp32"
+
+    def host_inputs(self):
+        return (self.x, self.y, self.g)
+
+    def config(self):
+        return {"workload": f"UvuTensorProduct(128, 32, 3, parity='full') shared weights, "
+                            f"forward + VJP (dx, dy, dw), {self.rows} rows per GPU",
+                "rows_per_gpu": self.rows, "weight_numel": self.tp.weight_numel,
+                "l2": "inputs larger than L2",
+                "parallelism": f"row shards on {self.world} GPU(s), one NCCL all_reduce of dw"}
+
+    def step_bytes(self):
+        return (3 * self.tp.input1_dimension + self.tp.input2_dimension) * 4 * self.rows * 2
+
+
+class RadialWorkload:
+    """Config 5: 1,048,576 edges over 65,536 nodes, sharded over the ranks."""
+
+    name, scaling, unit = "radial", "strong", "edges/s"
+    EDGES, NODES, RC = 1048576, 65536, 5.0
+
+    def __init__(self, args, device, rank, world):
+        import torch
+        from ictc_o2_hp_b200 import RadialUvuTensorProduct, UvuTensorProduct, ops
+        from ictc_o2_hp_b200.parallel import shard_bounds
+        self.ops, self.torch, self.world = ops, torch, world
+        total = args.rows or self.EDGES
+        start, stop = shard_bounds(total, world, rank)
+        self.total, self.edges = total, stop - start
+        torch.manual_seed(0)
+        tp = UvuTensorProduct(64, 1, 3, parity="full", parity_in2="canonical",
+                              shared_weights=False)
+        self.trunk = torch.nn.Sequential(torch.nn.Linear(8, 64), torch.nn.SiLU(),
+                                         torch.nn.Linear(64, 64), torch.nn.SiLU()).to(device)
+        self.model = RadialUvuTensorProduct(
+            tp, torch.nn.Linear(64, tp.weight_numel, bias=False)).to(device)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(3000)
+        nodes = torch.randn(self.NODES, tp.input1_dimension, device=device, generator=gen)
+        src = torch.randint(0, self.NODES, (total,), device=device, generator=gen)
+        off = torch.randint(1, self.NODES, (total,), device=device, generator=gen)
+        dst = (src + off) % self.NODES  # uniform over the other nodes: no self-loops
+        r = torch.rand(total, device=device, generator=gen) * 4.5 + 0.5
+        theta = torch.rand(total, device=device, generator=gen) * 2 * math.pi
+        sl = slice(start, stop)
+        # gather of node features by source: outside the reference chain
+        self.x = nodes[src[sl]].contiguous()
+        self.dst = dst[sl]
+        self.r = r[sl].contiguous()
+        th = theta[sl]
+        self.angular = torch.stack([torch.ones_like(th)] + [
+            f(m * th) for m in range(1, 4) for f in (torch.cos, torch.sin)], dim=-1).contiguous()
+        self.g = torch.ones(self.edges, tp.input1_dimension, device=device)
+        self.units = self.edges
+        self.launches = 6
+        self.params = list(self.trunk.parameters()) + list(self.model.parameters())
+
+    def basis(self, r):
+        torch = self.torch
+        n = torch.arange(1, 9, device=r.device, dtype=r.dtype)
+        bessel = math.sqrt(2 / self.RC) * torch.sin(n * math.pi * r[:, None] / self.RC) / r[:, None]
+        cutoff = 0.5 * (torch.cos(math.pi * r / self.RC) + 1)
+        return bessel * cutoff[:, None]
+
+    def step(self, x=None, y=None, g=None):
+        torch = self.torch
+        x = (self.x if x is None else x).detach().requires_grad_(True)
+        ang = (self.angular if y is None else y).detach().requires_grad_(True)
+        hidden = self.trunk(self.basis(self.r))
+        out = self.model(x, ang, hidden)
+        grads = torch.autograd.grad(out, [x, ang] + self.params, self.g if g is None else g)
+        if self.world > 1:
+            flat = torch.cat([t.reshape(-1) for t in grads[2:]])
+            torch.distributed.all_reduce(flat)
+        return out, grads
+
+    def kernels(self, time_op):
+        ops, m = self.ops, self.model
+        torch = self.torch
+        with torch.no_grad():
+            hidden = self.trunk(self.basis(self.r)).contiguous()
+        alpha = m.radial_out.weight.detach()
+        empty = alpha.new_empty(0)
+        rc = m._rconfig()
+        fwd = time_op(lambda: ops.radial_forward(self.x, self.angular, hidden, alpha, empty,
+                                                 m.tp._table, rc, False))
+        bwd = time_op(lambda: ops.radial_backward(self.x, self.angular, hidden, alpha, empty,
+                                                  self.g, m.tp._table, rc, False, 15))
+        wn = m.tp.weight_numel
+        flops = 2 * wn * 64 * self.edges  # affine regeneration per edge
+        return {"radial_forward": (fwd, flops), "radial_backward": (bwd, 3 * flops)}, "fp32"
+
+    def host_inputs(self):
+        return (self.x, self.angular, self.g)
+
+    def config(self):
+        return {"workload": "RadialUvuTensorProduct message-passing layer: 1048576 edges over "
+                            "65536 nodes, Bessel(8) x cosine cutoff 5.0, MLP 8-64-64 SiLU, fused "
+                            "affine (bias=False) + V=1 uvu C64 m3 full / angular canonical m3, "
+                            "forward + VJP through the radial network",
+                "edges_total": self.total, "edges_per_gpu": self.edges,
+                "l2": "inputs larger than L2 (per-edge features 3.7 GB)",
+                "parallelism": f"edge shards on {self.world} GPU(s), one NCCL all_reduce of all "
+                               "parameter gradients"}
+
+    def step_bytes(self):
+        return (3 * 896 + 2 * 7 + 64 * 2) * 4 * self.edges
+
+
+WORKLOADS = {"tp": TpWorkload, "uvu": UvuWorkload, "radial": RadialWorkload}
+
+
+# ------------------------------------------------------------------ GPU arm
 
 def run_gpu(args) -> dict | None:
     import torch
@@ -155,25 +404,9 @@ def run_gpu(args) -> dict | None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
+    torch.set_float32_matmul_precision("highest")
 
-    from ictc_o2_hp_b200 import TensorProduct, ops
-
-    rows = args.rows
-    torch.manual_seed(0)
-    tp = TensorProduct(CHANNELS, M_MAX, parity=PARITY).to(device)
-    W = tp.representation_dimension
-    gen = torch.Generator(device=device)
-    gen.manual_seed(1000 + rank)
-    x = torch.randn(rows, W, device=device, generator=gen).requires_grad_(True)
-    y = torch.randn(rows, W, device=device, generator=gen).requires_grad_(True)
-    g = torch.ones(rows, W, device=device)
-
-    def step():
-        out = tp(x, y)
-        dx, dy, dw = torch.autograd.grad(out, (x, y, tp.weight), g)
-        if world > 1:
-            dist.all_reduce(dw)
-        return out, dx, dy, dw
+    wl = WORKLOADS[args.workload](args, device, rank, world)
 
     def barrier():
         if world > 1:
@@ -187,7 +420,7 @@ def run_gpu(args) -> dict | None:
         return float(t.item())
 
     for _ in range(args.warmup):
-        step()
+        wl.step()
     barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -195,60 +428,49 @@ def run_gpu(args) -> dict | None:
         time.sleep(0.3)
         start.record()
         for _ in range(args.steps):
-            step()
+            wl.step()
         end.record()
         torch.cuda.synchronize()
+        time.sleep(0.2)
     barrier()
     ms = max_over_ranks(start.elapsed_time(end) / args.steps)
-    launches_per_step = 4  # forward; backward prescale, main, slot reduction
 
     # Per-kernel timing for the roofline, on the launching (current) stream.
-    def time_op(fn, reps):
+    def time_op(fn):
         for _ in range(2):
             fn()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        for _ in range(reps):
+        for _ in range(args.steps):
             fn()
         b.record()
         torch.cuda.synchronize()
-        return a.elapsed_time(b) / reps
+        return a.elapsed_time(b) / args.steps
 
     with torch.no_grad():
-        xd, yd = x.detach(), y.detach()
-        fwd_ms = time_op(lambda: ops.tp_forward(xd, yd, tp.weight.detach(), CHANNELS, M_MAX,
-                                                PARITY, "component"), args.steps)
-        bwd_ms = time_op(lambda: ops.tp_backward(xd, yd, tp.weight.detach(), g, CHANNELS, M_MAX,
-                                                 PARITY, "component"), args.steps)
-    fwd_ms, bwd_ms = max_over_ranks(fwd_ms), max_over_ranks(bwd_ms)
+        kernels, bound = wl.kernels(time_op)
+    kernels = {k: (max_over_ranks(t), work) for k, (t, work) in kernels.items()}
 
-    # End to end through the public API with host buffers: H2D of x, y and the
-    # cotangent, forward + VJP, D2H of out, dx, dy and dw, every step.
+    # End to end through the public API with host buffers: H2D of this step's
+    # inputs from pinned memory, forward + VJP, D2H of every result.
     e2e = None
     if not args.no_e2e:
-        pin = dict(dtype=torch.float32, pin_memory=True)
-        xh, yh, gh = (torch.empty(rows, W, **pin) for _ in range(3))
-        xh.copy_(x.detach()), yh.copy_(y.detach()), gh.fill_(1.0)
-        outh, dxh, dyh = (torch.empty(rows, W, **pin) for _ in range(3))
-        dwh = torch.empty(tp.weight.numel(), **pin)
-        xd2 = torch.empty(rows, W, device=device, requires_grad=False)
-        yd2, gd2 = torch.empty_like(xd2), torch.empty_like(xd2)
+        dev_in = wl.host_inputs()
+        host_in = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in dev_in]
+        for h, d in zip(host_in, dev_in):
+            h.copy_(d)
+        staged = [torch.empty_like(d) for d in dev_in]
+        results = wl.step()
+        flat_results = [t for t in _leaves(results)]
+        host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in flat_results]
 
         def e2e_step():
-            xd2.copy_(xh, non_blocking=True)
-            yd2.copy_(yh, non_blocking=True)
-            gd2.copy_(gh, non_blocking=True)
-            xa, ya = xd2.requires_grad_(True), yd2.requires_grad_(True)
-            out = tp(xa, ya)
-            dx, dy, dw = torch.autograd.grad(out, (xa, ya, tp.weight), gd2)
-            if world > 1:
-                dist.all_reduce(dw)
-            outh.copy_(out, non_blocking=True)
-            dxh.copy_(dx, non_blocking=True)
-            dyh.copy_(dy, non_blocking=True)
-            dwh.copy_(dw, non_blocking=True)
-            xd2.requires_grad_(False), yd2.requires_grad_(False)
+            for s, h in zip(staged, host_in):
+                s.copy_(h, non_blocking=True)
+            res = list(_leaves(wl.step(*staged)))
+            for h, t in zip(host_out, res):
+                h.copy_(t.detach(), non_blocking=True)
 
         e2e_steps = max(3, min(args.steps, 10))
         for _ in range(2):
@@ -263,10 +485,10 @@ def run_gpu(args) -> dict | None:
         torch.cuda.synchronize()
         barrier()
         e2e_ms = max_over_ranks(a.elapsed_time(b) / e2e_steps)
-        e2e = {"value": rows * world / (e2e_ms * 1e-3), "unit": "rows/s",
-               "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": 3 * rows * W * 4,
-               "d2h_bytes_per_step": 3 * rows * W * 4 + tp.weight.numel() * 4,
+        total_units = wl.units * world if wl.scaling == "weak" else wl.total
+        e2e = {"value": total_units / (e2e_ms * 1e-3), "unit": wl.unit, "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host_in),
+               "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in host_out),
                "steps": e2e_steps}
 
     if world > 1:
@@ -276,47 +498,40 @@ def run_gpu(args) -> dict | None:
 
     peak, peak_kind = peaks()
     hbm = float(peak["hbm_gbs"])
-    bwd_bytes = 20 * W * rows  # x, y, g read; dx, dy written (algorithmic)
-    fwd_bytes = 12 * W * rows  # x, y read; out written
-    dominant = ("tp_backward", bwd_bytes, bwd_ms) if bwd_ms >= fwd_ms else \
-        ("tp_forward", fwd_bytes, fwd_ms)
-    achieved = dominant[1] / (dominant[2] * 1e-3) / 1e9
-    step_bytes = 32 * W * rows
+    name, (kms, work) = max(kernels.items(), key=lambda kv: kv[1][0])
+    if bound == "hbm":
+        achieved = work / (kms * 1e-3) / 1e9
+        roof = {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS)",
+                "algorithmic_bytes_per_launch": work, "traffic": TRAFFIC.get(name)}
+    else:
+        achieved = work / (kms * 1e-3) / 1e12
+        roof = {"kernel": name, "bound": "fp32", "achieved": achieved, "peak": FP32_PEAK_TFLOPS,
+                "unit": "TFLOP/s", "frac": achieved / FP32_PEAK_TFLOPS,
+                "peak_source": "scalar FFMA throughput measured on this pool (no tensor cores: "
+                               "strict FP32)", "algorithmic_flops_per_launch": work,
+                "traffic": TRAFFIC.get(name)}
+    total_units = wl.units * world if wl.scaling == "weak" else wl.total
+    value = total_units / (ms * 1e-3)
     result = {
-        "metric": METRIC,
-        "value": rows * world / (ms * 1e-3),
-        "unit": "rows/s",
+        "metric": METRICS[wl.name],
+        "value": value,
+        "unit": wl.unit,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": ms,
         "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": rows * world / (ms * 1e-3) / A100_PUBLISHED_ROWS_PER_S,
+        "scaling": wl.scaling,
+        "vs_baseline": value / A100_TP_ROWS_PER_S if wl.name == "tp" else None,
         "dtype": "f32",
-        "data": "synthetic (seeded iid N(0,1) inputs, seeded module init, ones cotangent)",
-        "config": {
-            "workload": f"TensorProduct({CHANNELS}, {M_MAX}, parity='{PARITY}') forward + VJP "
-                        f"(dx, dy, dw), {rows} rows per GPU",
-            "rows_per_gpu": rows, "width": W, "weight_numel": tp.weight.numel(),
-            "l2": "inputs larger than L2 (each operand is rows x width x 4 B = "
-                  f"{rows * W * 4 / 1e6:.0f} MB)",
-            "parallelism": f"row shards on {world} GPU(s), one NCCL all_reduce of dw",
-        },
-        "step_hbm_fraction": step_bytes / (ms * 1e-3) / 1e9 / hbm,
-        "kernel_ms": {"tp_forward": fwd_ms, "tp_backward": bwd_ms},
-        "roofline": {
-            "kernel": dominant[0],
-            "bound": "hbm",
-            "achieved": achieved,
-            "peak": hbm,
-            "unit": "GB/s",
-            "frac": achieved / hbm,
-            "peak_source": f"{peak_kind} hbm_gbs",
-            "algorithmic_bytes_per_launch": dominant[1],
-            "traffic": None,
-        },
-        "gpu_launches": launches_per_step * args.steps,
+        "data": "synthetic (seeded iid N(0,1) inputs, seeded init, ones cotangent)",
+        "config": wl.config(),
+        "step_hbm_fraction": wl.step_bytes() * (world if wl.scaling == "weak" else 1)
+                             / world / (ms * 1e-3) / 1e9 / hbm,
+        "kernel_ms": {k: t for k, (t, _) in kernels.items()},
+        "roofline": roof,
+        "gpu_launches": wl.launches * args.steps,
         "clocks": clocks.summary(),
     }
     if e2e is not None:
@@ -324,37 +539,57 @@ def run_gpu(args) -> dict | None:
     return result
 
 
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
+# dominant kernels from ncu captures, scaled to the bench launch by units
+# processed (profiles/*.md give the commands and the raw figures).
+TRAFFIC = {}
+
+
+def _leaves(value):
+    import torch
+    if isinstance(value, torch.Tensor):
+        yield value
+    elif isinstance(value, (list, tuple)):
+        for v in value:
+            yield from _leaves(v)
+
+
 # ------------------------------------------------------------------ reference arm
 
 def run_reference(args) -> dict | None:
     if int(os.environ.get("RANK", "0")) != 0:
         return None
-    base = cpu_rows_per_second(args.cpu_rows, args.steps, max(1, min(args.warmup, 1)))
+    rows = args.cpu_rows or CPU_ROWS[args.workload]
+    base = cpu_units_per_second(args.workload, rows, args.steps, max(1, min(args.warmup, 1)))
     value = base["value"]
     return {
-        "metric": METRIC, "impl": "reference", "value": value, "unit": "rows/s",
-        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": args.cpu_rows * base["cores"] / value * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "metric": METRICS[args.workload], "impl": "reference", "value": value,
+        "unit": base["unit"], "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": rows * base["cores"] / value * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded iid N(0,1) inputs, ones cotangent)",
-        "config": {"workload": f"TensorProduct({CHANNELS}, {M_MAX}, parity='{PARITY}') forward "
-                               f"+ VJP on the CPU (reference algorithm, numpy port), bounded "
-                               f"sample of {args.cpu_rows} rows per core per step"},
+        "config": {"workload": f"{args.workload} forward + VJP on the host CPU (reference "
+                               f"algorithm, numpy port), bounded sample of {rows} rows per core "
+                               f"per step"},
         "cpu_baseline": base,
-        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0,
+        "e2e": {"value": value, "unit": base["unit"], "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
 
 
 def main(argv=None) -> int:
-    parser = argparse.ArgumentParser(description=__doc__)
+    parser = argparse.ArgumentParser(description=__doc__,
+                                     formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    parser.add_argument("--rows", type=int, default=65536)
-    parser.add_argument("--cpu-rows", type=int, default=1024,
-                        help="rows per host core per CPU-baseline step")
+    parser.add_argument("--workload", choices=tuple(WORKLOADS), default="tp")
+    parser.add_argument("--rows", type=int, default=0,
+                        help="rows per GPU (tp, uvu) or total edges (radial); 0 = config")
+    parser.add_argument("--cpu-rows", type=int, default=0,
+                        help="rows per host core per CPU-baseline step; 0 = default")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     args = parser.parse_args(argv)
@@ -372,7 +607,7 @@ def main(argv=None) -> int:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         # The process pool starts before the first CUDA call (spawned workers).
-        cpu = cpu_rows_per_second(args.cpu_rows, 3, 1)
+        cpu = cpu_units_per_second(args.workload, args.cpu_rows or CPU_ROWS[args.workload], 3, 1)
     result = run_gpu(args)
     if result is not None:
         if cpu is not None:
