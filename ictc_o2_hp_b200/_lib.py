@@ -36,6 +36,7 @@ SIGNATURES = {
                                              ctypes.POINTER(_size)]),
     "ictc_o2_tp_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _size, _i64, _i32,
                                    _i32, _i32, _i32, _vp]),
+    "ictc_o2_tp_backward_noalloc": (_i32, [_vp] * 7 + [_i64, _i32, _i32, _i32, _i32, _vp]),
     "ictc_o2_uvu_table": (_i32, [_i32] * 8 + [ctypes.POINTER(_i32), _i64,
                                               ctypes.POINTER(_i64)]),
     "ictc_o2_uvu_workspace": (_i32, [_i32] * 8 + [_i32, _i64, _i32, ctypes.POINTER(_size),

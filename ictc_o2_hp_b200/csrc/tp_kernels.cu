@@ -27,6 +27,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <initializer_list>
+#include <mutex>
 
 #include "common.cuh"
 #include "o2_paths.cuh"
@@ -1083,4 +1084,87 @@ extern "C" int32_t ictc_o2_tp_backward(const float* left, const float* right, co
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "reduce launch");
   return ICTC_OK;
+}
+
+// ------------------------------------------------------------ no-alloc backward
+//
+// Some callers cannot allocate device memory at the point where they need the
+// backward pass: a host runtime whose allocator is owned by someone else (a
+// framework pool that must not be bypassed, an embedded engine that reserved all
+// device memory up front) or code running under a policy that forbids
+// cudaMalloc/cudaFree on the hot path.  They get ictc_o2_tp_backward_noalloc: the
+// same kernels and launch plan as ictc_o2_tp_backward, with the workspace taken
+// from a fixed array in device global memory that the library owns.
+//
+// The array is kTpNoAllocScratchBytes (32 MiB) per GPU; every GPU on which the
+// library's module is loaded holds it until the process exits.  Host code must
+// not hand the array's name to a kernel (on the host the name is only a stand-in
+// for the device symbol), so the first call on each device looks up the device
+// address with cudaGetSymbolAddress while that device is current and caches it.
+// That first call should therefore be made before any stream capture begins.
+//
+// Nothing in the array has to start at zero: the prescale kernel rewrites the
+// weight chunks on every call, and every slot's partial weight-gradient row is
+// written in full before the slot reduction reads it.  All calls on a device
+// share the one array, so calls whose kernels overlap on the GPU (concurrent
+// streams, or several host threads) race on it; the caller must order them.
+
+namespace ictc {
+namespace {
+
+constexpr size_t kTpNoAllocScratchBytes = size_t(32) << 20;
+constexpr int kTpNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_tp_noalloc_scratch[kTpNoAllocScratchBytes];
+
+std::mutex g_tp_noalloc_mutex;
+void* g_tp_noalloc_address[kTpNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device (looked up once).
+int tp_noalloc_scratch(int device, void** address) {
+  if (device < 0 || device >= kTpNoAllocMaxDevices)
+    return fail(ICTC_ERR_UNSUPPORTED, "device ordinal %d beyond the %d supported", device,
+                kTpNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_tp_noalloc_mutex);
+  if (g_tp_noalloc_address[device] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_tp_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress (backward scratch)");
+    g_tp_noalloc_address[device] = p;
+  }
+  *address = g_tp_noalloc_address[device];
+  return ICTC_OK;
+}
+
+}  // namespace
+}  // namespace ictc
+
+extern "C" int32_t ictc_o2_tp_backward_noalloc(const float* left, const float* right,
+                                               const float* weight, const float* grad_output,
+                                               float* grad_left, float* grad_right,
+                                               float* grad_weight, int64_t rows, int32_t channels,
+                                               int32_t m_max, int32_t parity,
+                                               int32_t normalization, void* stream) {
+  int st = validate(rows, channels, m_max, parity, normalization);
+  if (st != ICTC_OK) return st;
+  if (rows == 0)  // writes a zero grad_weight; needs no workspace
+    return ictc_o2_tp_backward(left, right, weight, grad_output, grad_left, grad_right,
+                               grad_weight, nullptr, 0, rows, channels, m_max, parity,
+                               normalization, stream);
+  int device = 0;
+  if ((st = current_device(&device)) != ICTC_OK) return st;
+  size_t need = 0;
+  if ((st = ictc_o2_tp_backward_workspace(rows, channels, m_max, parity, device, &need)) !=
+      ICTC_OK)
+    return st;
+  if (need > kTpNoAllocScratchBytes)
+    return fail(ICTC_ERR_WORKSPACE,
+                "no-alloc backward: channels=%d m_max=%d needs %zu bytes of scratch, more than "
+                "the fixed %zu; call ictc_o2_tp_backward with a caller workspace instead",
+                channels, m_max, need, kTpNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if ((st = tp_noalloc_scratch(device, &scratch)) != ICTC_OK) return st;
+  return ictc_o2_tp_backward(left, right, weight, grad_output, grad_left, grad_right, grad_weight,
+                             scratch, kTpNoAllocScratchBytes, rows, channels, m_max, parity,
+                             normalization, stream);
 }

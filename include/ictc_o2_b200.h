@@ -87,6 +87,22 @@ ICTC_API int32_t ictc_o2_tp_backward(const float* left, const float* right, cons
                             int64_t rows, int32_t channels, int32_t m_max, int32_t parity,
                             int32_t normalization, void* stream);
 
+/* ictc_o2_tp_backward for callers that cannot allocate device memory (their
+ * allocator belongs to a host runtime or a memory pool they must not bypass, or
+ * device memory was reserved up front): no counterpart in the reference.  Same
+ * kernels and results as ictc_o2_tp_backward; the workspace is a fixed 32 MiB
+ * array in device memory owned by the library, held on every GPU that loads it.
+ * Sizes whose workspace (ictc_o2_tp_backward_workspace) exceeds 32 MiB return
+ * ICTC_ERR_WORKSPACE.  The first call on a device looks up the array's device
+ * address; make it before any stream capture.  Calls share the array: calls
+ * that overlap on the GPU race and must be ordered by the caller.  Nothing in
+ * the array needs clearing between calls.  Allocates no memory. */
+ICTC_API int32_t ictc_o2_tp_backward_noalloc(const float* left, const float* right,
+                                    const float* weight, const float* grad_output,
+                                    float* grad_left, float* grad_right, float* grad_weight,
+                                    int64_t rows, int32_t channels, int32_t m_max,
+                                    int32_t parity, int32_t normalization, void* stream);
+
 /* ------------------------------------------------------------ UvuTensorProduct
  * First input / output: C channels per representation copy, flat
  * [copy, channel, component] blocks; second input: V channels per copy
