@@ -38,8 +38,9 @@ if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
-# Scalar FP32 FFMA throughput measured on this pool's B200 (profiles/fp32_peak.md).
-FP32_PEAK_TFLOPS = 72.9
+# FP32 FMA peak of a B200: 148 SMs x 128 FMA lanes x 2 FLOP x 1.965 GHz (max SM clock).
+# The uvu and radial kernels are strict FP32 (no tensor cores), so this is their roof.
+FP32_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 
 METRICS = {
     "tp": "fwd+VJP rows/s, TensorProduct C128 m6 full N=65536; % HBM peak; 1–8 GPU",
@@ -508,8 +509,8 @@ def run_gpu(args) -> dict | None:
         achieved = work / (kms * 1e-3) / 1e12
         roof = {"kernel": name, "bound": "fp32", "achieved": achieved, "peak": FP32_PEAK_TFLOPS,
                 "unit": "TFLOP/s", "frac": achieved / FP32_PEAK_TFLOPS,
-                "peak_source": "scalar FFMA throughput measured on this pool (no tensor cores: "
-                               "strict FP32)", "algorithmic_flops_per_launch": work,
+                "peak_source": "nominal FP32 FMA peak at the 1965 MHz max SM clock (strict "
+                               "FP32, no tensor cores)", "algorithmic_flops_per_launch": work,
                 "traffic": TRAFFIC.get(name)}
     total_units = wl.units * world if wl.scaling == "weak" else wl.total
     value = total_units / (ms * 1e-3)
@@ -541,8 +542,9 @@ def run_gpu(args) -> dict | None:
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # dominant kernels from ncu captures, scaled to the bench launch by units
-# processed (profiles/*.md give the commands and the raw figures).
-TRAFFIC = {}
+# processed (profiles/tp_*_c128_m6_full.md give the commands and the raw figures:
+# 1,063.0 MB and 626.1 MB at 16,384 rows, x4 for the 65,536-row bench launch).
+TRAFFIC = {"tp_backward": 4.252e9, "tp_forward": 2.504e9}
 
 
 def _leaves(value):
