@@ -593,6 +593,68 @@ __global__ void __launch_bounds__(kWideWarps * 32, 1)
   });
 }
 
+// Forward with the group's path weights in shared memory: a CTA of
+// kGroupFwdWarps warps serves ONE channel group and its warps take rows round-
+// robin, so the weights (float4 chunks in Paths::vjp order, built at start from
+// the packed vector) cost 16 B x chunks per lane of shared memory instead of
+// Paths::n registers.  The freed registers buy resident warps, which hide the
+// latency of the coalesced global loads of x and y.
+constexpr int kGroupFwdWarps = 4;
+
+template <int M, bool FULL>
+__global__ void __launch_bounds__(kGroupFwdWarps * 32)
+    tp_forward_grouped(const float* __restrict__ x, const float* __restrict__ y,
+                       const float* __restrict__ w, float* __restrict__ out, int64_t rows,
+                       TpLayout L, Mags mags, int groups, int64_t row_slots, bool vec2) {
+  using P = Paths<M, FULL>;
+  constexpr int S = 2 * M + 2;
+  extern __shared__ __align__(16) float4 wsm[];  // [chunk][32 lanes]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int group = static_cast<int>(blockIdx.x % groups);
+  const LaneMap<FULL> lm(group, lane, L.C);
+  static_for<P::chunks>([&](auto k) {
+    if (k % kGroupFwdWarps != warp) return;
+    float v[4];
+    static_for<4>([&](auto e) {
+      constexpr int pos = 4 * k + e;
+      if constexpr (pos < P::n) {
+        constexpr int I = P::vjp.idx[pos];
+        constexpr ChanPath cp = P::table.p[I];
+        const bool used = lm.active && (!FULL || cp.copied || lm.q == 0);
+        v[e] = used ? __ldg(w + weight_index<M, FULL, I>(L.C, lm.c, lm.q)) * mags.m[cp.cls]
+                    : 0.0f;
+      } else {
+        v[e] = 0.0f;
+      }
+    });
+    wsm[k * 32 + lane] = make_float4(v[0], v[1], v[2], v[3]);
+  });
+  __syncthreads();
+  const SharedChunks chunks{static_cast<uint32_t>(__cvta_generic_to_shared(wsm + lane)),
+                            32 * static_cast<int>(sizeof(float4))};
+  const int64_t first = static_cast<int64_t>(blockIdx.x / groups) * kGroupFwdWarps + warp;
+  for (int64_t row = first; row < rows; row += row_slots) {
+    float a[S], b[S], o[S];
+    load_slots<M, FULL>(GlobalRow{x + row * L.width, vec2}, L, lm.c, lm.q, a);
+    load_slots<M, FULL>(GlobalRow{y + row * L.width, vec2}, L, lm.c, lm.q, b);
+#pragma unroll
+    for (int i = 0; i < S; ++i) o[i] = 0.0f;
+    float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    auto step = [&](auto K) {
+      constexpr int I = P::vjp.idx[K];
+      if constexpr (K % 4 == 0) w4 = chunks.ld(K / 4);
+      const float wv = K % 4 == 0 ? w4.x : (K % 4 == 1 ? w4.y : (K % 4 == 2 ? w4.z : w4.w));
+      path_forward<M, FULL, I>(a, b, o, wv);
+    };
+    static_for<P::nfreq>(step);
+    if (!FULL || lm.q == 0) {
+      static_for<P::n - P::nfreq>(
+          [&](auto J) { step(std::integral_constant<int, P::nfreq + J>{}); });
+    }
+    if (lm.active) store_slots<M, FULL>(out + row * L.width, L, lm.c, lm.q, vec2, o);
+  }
+}
+
 template <int M, bool FULL>
 __global__ void __launch_bounds__(kStagedWarps * 32, 1)
     tp_backward_staged(const float* __restrict__ x, const float* __restrict__ y,
@@ -725,6 +787,8 @@ using BackwardStagedFn = void (*)(const float*, const float*, const float4*, con
                                   float*, float*, float*, int64_t, int64_t, TpLayout, Mags, int,
                                   int, int, int);
 using PrescaleFn = void (*)(const float*, float4*, TpLayout, Mags, int);
+using ForwardGroupedFn = void (*)(const float*, const float*, const float*, float*, int64_t,
+                                  TpLayout, Mags, int, int64_t, bool);
 
 // ICTC_ONLY_ORDER=m builds one order only (quick register/spill checks).
 #ifdef ICTC_ONLY_ORDER
@@ -741,6 +805,7 @@ struct Kernels {
   BackwardStagedFn bwd_staged;
   PrescaleFn prescale;
   int chunks;  // float4 weight chunks per thread (Paths::chunks)
+  ForwardGroupedFn fwd_grouped;
 };
 
 template <int M, bool FULL>
@@ -750,9 +815,10 @@ constexpr Kernels kernels_for() {
     if constexpr (wide_forward_fits<M, FULL>()) wide = &tp_forward_wide<M, FULL>;
     return Kernels{wide, &tp_forward_direct<M, FULL>, &tp_backward_direct<M, FULL>,
                    &tp_forward_staged<M, FULL>, &tp_backward_staged<M, FULL>,
-                   &prescale_kernel<M, FULL>, Paths<M, FULL>::chunks};
+                   &prescale_kernel<M, FULL>, Paths<M, FULL>::chunks,
+                   &tp_forward_grouped<M, FULL>};
   } else {
-    return Kernels{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0};
+    return Kernels{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0, nullptr};
   }
 }
 
@@ -955,6 +1021,27 @@ extern "C" int32_t ictc_o2_tp_forward(const float* left, const float* right, con
   // measured shape; the staged and wide variants stay selectable for experiments.
   const char* variant = getenv("ICTC_TP_FORWARD");
   const bool al16 = aligned16({left, right, output});
+  if (variant == nullptr || strcmp(variant, "grouped") == 0) {
+    const bool vec2 = (L.width % 2 == 0) && aligned(left, 8) && aligned(right, 8) &&
+                      aligned(output, 8);
+    const int groups = static_cast<int>(ceil_div(channels, full ? 16 : 32));
+    const size_t smem = static_cast<size_t>(k.chunks) * 32 * sizeof(float4);
+    const void* fn = reinterpret_cast<const void*>(k.fwd_grouped);
+    if ((st = allow_smem(fn, smem)) != ICTC_OK) return st;
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn,
+                                                                  kGroupFwdWarps * 32, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    int64_t per_group =
+        static_cast<int64_t>(sm_count(device)) * (per_sm > 0 ? per_sm : 1) / groups;
+    if (per_group < 1) per_group = 1;
+    const int64_t needed = ceil_div(rows, kGroupFwdWarps);
+    if (per_group > needed) per_group = needed;
+    k.fwd_grouped<<<static_cast<unsigned>(per_group * groups), kGroupFwdWarps * 32, smem, s>>>(
+        left, right, weight, output, rows, L, mags, groups, per_group * kGroupFwdWarps, vec2);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "tp_forward launch");
+  }
   const bool want_wide = variant && strcmp(variant, "wide") == 0;
   const bool want_staged = variant && strcmp(variant, "staged") == 0;
   const StagedPlan wp =
