@@ -53,175 +53,322 @@ __global__ void transpose_alpha(const float* __restrict__ a, float* __restrict__
   }
 }
 
-// gw[r,u] = sum_{kc,a,b} c[kc,a,b] g_k[r,u,kc] x_i[r,u,a] y_j[r,b]
-__device__ __forceinline__ float edge_weight_grad(const float* __restrict__ x,
-                                                  const float* __restrict__ g, const float* yrow,
-                                                  int64_t row, int u, int W1, int2 ei, int2 ek,
-                                                  int2 ej, const float* c) {
-  const float* xs = x + row * W1 + ei.x + u * ei.y;
-  const float* gs = g + row * W1 + ek.x + u * ek.y;
-  const float x0 = __ldg(xs), x1 = ei.y == 2 ? __ldg(xs + 1) : 0.f;
-  const float g0 = __ldg(gs), g1 = ek.y == 2 ? __ldg(gs + 1) : 0.f;
-  const float y0 = yrow[ej.x], y1 = ej.y == 2 ? yrow[ej.x + 1] : 0.f;
-  const float t0 = c[0] * g0 * x0 + c[2] * g0 * x1 + c[4] * g1 * x0 + c[6] * g1 * x1;
-  const float t1 = c[1] * g0 * x0 + c[3] * g0 * x1 + c[5] * g1 * x0 + c[7] * g1 * x1;
-  return t0 * y0 + t1 * y1;
+// ------------------------------------------------------------ edge-weight gradient
+//
+// gw[e,p,u] = sum_{kc,a,b} c_p[kc][a][b] g_k[e,u,kc] x_i[e,u,a] y_j[e,b], the
+// gradient of the regenerated edge weight w[e,p,u], is never stored: the dhidden
+// and dalpha kernels rebuild it tile by tile from g, x and y.  One thread builds
+// eight consecutive channels of one edge; D1 and D3 (the dims of entries i and
+// k) are compile-time so the operands stay in registers.
+
+struct GwRegs {
+  float x[16], g[16], y0, y1;
+};
+
+template <int D1, int D3>
+__device__ __forceinline__ void gw8_load(GwRegs& r, const float* __restrict__ xrow,
+                                         const float* __restrict__ grow,
+                                         const float* __restrict__ yrow, int u0, int U, int2 ei,
+                                         int2 ek, int2 ej, bool valid, bool vec) {
+  const int nu = valid ? (U - u0 < 8 ? U - u0 : 8) : 0;
+  const float* xs = xrow + ei.x + u0 * D1;
+  const float* gs = grow + ek.x + u0 * D3;
+  if (vec && nu == 8) {
+#pragma unroll
+    for (int q = 0; q < 2 * D1; ++q) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(xs) + q);
+      r.x[4 * q] = v.x; r.x[4 * q + 1] = v.y; r.x[4 * q + 2] = v.z; r.x[4 * q + 3] = v.w;
+    }
+#pragma unroll
+    for (int q = 0; q < 2 * D3; ++q) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(gs) + q);
+      r.g[4 * q] = v.x; r.g[4 * q + 1] = v.y; r.g[4 * q + 2] = v.z; r.g[4 * q + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 8 * D1; ++q) r.x[q] = q / D1 < nu ? __ldg(xs + q) : 0.f;
+#pragma unroll
+    for (int q = 0; q < 8 * D3; ++q) r.g[q] = q / D3 < nu ? __ldg(gs + q) : 0.f;
+  }
+  r.y0 = valid ? __ldg(yrow + ej.x) : 0.f;
+  r.y1 = (valid && ej.y == 2) ? __ldg(yrow + ej.x + 1) : 0.f;
 }
 
-constexpr int kDhRows = 64;
-
-// dhidden for 64 edges x 64 h per CTA (grid.y over h blocks): per path, the gw tile
-// [u][64 edges] goes to shared memory, then dh[e,h] += sum_u gw[e,u] alpha[p*U+u,h].
-__global__ void __launch_bounds__(256)
-    radial_dhidden(const float* __restrict__ x, const float* __restrict__ ang,
-                   const float* __restrict__ g, const float* __restrict__ alpha,
-                   float* __restrict__ dh, int64_t rows, int U, int H, int W1, int W2, UvuDev t,
-                   bool avec) {
-  extern __shared__ __align__(16) float sm[];
-  const int W2a = (W2 + 3) & ~3;
-  float* angt = sm;                     // [64 rows][W2a]
-  float* gwt = sm + kDhRows * W2a;      // [U][64 rows]
-  const int rq = threadIdx.x >> 4, hq = threadIdx.x & 15;  // 16 x 16
-  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kDhRows;
-  const int h0 = blockIdx.y * 64 + hq * 4;
-  for (int idx = threadIdx.x; idx < kDhRows * W2; idx += blockDim.x) {
-    const int r = idx / W2, col = idx % W2;
-    const int64_t row = row0 + r;
-    angt[r * W2a + col] = row < rows ? __ldg(ang + row * W2 + col) : 0.f;
+template <int D1, int D3>
+__device__ __forceinline__ void gw8_compute(const GwRegs& r, const float (&c)[8],
+                                            float (&out)[8]) {
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const float x0 = r.x[u * D1], x1 = D1 == 2 ? r.x[u * D1 + 1] : 0.f;
+    const float g0 = r.g[u * D3], g1 = D3 == 2 ? r.g[u * D3 + 1] : 0.f;
+    float t0 = c[0] * g0 * x0, t1 = c[1] * g0 * x0;
+    if (D1 == 2) { t0 = fmaf(c[2] * g0, x1, t0); t1 = fmaf(c[3] * g0, x1, t1); }
+    if (D3 == 2) { t0 = fmaf(c[4] * g1, x0, t0); t1 = fmaf(c[5] * g1, x0, t1); }
+    if (D1 == 2 && D3 == 2) { t0 = fmaf(c[6] * g1, x1, t0); t1 = fmaf(c[7] * g1, x1, t1); }
+    out[u] = fmaf(t0, r.y0, t1 * r.y1);
   }
+}
+
+// Runs body.template operator()<D1, D3>() for the entry dims of one path.
+template <class Body>
+__device__ __forceinline__ void with_dims(int d1, int d3, Body&& body) {
+  if (d1 == 2) {
+    if (d3 == 2) body.template operator()<2, 2>(); else body.template operator()<2, 1>();
+  } else {
+    if (d3 == 2) body.template operator()<1, 2>(); else body.template operator()<1, 1>();
+  }
+}
+
+__device__ __forceinline__ void load_coef(const UvuDev& t, int p, float (&c)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) c[e] = __ldg(t.coef + 8 * p + e);
+}
+
+// ------------------------------------------------------------ dhidden
+//
+// dh[e,h] = sum_{p,u} gw[e,p,u] alpha[p*U+u, h]: a GEMM over K = (p, u) in steps of
+// 32 channels.  CTA tile 64 edges x 64 h, thread tile 4 edges x 4 h.  Per step the
+// gw tile [32 u][64 e] is built from g, x, y and the alpha rows [32 u][64 h] are
+// copied into shared memory; both are double-buffered, with the next step's
+// operands fetched into registers before this step's GEMM.
+constexpr int kDhE = 64, kDhH = 64, kDhU = 32;
+
+struct DhArgs {
+  const float* x; const float* ang; const float* g; const float* alpha; float* dh;
+  int64_t rows; int U, H, W1, W2; UvuDev t; bool vec, avec;
+};
+
+__global__ void __launch_bounds__(256, 2) radial_dhidden(DhArgs A) {
+  __shared__ __align__(16) float gwt[2][kDhU][kDhE];
+  __shared__ __align__(16) float at[2][kDhU][kDhH];
+  const int tid = threadIdx.x;
+  const int64_t e_base = static_cast<int64_t>(blockIdx.x) * kDhE;
+  const int hb = blockIdx.y * kDhH;
+  // generation: edge ge (lanes = consecutive edges), channel octet go (warp-uniform)
+  const int ge = tid & 63, go = tid >> 6;
+  const int64_t grow_i = e_base + ge;
+  const bool gvalid = grow_i < A.rows;
+  const float* xrow = A.x + (gvalid ? grow_i : 0) * A.W1;
+  const float* gr = A.g + (gvalid ? grow_i : 0) * A.W1;
+  const float* yrow = A.ang + (gvalid ? grow_i : 0) * A.W2;
+  // alpha rows: 32 x 64 floats = 512 float4, two per thread
+  // GEMM: edges e0..e0+3, h0..h0+3
+  const int e0 = (tid & 15) * 4, h0 = (tid >> 4) * 4;
+  const int nuc = (A.U + kDhU - 1) / kDhU;
+  const int nsteps = A.t.np * nuc;
   float acc[4][4];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
     for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
-  for (int p = 0; p < t.np; ++p) {
-    const int4 pt = t.paths[p];
-    float c[8];
+
+  GwRegs r;
+  float4 av[2];
+  int cur_d1 = 1, cur_d3 = 1;
+  float c[8];
+  auto fetch = [&](int step) {
+    const int p = step / nuc, uc = step % nuc;
+    const int4 pt = A.t.paths[p];
+    const int2 ei = A.t.in1[pt.x], ej = A.t.in2[pt.y], ek = A.t.in1[pt.z];
+    cur_d1 = ei.y;
+    cur_d3 = ek.y;
+    load_coef(A.t, p, c);
+    const int u0 = uc * kDhU + go * 8;
+    with_dims(ei.y, ek.y, [&]<int D1, int D3>() {
+      gw8_load<D1, D3>(r, xrow, gr, yrow, u0, A.U, ei, ek, ej, gvalid && u0 < A.U, A.vec);
+    });
 #pragma unroll
-    for (int e = 0; e < 8; ++e) c[e] = __ldg(t.coef + 8 * p + e);
-    const int2 ei = t.in1[pt.x], ej = t.in2[pt.y], ek = t.in1[pt.z];
-    __syncthreads();
-    for (int q = threadIdx.x; q < kDhRows * U; q += blockDim.x) {
-      const int u = q % U, r = q / U;
-      const int64_t row = row0 + r;
-      gwt[u * kDhRows + r] =
-          row < rows ? edge_weight_grad(x, g, angt + r * W2a, row, u, W1, ei, ek, ej, c) : 0.f;
-    }
-    __syncthreads();
-    const float* ap = alpha + static_cast<int64_t>(p) * U * H;
-    for (int u = 0; u < U; ++u) {
-      float av[4];
-      if (avec && h0 + 3 < H) {
-        const float4 a4 = __ldg(reinterpret_cast<const float4*>(ap + static_cast<int64_t>(u) * H + h0));
-        av[0] = a4.x; av[1] = a4.y; av[2] = a4.z; av[3] = a4.w;
+    for (int s = 0; s < 2; ++s) {
+      const int q = tid + s * 256;
+      const int uu = q >> 4, h = hb + (q & 15) * 4;
+      const int u = uc * kDhU + uu;
+      const float* src = A.alpha + (static_cast<int64_t>(p) * A.U + u) * A.H + h;
+      if (u < A.U && A.avec && h + 3 < A.H) {
+        av[s] = __ldg(reinterpret_cast<const float4*>(src));
       } else {
+        float v[4];
 #pragma unroll
-        for (int b = 0; b < 4; ++b) av[b] = h0 + b < H ? __ldg(ap + static_cast<int64_t>(u) * H + h0 + b) : 0.f;
+        for (int k = 0; k < 4; ++k) v[k] = (u < A.U && h + k < A.H) ? __ldg(src + k) : 0.f;
+        av[s] = make_float4(v[0], v[1], v[2], v[3]);
       }
-      const float4 g4 = *reinterpret_cast<const float4*>(gwt + u * kDhRows + rq * 4);
-      const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
+    }
+  };
+  auto stash = [&](int buf) {
+    float out[8];
+    with_dims(cur_d1, cur_d3, [&]<int D1, int D3>() { gw8_compute<D1, D3>(r, c, out); });
+#pragma unroll
+    for (int i = 0; i < 8; ++i) gwt[buf][go * 8 + i][ge] = out[i];
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int q = tid + s * 256;
+      *reinterpret_cast<float4*>(&at[buf][q >> 4][(q & 15) * 4]) = av[s];
+    }
+  };
+  if (nsteps > 0) {
+    fetch(0);
+    stash(0);
+  }
+  __syncthreads();
+  for (int step = 0; step < nsteps; ++step) {
+    const int buf = step & 1;
+    const bool more = step + 1 < nsteps;
+    if (more) fetch(step + 1);
+#pragma unroll 8
+    for (int u = 0; u < kDhU; ++u) {
+      const float4 a4 = *reinterpret_cast<const float4*>(&gwt[buf][u][e0]);
+      const float4 b4 = *reinterpret_cast<const float4*>(&at[buf][u][h0]);
+      const float av4[4] = {a4.x, a4.y, a4.z, a4.w};
+      const float bv4[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
       for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(gv[a], av[b], acc[a][b]);
+        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(av4[a], bv4[b], acc[a][b]);
     }
+    if (more) stash(buf ^ 1);
+    __syncthreads();
   }
 #pragma unroll
   for (int a = 0; a < 4; ++a) {
-    const int64_t row = row0 + rq * 4 + a;
+    const int64_t e = e_base + e0 + a;
+    if (e >= A.rows) continue;
 #pragma unroll
     for (int b = 0; b < 4; ++b)
-      if (row < rows && h0 + b < H) dh[row * H + h0 + b] = acc[a][b];
+      if (hb + h0 + b < A.H) A.dh[e * A.H + hb + h0 + b] = acc[a][b];
   }
 }
 
-// dalpha[p*U + u, h] (and dbias) partial over a row chunk; grid (paths, u blocks x h
-// blocks, chunks).  Tile 128 u x 32 h, thread 4 u x 4 h.
-__global__ void __launch_bounds__(256)
-    radial_dalpha(const float* __restrict__ x, const float* __restrict__ ang,
-                  const float* __restrict__ g, const float* __restrict__ hidden,
-                  float* __restrict__ da, float* __restrict__ db, int64_t rows,
-                  int64_t chunk_rows, int64_t da_numel, int64_t db_numel, int U, int H, int W1,
-                  int W2, UvuDev t) {
-  extern __shared__ __align__(16) float sm[];
-  float* gwt = sm;                // [32 rows][128 u]
-  float* ht = sm + kRT * 128;     // [32 rows][32 h]
+// ------------------------------------------------------------ dalpha, dbias
+//
+// dalpha[p*U+u, h] = sum_e gw[e,p,u] hidden[e,h] and dbias[p*U+u] = sum_e gw[e,p,u]:
+// per CTA one path, a 64 u x 64 h tile and one chunk of the edges (partials are
+// summed over chunks in a fixed order afterwards).  K = edges in steps of 32:
+// the gw tile [32 e][64 u] is built on chip, the hidden rows [32 e][64 h] copied,
+// both double-buffered with register prefetch of the next step.
+constexpr int kDaE = 32, kDaU = 64, kDaH = 64;
+
+struct DaArgs {
+  const float* x; const float* ang; const float* g; const float* hidden;
+  float* da; float* db; int64_t rows, chunk_rows, da_numel, db_numel;
+  int U, H, W1, W2; UvuDev t; bool vec, hvec;
+};
+
+template <int D1, int D3>
+__device__ __forceinline__ void radial_dalpha_body(const DaArgs& A, float (*gwt)[kDaE][kDaU],
+                                                   float (*ht)[kDaE][kDaH], float* red) {
+  const int tid = threadIdx.x;
   const int p = blockIdx.x;
-  const int ntu = (U + 127) / 128;
-  const int ub = (blockIdx.y % ntu) * 128, hb = (blockIdx.y / ntu) * 32;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int uq = (warp & 3) * 8 + (lane & 7);
-  const int hq = (warp >> 2) * 4 + (lane >> 3);
-  const int u0 = ub + uq * 4, h0 = hb + hq * 4;
-  const int4 pt = t.paths[p];
+  const int nut = (A.U + kDaU - 1) / kDaU;
+  const int ub = (blockIdx.y % nut) * kDaU, hb = (blockIdx.y / nut) * kDaH;
+  const int4 pt = A.t.paths[p];
+  const int2 ei = A.t.in1[pt.x], ej = A.t.in2[pt.y], ek = A.t.in1[pt.z];
   float c[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) c[e] = __ldg(t.coef + 8 * p + e);
-  const int2 ei = t.in1[pt.x], ej = t.in2[pt.y], ek = t.in1[pt.z];
-  float acc[4][4], bacc[4];
-#pragma unroll
-  for (int a = 0; a < 4; ++a) {
-    bacc[a] = 0.f;
-#pragma unroll
-    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
-  }
-  const int64_t rbeg = static_cast<int64_t>(blockIdx.z) * chunk_rows;
-  const int64_t rend = rbeg + chunk_rows < rows ? rbeg + chunk_rows : rows;
-  for (int64_t row0 = rbeg; row0 < rend; row0 += kRT) {
-    __syncthreads();
-    for (int s = 0; s < 16; ++s) {
-      const int q = threadIdx.x + s * 256;
-      const int uu = q & 127, r = q >> 7;
-      const int u = ub + uu;
-      const int64_t row = row0 + r;
-      float v = 0.f;
-      if (row < rend && u < U) {
-        const float* ys = ang + row * W2 + ej.x;
-        const float y0 = __ldg(ys), y1 = ej.y == 2 ? __ldg(ys + 1) : 0.f;
-        const float* xs = x + row * W1 + ei.x + u * ei.y;
-        const float* gs = g + row * W1 + ek.x + u * ek.y;
-        const float x0 = __ldg(xs), x1 = ei.y == 2 ? __ldg(xs + 1) : 0.f;
-        const float g0 = __ldg(gs), g1 = ek.y == 2 ? __ldg(gs + 1) : 0.f;
-        const float t0 = c[0] * g0 * x0 + c[2] * g0 * x1 + c[4] * g1 * x0 + c[6] * g1 * x1;
-        const float t1 = c[1] * g0 * x0 + c[3] * g0 * x1 + c[5] * g1 * x0 + c[7] * g1 * x1;
-        v = t0 * y0 + t1 * y1;
-      }
-      gwt[r * 128 + uu] = v;
-    }
-    for (int q = threadIdx.x; q < kRT * 32; q += 256) {
-      const int hh = q & 31, r = q >> 5;
-      const int h = hb + hh;
-      const int64_t row = row0 + r;
-      ht[q] = (row < rend && h < H) ? __ldg(hidden + row * H + h) : 0.f;
-    }
-    __syncthreads();
-    for (int r = 0; r < kRT; ++r) {
-      const float4 g4 = *reinterpret_cast<const float4*>(gwt + r * 128 + uq * 4);
-      const float4 h4 = *reinterpret_cast<const float4*>(ht + r * 32 + hq * 4);
-      const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
-      const float hv[4] = {h4.x, h4.y, h4.z, h4.w};
-#pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        bacc[a] += gv[a];
-#pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(gv[a], hv[b], acc[a][b]);
-      }
-    }
-  }
-  float* dout = da + static_cast<int64_t>(blockIdx.z) * da_numel;
+  load_coef(A.t, p, c);
+  // generation: edge ge of the step, channels ub + go*8 .. +7
+  const int ge = tid >> 3, go = tid & 7;
+  const int u0g = ub + go * 8;
+  // GEMM: u0..u0+3 (tile-relative), h0..h0+3
+  const int u0 = (tid & 15) * 4, h0 = (tid >> 4) * 4;
+  const int64_t rbeg = static_cast<int64_t>(blockIdx.z) * A.chunk_rows;
+  const int64_t rend = rbeg + A.chunk_rows < A.rows ? rbeg + A.chunk_rows : A.rows;
+  float acc[4][4], bsum[8];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int u = u0 + a, h = h0 + b;
-      if (u < U && h < H) dout[(static_cast<int64_t>(p) * U + u) * H + h] = acc[a][b];
-    }
-  if (db != nullptr && hb == 0 && hq == 0) {
-    float* bout = db + static_cast<int64_t>(blockIdx.z) * db_numel;
+    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
-      if (u0 + a < U) bout[static_cast<int64_t>(p) * U + u0 + a] = bacc[a];
+  for (int i = 0; i < 8; ++i) bsum[i] = 0.f;
+  GwRegs r;
+  float4 hv[2];
+  auto fetch = [&](int64_t e0) {
+    const int64_t e = e0 + ge;
+    const bool valid = e < rend && u0g < A.U;
+    const int64_t row = e < rend ? e : rbeg;
+    gw8_load<D1, D3>(r, A.x + row * A.W1, A.g + row * A.W1, A.ang + row * A.W2, u0g, A.U, ei,
+                     ek, ej, valid, A.vec);
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int q = tid + s * 256;
+      const int er = q >> 4, h = hb + (q & 15) * 4;
+      const int64_t ee = e0 + er;
+      const float* src = A.hidden + (ee < rend ? ee : rbeg) * A.H + h;
+      if (ee < rend && A.hvec && h + 3 < A.H) {
+        hv[s] = __ldg(reinterpret_cast<const float4*>(src));
+      } else {
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = (ee < rend && h + k < A.H) ? __ldg(src + k) : 0.f;
+        hv[s] = make_float4(v[0], v[1], v[2], v[3]);
+      }
+    }
+  };
+  auto stash = [&](int buf) {
+    float out[8];
+    gw8_compute<D1, D3>(r, c, out);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) bsum[i] += out[i];
+    *reinterpret_cast<float4*>(&gwt[buf][ge][go * 8]) = make_float4(out[0], out[1], out[2], out[3]);
+    *reinterpret_cast<float4*>(&gwt[buf][ge][go * 8 + 4]) =
+        make_float4(out[4], out[5], out[6], out[7]);
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      const int q = tid + s * 256;
+      *reinterpret_cast<float4*>(&ht[buf][q >> 4][(q & 15) * 4]) = hv[s];
+    }
+  };
+  const int64_t nsteps = rend > rbeg ? (rend - rbeg + kDaE - 1) / kDaE : 0;
+  if (nsteps > 0) {
+    fetch(rbeg);
+    stash(0);
   }
+  __syncthreads();
+  for (int64_t step = 0; step < nsteps; ++step) {
+    const int buf = static_cast<int>(step & 1);
+    const bool more = step + 1 < nsteps;
+    if (more) fetch(rbeg + (step + 1) * kDaE);
+#pragma unroll 8
+    for (int e = 0; e < kDaE; ++e) {
+      const float4 a4 = *reinterpret_cast<const float4*>(&gwt[buf][e][u0]);
+      const float4 b4 = *reinterpret_cast<const float4*>(&ht[buf][e][h0]);
+      const float av4[4] = {a4.x, a4.y, a4.z, a4.w};
+      const float bv4[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(av4[a], bv4[b], acc[a][b]);
+    }
+    if (more) stash(buf ^ 1);
+    __syncthreads();
+  }
+  float* dout = A.da + static_cast<int64_t>(blockIdx.z) * A.da_numel;
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int u = ub + u0 + a;
+    if (u >= A.U) continue;
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+      if (hb + h0 + b < A.H) dout[(static_cast<int64_t>(p) * A.U + u) * A.H + hb + h0 + b] = acc[a][b];
+  }
+  if (A.db != nullptr && hb == 0) {
+    // sum the per-thread bias partials over the 32 edge lanes, in lane order
+#pragma unroll
+    for (int i = 0; i < 8; ++i) red[ge * kDaU + go * 8 + i] = bsum[i];
+    __syncthreads();
+    if (tid < kDaU && ub + tid < A.U) {
+      float sum = 0.f;
+      for (int k = 0; k < kDaE; ++k) sum += red[k * kDaU + tid];
+      A.db[static_cast<int64_t>(blockIdx.z) * A.db_numel + static_cast<int64_t>(p) * A.U + ub +
+           tid] = sum;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256, 2) radial_dalpha(DaArgs A) {
+  __shared__ __align__(16) float gwt[2][kDaE][kDaU];
+  __shared__ __align__(16) float ht[2][kDaE][kDaH];
+  const int4 pt = A.t.paths[blockIdx.x];
+  const int d1 = A.t.in1[pt.x].y, d3 = A.t.in1[pt.z].y;
+  float* red = &gwt[0][0][0];  // reused after the main loop (kDaE x kDaU floats)
+  with_dims(d1, d3, [&]<int D1, int D3>() { radial_dalpha_body<D1, D3>(A, gwt, ht, red); });
 }
 
 __global__ void radial_sum_chunks(const float* __restrict__ partial, float* __restrict__ dst,
@@ -250,9 +397,9 @@ int radial_validate(const RadialConfig& c) {
 }
 
 int64_t radial_chunks(int device, int64_t rows, int P, int U, int H) {
-  const int64_t tiles = static_cast<int64_t>(P) * ((U + 127) / 128) * ((H + 31) / 32);
-  int64_t chunks = (2 * sm_count(device) + tiles - 1) / tiles;
-  const int64_t max_chunks = (rows + 255) / 256;
+  const int64_t tiles = static_cast<int64_t>(P) * ((U + kDaU - 1) / kDaU) * ((H + kDaH - 1) / kDaH);
+  int64_t chunks = (4 * sm_count(device) + tiles - 1) / tiles;
+  const int64_t max_chunks = (rows + 1023) / 1024;
   if (chunks > max_chunks) chunks = max_chunks;
   return chunks < 1 ? 1 : chunks;
 }
@@ -341,17 +488,10 @@ extern "C" int32_t ictc_o2_radial_forward(const float* left, const float* angula
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   float* at = static_cast<float*>(workspace);
   transpose_alpha<<<1024, 256, 0, s>>>(alpha, at, l.np, c.U, Up, c.H);
-  const size_t smem = rowtile_smem(kRadFwd, c.H, th.width2);
-  if (smem > 220 * 1024) return fail(ICTC_ERR_UNSUPPORTED, "hidden width too large (%d)", c.H);
-  if ((st = allow_smem(reinterpret_cast<const void*>(&rowtile<kRadFwd>), smem)) != ICTC_OK)
-    return st;
   const UvuDev t = radial_dev(device_table, l);
   RowtileArgs ra{left, nullptr, radial_hidden, angular, at, bias, output, nullptr, rows,
                  c.U, Up, c.H, th.width1, c.H, th.width2, t};
-  const dim3 grid(static_cast<unsigned>(ceil_div(rows, kRT)), 1);
-  rowtile<kRadFwd><<<grid, 256, smem, s>>>(ra);
-  const cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "radial forward launch");
+  return launch_rowtile<kRadFwd>(ra, s);
 }
 
 extern "C" int32_t ictc_o2_radial_backward(
@@ -405,44 +545,34 @@ extern "C" int32_t ictc_o2_radial_backward(
   if (needed & 3) {
     // dx and dy together: both need the regenerated edge weights
     transpose_alpha<<<1024, 256, 0, s>>>(alpha, at, l.np, c.U, Up, c.H);
-    const size_t smem = rowtile_smem(kRadDx, c.H, W2);
-    if (smem > 220 * 1024) return fail(ICTC_ERR_UNSUPPORTED, "hidden width too large (%d)", c.H);
-    if ((st = allow_smem(reinterpret_cast<const void*>(&rowtile<kRadDx>), smem)) != ICTC_OK)
-      return st;
     // scratch outputs when only one of dx / dy is requested are not allowed to
     // alias inputs; the caller passes both buffers (see the Python wrapper)
     if (!grad_left || !grad_angular)
       return fail(ICTC_ERR_INVALID, "dx and dy buffers are both required when either is");
     RowtileArgs ra{grad_output, left, radial_hidden, angular, at, bias, grad_left, grad_angular,
                    rows, c.U, Up, c.H, W1, c.H, W2, t};
-    const dim3 grid(static_cast<unsigned>(ceil_div(rows, kRT)), 1);
-    rowtile<kRadDx><<<grid, 256, smem, s>>>(ra);
+    if ((st = launch_rowtile<kRadDx>(ra, s)) != ICTC_OK) return st;
   }
+  const bool vec = (W1 % 4 == 0) && (c.U % 8 == 0) && aligned(left, 16) && aligned(grad_output, 16);
   if (needed & 4) {
-    const int W2a = (W2 + 3) & ~3;
-    const size_t smem = (static_cast<size_t>(kDhRows) * W2a + static_cast<size_t>(c.U) * kDhRows) *
-                        sizeof(float);
-    if ((st = allow_smem(reinterpret_cast<const void*>(&radial_dhidden), smem)) != ICTC_OK)
-      return st;
-    const bool avec = (c.H % 4 == 0) && aligned(alpha, 16);
-    const dim3 grid(static_cast<unsigned>(ceil_div(rows, kDhRows)), (c.H + 63) / 64);
-    radial_dhidden<<<grid, 256, smem, s>>>(left, angular, grad_output, alpha, grad_hidden, rows,
-                                           c.U, c.H, W1, W2, t, avec);
+    DhArgs da{left, angular, grad_output, alpha, grad_hidden, rows, c.U, c.H, W1, W2, t, vec,
+              (c.H % 4 == 0) && aligned(alpha, 16)};
+    const dim3 grid(static_cast<unsigned>(ceil_div(rows, kDhE)), (c.H + kDhH - 1) / kDhH);
+    radial_dhidden<<<grid, 256, 0, s>>>(da);
   }
   if (needed & 24) {
     // grad_alpha doubles as scratch when only the bias gradient is requested
     if (!grad_alpha) return fail(ICTC_ERR_INVALID, "grad_alpha is required when dbias is");
-    const size_t smem = (kRT * 128 + kRT * 32) * sizeof(float);
-    if ((st = allow_smem(reinterpret_cast<const void*>(&radial_dalpha), smem)) != ICTC_OK)
-      return st;
-    const int64_t chunk_rows = ((ceil_div(rows, chunks) + kRT - 1) / kRT) * kRT;
-    const dim3 grid(static_cast<unsigned>(l.np), ((c.U + 127) / 128) * ((c.H + 31) / 32),
+    const int64_t chunk_rows = ((ceil_div(rows, chunks) + kDaE - 1) / kDaE) * kDaE;
+    const dim3 grid(static_cast<unsigned>(l.np),
+                    ((c.U + kDaU - 1) / kDaU) * ((c.H + kDaH - 1) / kDaH),
                     static_cast<unsigned>(chunks));
     const int64_t da_numel = Wn * c.H;
     float* da = chunks > 1 ? partial : grad_alpha;
     float* db = chunks > 1 ? partial + chunks * da_numel : ((needed & 16) ? grad_bias : nullptr);
-    radial_dalpha<<<grid, 256, smem, s>>>(left, angular, grad_output, radial_hidden, da, db, rows,
-                                          chunk_rows, da_numel, Wn, c.U, c.H, W1, W2, t);
+    DaArgs aa{left, angular, grad_output, radial_hidden, da, db, rows, chunk_rows, da_numel, Wn,
+              c.U, c.H, W1, W2, t, vec, (c.H % 4 == 0) && aligned(radial_hidden, 16)};
+    radial_dalpha<<<grid, 256, 0, s>>>(aa);
     if (chunks > 1) {
       radial_sum_chunks<<<1024, 256, 0, s>>>(partial, grad_alpha, da_numel,
                                              static_cast<int>(chunks));

@@ -1,6 +1,7 @@
 // Row-tiled GEMM + O(2) coupling kernel shared by the uvu and radial products.
 //
-// A CTA owns 32 rows x 128 channels u (256 threads, 4 rows x 4 u each) and walks
+// A CTA owns RT rows x UT channels u (RT x UT = 4096: 32 x 128, or 64 x 64 for
+// products with at most 64 channels; 256 threads, 4 rows x 4 u each) and walks
 // the paths of the product.  Per path p it forms, for every (row, u),
 //   proj[r, u, b] = sum_k A[r, k, b] * Wp[k, u]                       (a GEMM)
 // where A is the second input y_j (uvu; k = v, b = component of entry j) or the
@@ -20,13 +21,23 @@
 
 #include <cstdint>
 
+#include "common.cuh"
+
 namespace ictc {
 
 enum RowMode { kUvuFwd = 0, kUvuDx = 1, kRadFwd = 2, kRadDx = 3 };
 
-constexpr int kRT = 32;   // rows per CTA
-constexpr int kUT = 128;  // u per CTA
+constexpr int kRT = 32;   // rows per CTA of the 128-channel tile
+constexpr int kUT = 128;  // widest channel tile
 constexpr int kKC = 32;   // k per weight tile
+
+// Rows per CTA for a channel tile of UT (the tile holds 4096 (row, u) outputs).
+template <int UT>
+constexpr int rows_per_tile() { return 4096 / UT; }
+
+// Odd row stride of the small per-row tiles (angular input, dy partials): lanes
+// of one warp read eight rows at a stride of 4 rows, conflict-free when odd.
+__host__ __device__ constexpr int odd_stride(int w) { return (w % 2 == 1) ? w : w + 1; }
 
 struct UvuDev {
   const int2* in1;
@@ -59,45 +70,49 @@ __device__ __forceinline__ void rt_cp_async16(void* smem, const void* gmem, bool
                : "memory");
 }
 
-// Dynamic shared memory of rowtile<MODE> for a given A width and W2.
-inline size_t rowtile_smem(int mode, int Wa, int W2) {
-  size_t f = static_cast<size_t>(Wa) * kRT + 2 * kKC * kUT;
-  if (mode >= kRadFwd) f += static_cast<size_t>(kRT) * ((W2 + 3) & ~3);
-  if (mode == kRadDx) f += static_cast<size_t>(8) * kRT * ((W2 + 3) & ~3);
+// Dynamic shared memory of rowtile<MODE, UT> for a given A width and W2.
+inline size_t rowtile_smem(int mode, int ut, int Wa, int W2) {
+  const size_t rt = static_cast<size_t>(4096 / ut);
+  size_t f = ((static_cast<size_t>(Wa) * rt + 3) & ~size_t(3)) + 2 * kKC * static_cast<size_t>(ut);
+  if (mode >= kRadFwd) f += rt * odd_stride(W2);
+  if (mode == kRadDx) f += 8 * rt * odd_stride(W2);
   return f * sizeof(float);
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(256) rowtile(RowtileArgs A) {
+template <int MODE, int UT>
+__global__ void __launch_bounds__(256, UT == 64 ? 2 : 1) rowtile(RowtileArgs A) {
   constexpr bool RADIAL = MODE >= kRadFwd;
   constexpr bool DX = MODE == kUvuDx || MODE == kRadDx;
+  constexpr int RT = rows_per_tile<UT>();
+  constexpr int NUQ = UT / 4;  // channel quads per tile
   extern __shared__ __align__(16) float sm[];
   const UvuDev& t = A.t;
-  const int W2a = (A.W2 + 3) & ~3;
-  float* atile = sm;                                       // [Wa][32]
-  float* wtile = sm + static_cast<size_t>(A.Wa) * kRT;     // [2][32 k][128 u]
-  float* angt = wtile + 2 * kKC * kUT;                     // [32 rows][W2a] (radial)
-  float* dyp = angt + kRT * W2a;                           // [8 warps][32 rows][W2a] (kRadDx)
+  const int W2a = odd_stride(A.W2);
+  float* atile = sm;                                               // [Wa][RT]
+  float* wtile = sm + ((static_cast<size_t>(A.Wa) * RT + 3) & ~size_t(3));  // [2][32 k][UT u]
+  float* angt = wtile + 2 * kKC * UT;                              // [RT rows][W2a] (radial)
+  float* dyp = angt + RT * W2a;                                    // [8 warps][RT][W2a] (kRadDx)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int uq = warp * 4 + (lane & 3);  // 0..31
-  const int rq = lane >> 2;              // 0..7
-  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRT;
-  const int ub = blockIdx.y * kUT;
+  // a warp covers 4 channel quads x 8 row quads
+  const int uq = (warp % (NUQ / 4)) * 4 + (lane & 3);
+  const int rq = (warp / (NUQ / 4)) * 8 + (lane >> 2);
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * RT;
+  const int ub = blockIdx.y * UT;
   const int u0 = ub + uq * 4;
 
-  for (int idx = threadIdx.x; idx < kRT * A.Wa; idx += blockDim.x) {
+  for (int idx = threadIdx.x; idx < RT * A.Wa; idx += blockDim.x) {
     const int c = idx % A.Wa, r = idx / A.Wa;
     const int64_t row = row0 + r;
-    atile[c * kRT + r] = row < A.rows ? __ldg(A.a_src + row * A.Wa + c) : 0.0f;
+    atile[c * RT + r] = row < A.rows ? __ldg(A.a_src + row * A.Wa + c) : 0.0f;
   }
   if (RADIAL) {
-    for (int idx = threadIdx.x; idx < kRT * A.W2; idx += blockDim.x) {
+    for (int idx = threadIdx.x; idx < RT * A.W2; idx += blockDim.x) {
       const int c = idx % A.W2, r = idx / A.W2;
       const int64_t row = row0 + r;
       angt[r * W2a + c] = row < A.rows ? __ldg(A.ang + row * A.W2 + c) : 0.0f;
     }
     if (MODE == kRadDx)
-      for (int idx = threadIdx.x; idx < 8 * kRT * W2a; idx += blockDim.x) dyp[idx] = 0.f;
+      for (int idx = threadIdx.x; idx < 8 * RT * W2a; idx += blockDim.x) dyp[idx] = 0.f;
   }
 
   const int nkc = (A.K + kKC - 1) / kKC;
@@ -106,15 +121,15 @@ __global__ void __launch_bounds__(256) rowtile(RowtileArgs A) {
   auto issue = [&](int T, int buf) {
     const int p = path_at(T / nkc);
     const int k0 = (T % nkc) * kKC;
-    float* dst = wtile + buf * (kKC * kUT);
+    float* dst = wtile + buf * (kKC * UT);
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
+    for (int s = 0; s < kKC * NUQ / 256; ++s) {
       const int q = threadIdx.x + s * 256;  // float4 index in the tile
-      const int kr = q >> 5, c4 = q & 31;
+      const int kr = q / NUQ, c4 = q % NUQ;
       const int k = k0 + kr, u = ub + c4 * 4;
       const bool valid = k < A.K && u < A.Up;
       const float* src = valid ? A.wt + (static_cast<int64_t>(p) * A.K + k) * A.Up + u : A.wt;
-      rt_cp_async16(dst + kr * kUT + c4 * 4, src, valid);
+      rt_cp_async16(dst + kr * UT + c4 * 4, src, valid);
     }
   };
 
@@ -163,16 +178,16 @@ __global__ void __launch_bounds__(256) rowtile(RowtileArgs A) {
     }
     // GEMM over this k chunk
     const int db = RADIAL ? 1 : ej.y;
-    const float* wb = wtile + (T & 1) * (kKC * kUT) + uq * 4;
+    const float* wb = wtile + (T & 1) * (kKC * UT) + uq * 4;
     const int kn = min(kKC, A.K - kc * kKC);
     auto step = [&](int kk, int nb) {
-      const float4 w4 = *reinterpret_cast<const float4*>(wb + kk * kUT);
+      const float4 w4 = *reinterpret_cast<const float4*>(wb + kk * UT);
       const int col = RADIAL ? kc * kKC + kk : ej.x + (kc * kKC + kk) * nb;
-      const float4 y0 = *reinterpret_cast<const float4*>(atile + col * kRT + rq * 4);
+      const float4 y0 = *reinterpret_cast<const float4*>(atile + col * RT + rq * 4);
       const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
       const float ya[4] = {y0.x, y0.y, y0.z, y0.w};
       if (nb == 2) {
-        const float4 y1 = *reinterpret_cast<const float4*>(atile + (col + 1) * kRT + rq * 4);
+        const float4 y1 = *reinterpret_cast<const float4*>(atile + (col + 1) * RT + rq * 4);
         const float yb[4] = {y1.x, y1.y, y1.z, y1.w};
 #pragma unroll
         for (int r = 0; r < 4; ++r)
@@ -254,7 +269,7 @@ __global__ void __launch_bounds__(256) rowtile(RowtileArgs A) {
         if ((lane & 3) == 0) {
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
-            float* d = dyp + (warp * kRT + rq * 4 + r) * W2a + ej.x;
+            float* d = dyp + (warp * RT + rq * 4 + r) * W2a + ej.x;
             d[0] += dyr[r][0];
             if (ej.y == 2) d[1] += dyr[r][1];
           }
@@ -285,15 +300,37 @@ __global__ void __launch_bounds__(256) rowtile(RowtileArgs A) {
     __syncthreads();  // buffer T & 1 is refilled at T + 2
   }
   if (MODE == kRadDx) {
-    // dy of the 32 rows: sum of the eight warps' shares in warp order
-    for (int idx = threadIdx.x; idx < kRT * A.W2; idx += blockDim.x) {
+    // dy of the tile's rows: sum of the eight warps' shares in warp order
+    for (int idx = threadIdx.x; idx < RT * A.W2; idx += blockDim.x) {
       const int r = idx / A.W2, col = idx % A.W2;
       const int64_t row = row0 + r;
       float s = 0.f;
-      for (int w = 0; w < 8; ++w) s += dyp[(w * kRT + r) * W2a + col];
+      for (int w = 0; w < 8; ++w) s += dyp[(w * RT + r) * W2a + col];
       if (row < A.rows) A.dy[row * A.W2 + col] = s;
     }
   }
+}
+
+// Launches rowtile<MODE> with the 64-channel tile when the product has at most 64
+// channels (no idle half tile), else the 128-channel tile.
+template <int MODE>
+int launch_rowtile(const RowtileArgs& ra, cudaStream_t stream) {
+  const int ut = ra.U <= 64 ? 64 : kUT;
+  const size_t smem = rowtile_smem(MODE, ut, ra.Wa, ra.W2);
+  if (smem > 220 * 1024)
+    return fail(ICTC_ERR_UNSUPPORTED, "operand rows too wide for the row tile (%zu bytes)", smem);
+  const void* fn = ut == 64 ? reinterpret_cast<const void*>(&rowtile<MODE, 64>)
+                            : reinterpret_cast<const void*>(&rowtile<MODE, kUT>);
+  const int st = allow_smem(fn, smem);
+  if (st != ICTC_OK) return st;
+  const dim3 grid(static_cast<unsigned>(ceil_div(ra.rows, 4096 / ut)),
+                  static_cast<unsigned>(ceil_div(ra.U, ut)));
+  if (ut == 64)
+    rowtile<MODE, 64><<<grid, 256, smem, stream>>>(ra);
+  else
+    rowtile<MODE, kUT><<<grid, 256, smem, stream>>>(ra);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "row tile launch");
 }
 
 }  // namespace ictc

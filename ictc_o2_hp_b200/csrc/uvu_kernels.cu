@@ -610,14 +610,9 @@ extern "C" int32_t ictc_o2_uvu_forward(const float* left, const float* right, co
     if (!aligned(workspace, 16)) return fail(ICTC_ERR_INVALID, "workspace must be 16-byte aligned");
     float* wt = static_cast<float*>(workspace);
     transpose_weights<<<1024, 256, 0, s>>>(weight, wt, l.np, c.U, Up, c.V);
-    const size_t smem = rowtile_smem(kUvuFwd, W2, W2);
-    if (smem > 220 * 1024) return fail(ICTC_ERR_UNSUPPORTED, "second input too wide (%d)", W2);
-    if ((st = allow_smem(reinterpret_cast<const void*>(&rowtile<kUvuFwd>), smem)) != ICTC_OK)
-      return st;
-    const dim3 grid(static_cast<unsigned>(ceil_div(rows, kRT)), (c.U + kUT - 1) / kUT);
     RowtileArgs ra{left, nullptr, right, nullptr, wt, nullptr, output, nullptr, rows,
                    c.U, Up, c.V, W1, W2, W2, t};
-    rowtile<kUvuFwd><<<grid, 256, smem, s>>>(ra);
+    if ((st = launch_rowtile<kUvuFwd>(ra, s)) != ICTC_OK) return st;
   }
   e = cudaGetLastError();
   return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "uvu forward launch");
@@ -680,14 +675,9 @@ extern "C" int32_t ictc_o2_uvu_backward(const float* left, const float* right, c
   float* partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + wt_bytes);
   if (needed & 1) {
     transpose_weights<<<1024, 256, 0, s>>>(weight, wt, l.np, c.U, Up, c.V);
-    const size_t smem = rowtile_smem(kUvuDx, W2, W2);
-    if (smem > 220 * 1024) return fail(ICTC_ERR_UNSUPPORTED, "second input too wide (%d)", W2);
-    if ((st = allow_smem(reinterpret_cast<const void*>(&rowtile<kUvuDx>), smem)) != ICTC_OK)
-      return st;
-    const dim3 grid(static_cast<unsigned>(ceil_div(rows, kRT)), (c.U + kUT - 1) / kUT);
     RowtileArgs ra{grad_output, nullptr, right, nullptr, wt, nullptr, grad_left, nullptr, rows,
                    c.U, Up, c.V, W1, W2, W2, t};
-    rowtile<kUvuDx><<<grid, 256, smem, s>>>(ra);
+    if ((st = launch_rowtile<kUvuDx>(ra, s)) != ICTC_OK) return st;
   }
   if (needed & 2) {
     const size_t smem = 128 * kDpStride * sizeof(float) > 4 * 64 * 32 * sizeof(float)
