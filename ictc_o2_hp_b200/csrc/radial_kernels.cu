@@ -57,9 +57,11 @@ __global__ void transpose_alpha(const float* __restrict__ a, float* __restrict__
 //
 // gw[e,p,u] = sum_{kc,a,b} c_p[kc][a][b] g_k[e,u,kc] x_i[e,u,a] y_j[e,b], the
 // gradient of the regenerated edge weight w[e,p,u], is never stored: the dhidden
-// and dalpha kernels rebuild it tile by tile from g, x and y.  One thread builds
-// eight consecutive channels of one edge; D1 and D3 (the dims of entries i and
-// k) are compile-time so the operands stay in registers.
+// and dalpha kernels rebuild it tile by tile from g, x and y.  Per edge the
+// second input is folded into the coefficients first, C[kc][a] = sum_b c y_b,
+// so gw = sum_{kc,a} C[kc][a] g[kc] x[a].  One thread builds eight consecutive
+// channels of one edge; D1 and D3 (the dims of entries i and k) are compile-time
+// so the operands stay in registers.
 
 struct GwRegs {
   float x[16], g[16], y0, y1;
@@ -97,15 +99,22 @@ __device__ __forceinline__ void gw8_load(GwRegs& r, const float* __restrict__ xr
 template <int D1, int D3>
 __device__ __forceinline__ void gw8_compute(const GwRegs& r, const float (&c)[8],
                                             float (&out)[8]) {
+  // C[kc][a] = c[kc][a][0] y0 + c[kc][a][1] y1 (coefficients at 4 kc + 2 a + b)
+  const float c00 = fmaf(c[0], r.y0, c[1] * r.y1), c01 = fmaf(c[2], r.y0, c[3] * r.y1);
+  const float c10 = fmaf(c[4], r.y0, c[5] * r.y1), c11 = fmaf(c[6], r.y0, c[7] * r.y1);
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
     const float x0 = r.x[u * D1], x1 = D1 == 2 ? r.x[u * D1 + 1] : 0.f;
     const float g0 = r.g[u * D3], g1 = D3 == 2 ? r.g[u * D3 + 1] : 0.f;
-    float t0 = c[0] * g0 * x0, t1 = c[1] * g0 * x0;
-    if (D1 == 2) { t0 = fmaf(c[2] * g0, x1, t0); t1 = fmaf(c[3] * g0, x1, t1); }
-    if (D3 == 2) { t0 = fmaf(c[4] * g1, x0, t0); t1 = fmaf(c[5] * g1, x0, t1); }
-    if (D1 == 2 && D3 == 2) { t0 = fmaf(c[6] * g1, x1, t0); t1 = fmaf(c[7] * g1, x1, t1); }
-    out[u] = fmaf(t0, r.y0, t1 * r.y1);
+    float t0 = c00 * x0, t1 = 0.f;
+    if (D1 == 2) t0 = fmaf(c01, x1, t0);
+    if (D3 == 2) {
+      t1 = c10 * x0;
+      if (D1 == 2) t1 = fmaf(c11, x1, t1);
+      out[u] = fmaf(g0, t0, g1 * t1);
+    } else {
+      out[u] = g0 * t0;
+    }
   }
 }
 
@@ -124,21 +133,40 @@ __device__ __forceinline__ void load_coef(const UvuDev& t, int p, float (&c)[8])
   for (int e = 0; e < 8; ++e) c[e] = __ldg(t.coef + 8 * p + e);
 }
 
+// 4 x 8 thread tile of a 64 x 64 CTA tile from k-major shared operands:
+// rows m0..m0+3 of A[k][64], columns n0..n0+3 and n0+32..n0+35 of B[k][64].
+template <int KS>
+__device__ __forceinline__ void mma_4x8(const float (*A)[64], const float (*B)[64], int m0,
+                                        int n0, float (&acc)[4][8]) {
+#pragma unroll
+  for (int k = 0; k < KS; ++k) {
+    const float4 a4 = *reinterpret_cast<const float4*>(&A[k][m0]);
+    const float4 b0 = *reinterpret_cast<const float4*>(&B[k][n0]);
+    const float4 b1 = *reinterpret_cast<const float4*>(&B[k][n0 + 32]);
+    const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+  }
+}
+
 // ------------------------------------------------------------ dhidden
 //
 // dh[e,h] = sum_{p,u} gw[e,p,u] alpha[p*U+u, h]: a GEMM over K = (p, u) in steps of
-// 32 channels.  CTA tile 64 edges x 64 h, thread tile 4 edges x 4 h.  Per step the
-// gw tile [32 u][64 e] is built from g, x, y and the alpha rows [32 u][64 h] are
-// copied into shared memory; both are double-buffered, with the next step's
-// operands fetched into registers before this step's GEMM.
-constexpr int kDhE = 64, kDhH = 64, kDhU = 32;
+// 16 channels.  CTA of 128 threads for a 64 edge x 64 h tile (thread tile 4 edges x
+// 8 h).  Per step the gw tile [16 u][64 e] is built from g, x, y and the alpha rows
+// [16 u][64 h] are copied into shared memory; both double-buffered, the next
+// step's operands fetched into registers before this step's GEMM.
+constexpr int kDhE = 64, kDhH = 64, kDhU = 16;
 
 struct DhArgs {
   const float* x; const float* ang; const float* g; const float* alpha; float* dh;
   int64_t rows; int U, H, W1, W2; UvuDev t; bool vec, avec;
 };
 
-__global__ void __launch_bounds__(256, 2) radial_dhidden(DhArgs A) {
+__global__ void __launch_bounds__(128, 4) radial_dhidden(DhArgs A) {
   __shared__ __align__(16) float gwt[2][kDhU][kDhE];
   __shared__ __align__(16) float at[2][kDhU][kDhH];
   const int tid = threadIdx.x;
@@ -151,16 +179,15 @@ __global__ void __launch_bounds__(256, 2) radial_dhidden(DhArgs A) {
   const float* xrow = A.x + (gvalid ? grow_i : 0) * A.W1;
   const float* gr = A.g + (gvalid ? grow_i : 0) * A.W1;
   const float* yrow = A.ang + (gvalid ? grow_i : 0) * A.W2;
-  // alpha rows: 32 x 64 floats = 512 float4, two per thread
-  // GEMM: edges e0..e0+3, h0..h0+3
-  const int e0 = (tid & 15) * 4, h0 = (tid >> 4) * 4;
+  // GEMM: edges m0..m0+3, h n0..n0+3 and n0+32..n0+35
+  const int m0 = (tid >> 3) * 4, n0 = (tid & 7) * 4;
   const int nuc = (A.U + kDhU - 1) / kDhU;
   const int nsteps = A.t.np * nuc;
-  float acc[4][4];
+  float acc[4][8];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+    for (int b = 0; b < 8; ++b) acc[a][b] = 0.f;
 
   GwRegs r;
   float4 av[2];
@@ -179,7 +206,7 @@ __global__ void __launch_bounds__(256, 2) radial_dhidden(DhArgs A) {
     });
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
-      const int q = tid + s * 256;
+      const int q = tid + s * 128;
       const int uu = q >> 4, h = hb + (q & 15) * 4;
       const int u = uc * kDhU + uu;
       const float* src = A.alpha + (static_cast<int64_t>(p) * A.U + u) * A.H + h;
@@ -200,7 +227,7 @@ __global__ void __launch_bounds__(256, 2) radial_dhidden(DhArgs A) {
     for (int i = 0; i < 8; ++i) gwt[buf][go * 8 + i][ge] = out[i];
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
-      const int q = tid + s * 256;
+      const int q = tid + s * 128;
       *reinterpret_cast<float4*>(&at[buf][q >> 4][(q & 15) * 4]) = av[s];
     }
   };
@@ -213,38 +240,31 @@ __global__ void __launch_bounds__(256, 2) radial_dhidden(DhArgs A) {
     const int buf = step & 1;
     const bool more = step + 1 < nsteps;
     if (more) fetch(step + 1);
-#pragma unroll 8
-    for (int u = 0; u < kDhU; ++u) {
-      const float4 a4 = *reinterpret_cast<const float4*>(&gwt[buf][u][e0]);
-      const float4 b4 = *reinterpret_cast<const float4*>(&at[buf][u][h0]);
-      const float av4[4] = {a4.x, a4.y, a4.z, a4.w};
-      const float bv4[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(av4[a], bv4[b], acc[a][b]);
-    }
+    mma_4x8<kDhU>(gwt[buf], at[buf], m0, n0, acc);
     if (more) stash(buf ^ 1);
     __syncthreads();
   }
 #pragma unroll
   for (int a = 0; a < 4; ++a) {
-    const int64_t e = e_base + e0 + a;
+    const int64_t e = e_base + m0 + a;
     if (e >= A.rows) continue;
 #pragma unroll
-    for (int b = 0; b < 4; ++b)
-      if (hb + h0 + b < A.H) A.dh[e * A.H + hb + h0 + b] = acc[a][b];
+    for (int b = 0; b < 8; ++b) {
+      const int h = hb + n0 + (b & 3) + (b >> 2) * 32;
+      if (h < A.H) A.dh[e * A.H + h] = acc[a][b];
+    }
   }
 }
 
 // ------------------------------------------------------------ dalpha, dbias
 //
 // dalpha[p*U+u, h] = sum_e gw[e,p,u] hidden[e,h] and dbias[p*U+u] = sum_e gw[e,p,u]:
-// per CTA one path, a 64 u x 64 h tile and one chunk of the edges (partials are
-// summed over chunks in a fixed order afterwards).  K = edges in steps of 32:
-// the gw tile [32 e][64 u] is built on chip, the hidden rows [32 e][64 h] copied,
-// both double-buffered with register prefetch of the next step.
-constexpr int kDaE = 32, kDaU = 64, kDaH = 64;
+// per CTA (128 threads) one path, a 64 u x 64 h tile (thread tile 4 u x 8 h) and
+// one chunk of the edges (partials are summed over chunks in a fixed order
+// afterwards).  K = edges in steps of 16: the gw tile [16 e][64 u] is built on
+// chip, the hidden rows [16 e][64 h] copied, both double-buffered with register
+// prefetch of the next step.
+constexpr int kDaE = 16, kDaU = 64, kDaH = 64;
 
 struct DaArgs {
   const float* x; const float* ang; const float* g; const float* hidden;
@@ -266,15 +286,15 @@ __device__ __forceinline__ void radial_dalpha_body(const DaArgs& A, float (*gwt)
   // generation: edge ge of the step, channels ub + go*8 .. +7
   const int ge = tid >> 3, go = tid & 7;
   const int u0g = ub + go * 8;
-  // GEMM: u0..u0+3 (tile-relative), h0..h0+3
-  const int u0 = (tid & 15) * 4, h0 = (tid >> 4) * 4;
+  // GEMM: u m0..m0+3 (tile-relative), h n0..n0+3 and n0+32..n0+35
+  const int m0 = (tid >> 3) * 4, n0 = (tid & 7) * 4;
   const int64_t rbeg = static_cast<int64_t>(blockIdx.z) * A.chunk_rows;
   const int64_t rend = rbeg + A.chunk_rows < A.rows ? rbeg + A.chunk_rows : A.rows;
-  float acc[4][4], bsum[8];
+  float acc[4][8], bsum[8];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+    for (int b = 0; b < 8; ++b) acc[a][b] = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) bsum[i] = 0.f;
   GwRegs r;
@@ -287,7 +307,7 @@ __device__ __forceinline__ void radial_dalpha_body(const DaArgs& A, float (*gwt)
                      ek, ej, valid, A.vec);
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
-      const int q = tid + s * 256;
+      const int q = tid + s * 128;
       const int er = q >> 4, h = hb + (q & 15) * 4;
       const int64_t ee = e0 + er;
       const float* src = A.hidden + (ee < rend ? ee : rbeg) * A.H + h;
@@ -311,7 +331,7 @@ __device__ __forceinline__ void radial_dalpha_body(const DaArgs& A, float (*gwt)
         make_float4(out[4], out[5], out[6], out[7]);
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
-      const int q = tid + s * 256;
+      const int q = tid + s * 128;
       *reinterpret_cast<float4*>(&ht[buf][q >> 4][(q & 15) * 4]) = hv[s];
     }
   };
@@ -325,31 +345,23 @@ __device__ __forceinline__ void radial_dalpha_body(const DaArgs& A, float (*gwt)
     const int buf = static_cast<int>(step & 1);
     const bool more = step + 1 < nsteps;
     if (more) fetch(rbeg + (step + 1) * kDaE);
-#pragma unroll 8
-    for (int e = 0; e < kDaE; ++e) {
-      const float4 a4 = *reinterpret_cast<const float4*>(&gwt[buf][e][u0]);
-      const float4 b4 = *reinterpret_cast<const float4*>(&ht[buf][e][h0]);
-      const float av4[4] = {a4.x, a4.y, a4.z, a4.w};
-      const float bv4[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(av4[a], bv4[b], acc[a][b]);
-    }
+    mma_4x8<kDaE>(gwt[buf], ht[buf], m0, n0, acc);
     if (more) stash(buf ^ 1);
     __syncthreads();
   }
   float* dout = A.da + static_cast<int64_t>(blockIdx.z) * A.da_numel;
 #pragma unroll
   for (int a = 0; a < 4; ++a) {
-    const int u = ub + u0 + a;
+    const int u = ub + m0 + a;
     if (u >= A.U) continue;
 #pragma unroll
-    for (int b = 0; b < 4; ++b)
-      if (hb + h0 + b < A.H) dout[(static_cast<int64_t>(p) * A.U + u) * A.H + hb + h0 + b] = acc[a][b];
+    for (int b = 0; b < 8; ++b) {
+      const int h = hb + n0 + (b & 3) + (b >> 2) * 32;
+      if (h < A.H) dout[(static_cast<int64_t>(p) * A.U + u) * A.H + h] = acc[a][b];
+    }
   }
   if (A.db != nullptr && hb == 0) {
-    // sum the per-thread bias partials over the 32 edge lanes, in lane order
+    // sum the per-thread bias partials over the 16 edge lanes, in lane order
 #pragma unroll
     for (int i = 0; i < 8; ++i) red[ge * kDaU + go * 8 + i] = bsum[i];
     __syncthreads();
@@ -362,7 +374,7 @@ __device__ __forceinline__ void radial_dalpha_body(const DaArgs& A, float (*gwt)
   }
 }
 
-__global__ void __launch_bounds__(256, 2) radial_dalpha(DaArgs A) {
+__global__ void __launch_bounds__(128, 4) radial_dalpha(DaArgs A) {
   __shared__ __align__(16) float gwt[2][kDaE][kDaU];
   __shared__ __align__(16) float ht[2][kDaE][kDaH];
   const int4 pt = A.t.paths[blockIdx.x];
@@ -398,7 +410,7 @@ int radial_validate(const RadialConfig& c) {
 
 int64_t radial_chunks(int device, int64_t rows, int P, int U, int H) {
   const int64_t tiles = static_cast<int64_t>(P) * ((U + kDaU - 1) / kDaU) * ((H + kDaH - 1) / kDaH);
-  int64_t chunks = (4 * sm_count(device) + tiles - 1) / tiles;
+  int64_t chunks = (8 * sm_count(device) + tiles - 1) / tiles;
   const int64_t max_chunks = (rows + 1023) / 1024;
   if (chunks > max_chunks) chunks = max_chunks;
   return chunks < 1 ? 1 : chunks;
@@ -558,7 +570,7 @@ extern "C" int32_t ictc_o2_radial_backward(
     DhArgs da{left, angular, grad_output, alpha, grad_hidden, rows, c.U, c.H, W1, W2, t, vec,
               (c.H % 4 == 0) && aligned(alpha, 16)};
     const dim3 grid(static_cast<unsigned>(ceil_div(rows, kDhE)), (c.H + kDhH - 1) / kDhH);
-    radial_dhidden<<<grid, 256, 0, s>>>(da);
+    radial_dhidden<<<grid, 128, 0, s>>>(da);
   }
   if (needed & 24) {
     // grad_alpha doubles as scratch when only the bias gradient is requested
@@ -572,7 +584,7 @@ extern "C" int32_t ictc_o2_radial_backward(
     float* db = chunks > 1 ? partial + chunks * da_numel : ((needed & 16) ? grad_bias : nullptr);
     DaArgs aa{left, angular, grad_output, radial_hidden, da, db, rows, chunk_rows, da_numel, Wn,
               c.U, c.H, W1, W2, t, vec, (c.H % 4 == 0) && aligned(radial_hidden, 16)};
-    radial_dalpha<<<grid, 256, 0, s>>>(aa);
+    radial_dalpha<<<grid, 128, 0, s>>>(aa);
     if (chunks > 1) {
       radial_sum_chunks<<<1024, 256, 0, s>>>(partial, grad_alpha, da_numel,
                                              static_cast<int>(chunks));
