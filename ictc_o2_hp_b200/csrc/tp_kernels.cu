@@ -445,19 +445,24 @@ __device__ __forceinline__ void issue_stage(const StageRing& ring, int s, int64_
 }
 
 // Pipeline driver: calls body(stage_base, row) for every row of this CTA's
-// blocks (row < rows), with the whole stage resident in shared memory.
+// blocks (row < rows), with the whole stage resident in shared memory.  Each
+// warp counts itself out of a stage when done with it (acquire-release atomic
+// on a per-stage counter); the warp that completes the count refills the stage
+// at once, so no warp ever blocks waiting for the others to release a stage.
 template <int NT, class Body>
 __device__ __forceinline__ void staged_loop(unsigned char* smem, unsigned char* base, int stages,
                                             int R, int64_t rows, int64_t W,
                                             const float* const* src, Body&& body) {
   const StageRing ring = stage_ring(smem, base, stages);
+  // the counters live where the stages' "empty" barriers would be
+  unsigned* done = reinterpret_cast<unsigned*>(ring.empty);
   const int nwarps = blockDim.x >> 5;
   const int r = (threadIdx.x >> 5) / (nwarps / R);
   const int64_t nblocks = (rows + R - 1) / R;
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&ring.full[s], 1);
-      mbar_init(&ring.empty[s], nwarps);
+      done[s] = 0;
     }
     fence_mbarrier_init();
   }
@@ -472,20 +477,24 @@ __device__ __forceinline__ void staged_loop(unsigned char* smem, unsigned char* 
   bool ok = true;
   for (int64_t block = blockIdx.x; block < nblocks && ok; block += gridDim.x, ++it) {
     const int s = static_cast<int>(it % stages);
-    ok = mbar_wait(&ring.full[s], static_cast<uint32_t>((it / stages) & 1), 1);
+    const uint32_t round = static_cast<uint32_t>(it / stages);
+    ok = mbar_wait(&ring.full[s], round & 1, 1);
     if (!ok) break;
     const int64_t row = block * R + r;
     if (row < rows) body(ring.buf + static_cast<int64_t>(s) * NT * R * W + r * W, row);
     __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(&ring.empty[s]);
-    if (threadIdx.x == 0 && it > 0) {
-      // refill the stage of iteration it - 1 with the block of iteration it - 1 + stages
-      const int64_t prev = it - 1;
-      const int ps = static_cast<int>(prev % stages);
-      const int64_t next = block + static_cast<int64_t>(stages - 1) * gridDim.x;
-      if (next < nblocks) {
-        ok = mbar_wait(&ring.empty[ps], static_cast<uint32_t>((prev / stages) & 1), 2);
-        if (ok) issue_stage<NT>(ring, ps, next, R, rows, W, src);
+    if ((threadIdx.x & 31) == 0) {
+      unsigned prev;
+      asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+                   : "=r"(prev)
+                   : "r"(smem_addr(&done[s]))
+                   : "memory");
+      if (prev + 1 == static_cast<unsigned>(nwarps) * (round + 1)) {
+        // every warp is done reading stage s: order those reads before the
+        // asynchronous copy that overwrites it, then refill
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        const int64_t next = block + static_cast<int64_t>(stages) * gridDim.x;
+        if (next < nblocks) issue_stage<NT>(ring, s, next, R, rows, W, src);
       }
     }
   }

@@ -57,6 +57,8 @@ def test_golden(name, cuda_device):
     (17, 2, 9, True, 70),
     (128, 1, 40, False, 33),
     (3, 0, 5, True, 11),
+    (16, 5, 12, True, 45),     # second input wider than 8 values
+    (72, 2, 64, False, 130),   # two channel tiles in the weight gradient
 ])
 def test_against_oracle(u, m_max, hidden, bias, rows, cuda_device):
     oracle_tp = O.UvuOracle(u, 1, m_max, "full", "canonical")
