@@ -1025,12 +1025,28 @@ extern "C" int32_t ictc_o2_tp_forward(const float* left, const float* right, con
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int device = 0;
   if ((st = current_device(&device)) != ICTC_OK) return st;
-  // The forward's arithmetic per byte is low enough that the direct kernel (12
-  // resident warps per SM, L1-cached loads) outruns the staged ring at every
-  // measured shape; the staged and wide variants stay selectable for experiments.
   const char* variant = getenv("ICTC_TP_FORWARD");
   const bool al16 = aligned16({left, right, output});
-  if (variant == nullptr || strcmp(variant, "grouped") == 0) {
+  // Default: the wide staged kernel (16 warps, weights and two-row stages in shared
+  // memory) from m_max = 4 up, where its rows are long enough to keep the bulk
+  // copies busy; below that, and when it does not fit, the grouped kernel.
+  // Measured over the benchmark sweep (C 32..256, m_max 1..6, both parities).
+  const bool want_wide = (variant == nullptr && m_max >= 4) ||
+                         (variant != nullptr && strcmp(variant, "wide") == 0);
+  const StagedPlan wp =
+      (want_wide && k.fwd_wide && al16)
+          ? plan_staged(device, rows, L, full, 2, weight_chunk_bytes(k, channels, full),
+                        kWideWarps, 2, true)
+          : StagedPlan{};
+  if (wp.ok) {
+    if ((st = allow_smem(reinterpret_cast<const void*>(k.fwd_wide), wp.smem)) != ICTC_OK)
+      return st;
+    k.fwd_wide<<<static_cast<unsigned>(wp.grid), wp.warps * 32, wp.smem, s>>>(
+        left, right, weight, output, rows, L, mags, wp.groups, wp.R, wp.stages);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "tp_forward launch");
+  }
+  if (variant == nullptr || strcmp(variant, "grouped") == 0 || want_wide) {
     const bool vec2 = (L.width % 2 == 0) && aligned(left, 8) && aligned(right, 8) &&
                       aligned(output, 8);
     const int groups = static_cast<int>(ceil_div(channels, full ? 16 : 32));
@@ -1051,20 +1067,9 @@ extern "C" int32_t ictc_o2_tp_forward(const float* left, const float* right, con
     e = cudaGetLastError();
     return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "tp_forward launch");
   }
-  const bool want_wide = variant && strcmp(variant, "wide") == 0;
-  const bool want_staged = variant && strcmp(variant, "staged") == 0;
-  const StagedPlan wp =
-      (want_wide && k.fwd_wide)
-          ? plan_staged(device, rows, L, full, 2, weight_chunk_bytes(k, channels, full),
-                        kWideWarps, 2, true)
-          : StagedPlan{};
+  const bool want_staged = strcmp(variant, "staged") == 0;
   const StagedPlan sp = want_staged ? plan_staged(device, rows, L, full, 2, 0) : StagedPlan{};
-  if (wp.ok && al16) {
-    if ((st = allow_smem(reinterpret_cast<const void*>(k.fwd_wide), wp.smem)) != ICTC_OK)
-      return st;
-    k.fwd_wide<<<static_cast<unsigned>(wp.grid), wp.warps * 32, wp.smem, s>>>(
-        left, right, weight, output, rows, L, mags, wp.groups, wp.R, wp.stages);
-  } else if (sp.ok && al16) {
+  if (sp.ok && al16) {
     if ((st = allow_smem(reinterpret_cast<const void*>(k.fwd_staged), sp.smem)) != ICTC_OK)
       return st;
     k.fwd_staged<<<static_cast<unsigned>(sp.grid), sp.warps * 32, sp.smem, s>>>(

@@ -234,11 +234,11 @@ def test_tuple_and_component_major_layouts(cuda_device):
     assert torch.equal(comp._to_channel_major(cm), ref)
 
 
-@pytest.mark.parametrize("variant", ["staged", "wide", "direct"])
+@pytest.mark.parametrize("variant", ["staged", "wide", "direct", "grouped"])
 def test_forward_variants_agree(variant, cuda_device, monkeypatch):
-    """The staged, wide and register-weight direct forward kernels (selectable with
-    ICTC_TP_FORWARD) give the same values as the default kernel (weights in shared
-    memory, one channel group per CTA)."""
+    """Every forward kernel selectable with ICTC_TP_FORWARD (staged ring, wide
+    staged, register-weight direct, shared-weight grouped) gives the same values
+    as the default choice."""
     from ictc_o2_hp_b200 import TensorProduct
     torch.manual_seed(7)
     for channels, m_max, parity in ((128, 6, "full"), (32, 2, "canonical"), (48, 3, "full")):
