@@ -152,6 +152,343 @@ __device__ __forceinline__ void mma_4x8(const float (*A)[64], const float (*B)[6
   }
 }
 
+// ------------------------------------------------------------ forward and dx / dy
+//
+// radial_tile<MODE, UT>: a CTA owns RT edges x UT channels and walks the paths.
+// Per path p it regenerates the edge weights of its tile,
+//   w[e,p,u] = sum_h hidden[e,h] alpha[p*U+u, h] (+ bias),
+// as a GEMM (K = H in chunks of 64; the hidden tile stays in shared memory for
+// the whole CTA, alpha_p streams through a cp.async double buffer), with 256
+// threads in 4 edge x 8 channel tiles (channels tc*4..+3 and UT/2 + tc*4..+3).
+// The coupling then folds the second input into the coefficients per edge,
+// C[kc][a] = sum_b c_p[kc][a][b] y_j[e,b], and
+//   forward:  out_k[e,u,kc] += w sum_a C[kc][a] x_i[e,u,a]   (paths grouped by k)
+//   dx mode:  dx_i[e,u,a]   += w sum_kc C[kc][a] g_k[e,u,kc]  (paths grouped by i)
+//             dy_j[e,b]     += sum_u w sum_{kc,a} c[kc][a][b] g_k x_i
+// The accumulators of the current k (or i) group stay in registers; dy is
+// reduced over the tile's channels with shuffles, then added per path in path
+// order into a shared per-edge row (deterministic).  Path metadata is copied to
+// shared memory once per CTA.
+enum RadTileMode { kRtFwd = 0, kRtDx = 1 };
+constexpr int kRtThreads = 256;
+constexpr int kRtKC = 64;  // hidden features per weight chunk
+
+struct RadTileArgs {
+  const float* opnd;    // forward: x; dx mode: g   [rows, W1]
+  const float* x;       // dx mode: x               [rows, W1]
+  const float* hidden;  // [rows, H]
+  const float* ang;     // [rows, W2]
+  const float* at;      // alpha as [P][H][Up]
+  const float* bias;    // [P * U] or null
+  float* out;           // forward output or dx     [rows, W1]
+  float* dy;            // dx mode                  [rows, W2]
+  int64_t rows;
+  int U, Up, H, W1, W2;
+  UvuDev t;
+  bool vec;  // 16-byte access to 4-channel groups of opnd / x / out
+};
+
+template <int UT>
+struct RtShape {
+  static constexpr int TC = UT / 8;           // threads along the channels
+  static constexpr int TR = kRtThreads / TC;  // thread rows
+  static constexpr int RT = TR * 4;           // edges per CTA
+};
+
+inline size_t radial_tile_smem(int ut, int H, int W2, int np, int n1, int n2, bool dx) {
+  const size_t rt = static_cast<size_t>(kRtThreads / (ut / 8)) * 4;
+  const size_t kc = static_cast<size_t>(H < kRtKC ? H : kRtKC);
+  const size_t w2s = static_cast<size_t>(odd_stride(W2));
+  const size_t floats = static_cast<size_t>(H) * rt + 2 * kc * ut + rt * w2s +
+                        static_cast<size_t>(np) * 8 + (dx ? rt * w2s : 0);
+  const size_t aligned_floats = (floats + 3) & ~size_t(3);
+  const size_t ints = static_cast<size_t>(np) * 4 + static_cast<size_t>(n1 + n2) * 2 + np;
+  return (aligned_floats + ints) * 4;
+}
+
+// Loads 4 channels x D values of one entry of one row (zeros past U or rows).
+template <int D>
+__device__ __forceinline__ void load4(float (&v)[4 * D], const float* __restrict__ src,
+                                      bool row_ok, int u, int U, bool vec) {
+  if (vec && row_ok && u + 3 < U) {
+#pragma unroll
+    for (int q = 0; q < D; ++q) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(src) + q);
+      v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4 * D; ++q) v[q] = (row_ok && u + q / D < U) ? __ldg(src + q) : 0.f;
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void store4(float* __restrict__ dst, const float (&v)[4][2],
+                                       bool row_ok, int u, int U, bool vec) {
+  if (!row_ok) return;
+  if (vec && u + 3 < U) {
+#pragma unroll
+    for (int q = 0; q < D; ++q) {
+      float4 t;
+      t.x = v[(4 * q) / D][(4 * q) % D];
+      t.y = v[(4 * q + 1) / D][(4 * q + 1) % D];
+      t.z = v[(4 * q + 2) / D][(4 * q + 2) % D];
+      t.w = v[(4 * q + 3) / D][(4 * q + 3) % D];
+      reinterpret_cast<float4*>(dst)[q] = t;
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4 * D; ++q)
+      if (u + q / D < U) dst[q] = v[q / D][q % D];
+  }
+}
+
+template <int MODE, int UT>
+__global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
+  using Sh = RtShape<UT>;
+  constexpr int RT = Sh::RT, TC = Sh::TC;
+  extern __shared__ __align__(16) float sm[];
+  const int tid = threadIdx.x;
+  const int kc = A.H < kRtKC ? A.H : kRtKC;
+  const int nkc = (A.H + kRtKC - 1) / kRtKC;
+  const int W2s = odd_stride(A.W2);
+  const int np = A.t.np;
+  float* Ht = sm;                                          // [H][RT]
+  float* Wt = Ht + static_cast<size_t>(A.H) * RT;          // [2][kc][UT]
+  float* angt = Wt + 2 * kc * UT;                          // [RT][W2s]
+  float* coef = angt + RT * W2s;                           // [np][8]
+  float* dyacc = coef + np * 8;                            // [RT][W2s] (dx mode)
+  float* fend = dyacc + (MODE == kRtDx ? RT * W2s : 0);
+  int4* paths = reinterpret_cast<int4*>(sm + ((fend - sm + 3) & ~3));
+  int2* in1 = reinterpret_cast<int2*>(paths + np);
+  int2* in2 = in1 + A.t.n1;
+  int* order = reinterpret_cast<int*>(in2 + A.t.n2);
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * RT;
+  const int ub = blockIdx.y * UT;
+
+  for (int q = tid; q < np; q += kRtThreads) {
+    paths[q] = A.t.paths[q];
+    order[q] = MODE == kRtDx ? A.t.by_i[q] : q;
+  }
+  for (int q = tid; q < np * 8; q += kRtThreads) coef[q] = __ldg(A.t.coef + q);
+  for (int q = tid; q < A.t.n1; q += kRtThreads) in1[q] = A.t.in1[q];
+  for (int q = tid; q < A.t.n2; q += kRtThreads) in2[q] = A.t.in2[q];
+  for (int idx = tid; idx < RT * A.H; idx += kRtThreads) {
+    const int r = idx / A.H, h = idx - r * A.H;
+    const int64_t row = row0 + r;
+    Ht[h * RT + r] = row < A.rows ? __ldg(A.hidden + row * A.H + h) : 0.f;
+  }
+  for (int idx = tid; idx < RT * A.W2; idx += kRtThreads) {
+    const int r = idx / A.W2, c = idx - r * A.W2;
+    const int64_t row = row0 + r;
+    angt[r * W2s + c] = row < A.rows ? __ldg(A.ang + row * A.W2 + c) : 0.f;
+  }
+  if (MODE == kRtDx)
+    for (int idx = tid; idx < RT * W2s; idx += kRtThreads) dyacc[idx] = 0.f;
+  __syncthreads();
+
+  const int tc = tid % TC, tr = tid / TC;
+  const int e0 = tr * 4;
+  const int ntiles = np * nkc;
+  auto issue = [&](int T, int buf) {
+    const int p = order[T / nkc], k0 = (T % nkc) * kRtKC;
+    float* dst = Wt + buf * kc * UT;
+    for (int q = tid; q < kc * (UT / 4); q += kRtThreads) {
+      const int kr = q / (UT / 4), c4 = q - kr * (UT / 4);
+      const int k = k0 + kr, u = ub + c4 * 4;
+      const bool valid = k < A.H && u < A.Up;
+      const float* src = valid ? A.at + (static_cast<int64_t>(p) * A.H + k) * A.Up + u : A.at;
+      rt_cp_async16(dst + kr * UT + c4 * 4, src, valid);
+    }
+  };
+
+  float acc[4][8];
+  float res[4][8][2];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 8; ++b) res[a][b][0] = res[a][b][1] = 0.f;
+
+  if (ntiles > 0) issue(0, 0);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int T = 0; T < ntiles; ++T) {
+    if (T + 1 < ntiles) issue(T + 1, (T + 1) & 1);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncthreads();
+    const int pos = T / nkc, ck = T - pos * nkc;
+    const int p = order[pos];
+    if (ck == 0) {
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 8; ++b) acc[a][b] = 0.f;
+    }
+    const int kn = A.H - ck * kRtKC < kRtKC ? A.H - ck * kRtKC : kRtKC;
+    const float* Wb = Wt + (T & 1) * kc * UT;
+    const float* Hb = Ht + static_cast<size_t>(ck) * kRtKC * RT;
+    auto kstep = [&](int k) {
+      const float4 a4 = *reinterpret_cast<const float4*>(Hb + k * RT + e0);
+      const float4 b0 = *reinterpret_cast<const float4*>(Wb + k * UT + tc * 4);
+      const float4 b1 = *reinterpret_cast<const float4*>(Wb + k * UT + UT / 2 + tc * 4);
+      const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    };
+    if (kn == kRtKC) {
+#pragma unroll 8
+      for (int k = 0; k < kRtKC; ++k) kstep(k);
+    } else {
+      for (int k = 0; k < kn; ++k) kstep(k);
+    }
+    if (ck == nkc - 1) {
+      const int4 pt = paths[p];
+      const int2 ei = in1[pt.x], ej = in2[pt.y], ek = in1[pt.z];
+      const float* c = coef + 8 * p;
+      const int key = MODE == kRtFwd ? pt.z : pt.x;
+      with_dims(ei.y, ek.y, [&]<int D1, int D3>() {
+#pragma unroll
+        for (int ee = 0; ee < 4; ++ee) {
+          const int r = e0 + ee;
+          const int64_t row = row0 + r;
+          const bool row_ok = row < A.rows;
+          const float y0 = angt[r * W2s + ej.x];
+          const float y1 = ej.y == 2 ? angt[r * W2s + ej.x + 1] : 0.f;
+          const float c00 = fmaf(c[0], y0, c[1] * y1), c01 = fmaf(c[2], y0, c[3] * y1);
+          const float c10 = fmaf(c[4], y0, c[5] * y1), c11 = fmaf(c[6], y0, c[7] * y1);
+          float dyp0 = 0.f, dyp1 = 0.f;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const int u = ub + (half ? UT / 2 : 0) + tc * 4;
+            if (MODE == kRtFwd) {
+              float xv[4 * D1];
+              load4<D1>(xv, A.opnd + row * A.W1 + ei.x + static_cast<int64_t>(u) * D1, row_ok, u,
+                        A.U, A.vec);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                float w = acc[ee][half * 4 + q];
+                if (A.bias != nullptr && u + q < A.U) w += __ldg(A.bias + p * A.U + u + q);
+                const float x0 = xv[q * D1], x1 = D1 == 2 ? xv[q * D1 + 1] : 0.f;
+                float t0 = c00 * x0;
+                if (D1 == 2) t0 = fmaf(c01, x1, t0);
+                res[ee][half * 4 + q][0] = fmaf(w, t0, res[ee][half * 4 + q][0]);
+                if (D3 == 2) {
+                  float t1 = c10 * x0;
+                  if (D1 == 2) t1 = fmaf(c11, x1, t1);
+                  res[ee][half * 4 + q][1] = fmaf(w, t1, res[ee][half * 4 + q][1]);
+                }
+              }
+            } else {
+              float gv[4 * D3], xv[4 * D1];
+              load4<D3>(gv, A.opnd + row * A.W1 + ek.x + static_cast<int64_t>(u) * D3, row_ok, u,
+                        A.U, A.vec);
+              load4<D1>(xv, A.x + row * A.W1 + ei.x + static_cast<int64_t>(u) * D1, row_ok, u,
+                        A.U, A.vec);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                float w = acc[ee][half * 4 + q];
+                if (A.bias != nullptr && u + q < A.U) w += __ldg(A.bias + p * A.U + u + q);
+                const float g0 = gv[q * D3], g1 = D3 == 2 ? gv[q * D3 + 1] : 0.f;
+                const float x0 = xv[q * D1], x1 = D1 == 2 ? xv[q * D1 + 1] : 0.f;
+                // dx[a] += w sum_kc C[kc][a] g[kc]
+                float s0 = c00 * g0;
+                if (D3 == 2) s0 = fmaf(c10, g1, s0);
+                res[ee][half * 4 + q][0] = fmaf(w, s0, res[ee][half * 4 + q][0]);
+                if (D1 == 2) {
+                  float s1 = c01 * g0;
+                  if (D3 == 2) s1 = fmaf(c11, g1, s1);
+                  res[ee][half * 4 + q][1] = fmaf(w, s1, res[ee][half * 4 + q][1]);
+                }
+                // dy[b] += w sum_{kc,a} c[kc][a][b] g[kc] x[a]  (index 4 kc + 2 a + b)
+                float d0 = c[0] * g0 * x0, d1 = c[1] * g0 * x0;
+                if (D1 == 2) { d0 = fmaf(c[2] * g0, x1, d0); d1 = fmaf(c[3] * g0, x1, d1); }
+                if (D3 == 2) { d0 = fmaf(c[4] * g1, x0, d0); d1 = fmaf(c[5] * g1, x0, d1); }
+                if (D1 == 2 && D3 == 2) {
+                  d0 = fmaf(c[6] * g1, x1, d0);
+                  d1 = fmaf(c[7] * g1, x1, d1);
+                }
+                dyp0 = fmaf(w, d0, dyp0);
+                dyp1 = fmaf(w, d1, dyp1);
+              }
+            }
+          }
+          if (MODE == kRtDx) {
+            // sum over the TC threads that share these edges (consecutive lanes)
+#pragma unroll
+            for (int m = 1; m < TC; m <<= 1) {
+              dyp0 += __shfl_xor_sync(0xffffffffu, dyp0, m);
+              dyp1 += __shfl_xor_sync(0xffffffffu, dyp1, m);
+            }
+            if (tc == 0) {
+              dyacc[r * W2s + ej.x] += dyp0;
+              if (ej.y == 2) dyacc[r * W2s + ej.x + 1] += dyp1;
+            }
+          }
+        }
+      });
+      const bool last = pos + 1 == np ||
+                        (MODE == kRtFwd ? paths[order[pos + 1]].z : paths[order[pos + 1]].x) != key;
+      if (last) {
+        const int2 eo = in1[key];
+        const int dd = eo.y;
+#pragma unroll
+        for (int ee = 0; ee < 4; ++ee) {
+          const int64_t row = row0 + e0 + ee;
+          const bool row_ok = row < A.rows;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const int u = ub + (half ? UT / 2 : 0) + tc * 4;
+            float v[4][2];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              v[q][0] = res[ee][half * 4 + q][0];
+              v[q][1] = res[ee][half * 4 + q][1];
+            }
+            float* dst = A.out + row * A.W1 + eo.x + static_cast<int64_t>(u) * dd;
+            if (dd == 2) store4<2>(dst, v, row_ok, u, A.U, A.vec);
+            else store4<1>(dst, v, row_ok, u, A.U, A.vec);
+          }
+#pragma unroll
+          for (int b = 0; b < 8; ++b) res[ee][b][0] = res[ee][b][1] = 0.f;
+        }
+      }
+    }
+    __syncthreads();  // weight buffer T & 1 is refilled at T + 2
+  }
+  if (MODE == kRtDx) {
+    for (int idx = tid; idx < RT * A.W2; idx += kRtThreads) {
+      const int r = idx / A.W2, col = idx - r * A.W2;
+      const int64_t row = row0 + r;
+      if (row < A.rows) A.dy[row * A.W2 + col] = dyacc[r * W2s + col];
+    }
+  }
+}
+
+template <int MODE>
+int launch_radial_tile(const RadTileArgs& ra, cudaStream_t s) {
+  const int ut = ra.U <= 64 ? 64 : 128;
+  const size_t smem = radial_tile_smem(ut, ra.H, ra.W2, ra.t.np, ra.t.n1, ra.t.n2, MODE == kRtDx);
+  if (smem > 225 * 1024)
+    return fail(ICTC_ERR_UNSUPPORTED, "radial tile needs %zu bytes of shared memory (hidden %d)",
+                smem, ra.H);
+  const void* fn = ut == 64 ? reinterpret_cast<const void*>(&radial_tile<MODE, 64>)
+                            : reinterpret_cast<const void*>(&radial_tile<MODE, 128>);
+  const int st = allow_smem(fn, smem);
+  if (st != ICTC_OK) return st;
+  const int rt = ut == 64 ? RtShape<64>::RT : RtShape<128>::RT;
+  const dim3 grid(static_cast<unsigned>(ceil_div(ra.rows, rt)),
+                  MODE == kRtDx ? 1u : static_cast<unsigned>(ceil_div(ra.U, ut)));
+  if (ut == 64)
+    radial_tile<MODE, 64><<<grid, kRtThreads, smem, s>>>(ra);
+  else
+    radial_tile<MODE, 128><<<grid, kRtThreads, smem, s>>>(ra);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "radial tile launch");
+}
+
 // ------------------------------------------------------------ dhidden
 //
 // dh[e,h] = sum_{p,u} gw[e,p,u] alpha[p*U+u, h]: a GEMM over K = (p, u) in steps of
@@ -501,9 +838,11 @@ extern "C" int32_t ictc_o2_radial_forward(const float* left, const float* angula
   float* at = static_cast<float*>(workspace);
   transpose_alpha<<<1024, 256, 0, s>>>(alpha, at, l.np, c.U, Up, c.H);
   const UvuDev t = radial_dev(device_table, l);
-  RowtileArgs ra{left, nullptr, radial_hidden, angular, at, bias, output, nullptr, rows,
-                 c.U, Up, c.H, th.width1, c.H, th.width2, t};
-  return launch_rowtile<kRadFwd>(ra, s);
+  const bool vec = (th.width1 % 4 == 0) && (c.U % 4 == 0) && aligned(left, 16) &&
+                   aligned(output, 16);
+  RadTileArgs ra{left, nullptr, radial_hidden, angular, at, bias, output, nullptr, rows,
+                 c.U, Up, c.H, th.width1, th.width2, t, vec};
+  return launch_radial_tile<kRtFwd>(ra, s);
 }
 
 extern "C" int32_t ictc_o2_radial_backward(
@@ -561,9 +900,11 @@ extern "C" int32_t ictc_o2_radial_backward(
     // alias inputs; the caller passes both buffers (see the Python wrapper)
     if (!grad_left || !grad_angular)
       return fail(ICTC_ERR_INVALID, "dx and dy buffers are both required when either is");
-    RowtileArgs ra{grad_output, left, radial_hidden, angular, at, bias, grad_left, grad_angular,
-                   rows, c.U, Up, c.H, W1, c.H, W2, t};
-    if ((st = launch_rowtile<kRadDx>(ra, s)) != ICTC_OK) return st;
+    const bool tvec = (W1 % 4 == 0) && (c.U % 4 == 0) && aligned(left, 16) &&
+                      aligned(grad_output, 16) && aligned(grad_left, 16);
+    RadTileArgs ra{grad_output, left, radial_hidden, angular, at, bias, grad_left, grad_angular,
+                   rows, c.U, Up, c.H, W1, W2, t, tvec};
+    if ((st = launch_radial_tile<kRtDx>(ra, s)) != ICTC_OK) return st;
   }
   const bool vec = (W1 % 4 == 0) && (c.U % 8 == 0) && aligned(left, 16) && aligned(grad_output, 16);
   if (needed & 4) {
