@@ -18,6 +18,7 @@
 
 #include "common.cuh"
 #include "rowtile.cuh"
+#include "tma.cuh"
 #include "uvu_table.cuh"
 
 namespace ictc {
@@ -171,7 +172,8 @@ __device__ __forceinline__ void mma_4x8(const float (*A)[64], const float (*B)[6
 // shared memory once per CTA.
 enum RadTileMode { kRtFwd = 0, kRtDx = 1 };
 constexpr int kRtThreads = 256;
-constexpr int kRtKC = 64;  // hidden features per weight chunk
+constexpr int kRtKC = 64;     // hidden features per weight chunk
+constexpr int kRtStages = 4;  // weight chunks in flight
 
 struct RadTileArgs {
   const float* opnd;    // forward: x; dx mode: g   [rows, W1]
@@ -199,11 +201,11 @@ inline size_t radial_tile_smem(int ut, int H, int W2, int np, int n1, int n2, bo
   const size_t rt = static_cast<size_t>(kRtThreads / (ut / 8)) * 4;
   const size_t kc = static_cast<size_t>(H < kRtKC ? H : kRtKC);
   const size_t w2s = static_cast<size_t>(odd_stride(W2));
-  const size_t floats = static_cast<size_t>(H) * rt + 2 * kc * ut + rt * w2s +
+  const size_t floats = static_cast<size_t>(H) * rt + kRtStages * kc * ut + rt * w2s +
                         static_cast<size_t>(np) * 8 + (dx ? rt * w2s : 0);
   const size_t aligned_floats = (floats + 3) & ~size_t(3);
   const size_t ints = static_cast<size_t>(np) * 4 + static_cast<size_t>(n1 + n2) * 2 + np;
-  return (aligned_floats + ints) * 4;
+  return 128 + (aligned_floats + ints) * 4;
 }
 
 // Loads 4 channels x D values of one entry of one row (zeros past U or rows).
@@ -247,15 +249,20 @@ template <int MODE, int UT>
 __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
   using Sh = RtShape<UT>;
   constexpr int RT = Sh::RT, TC = Sh::TC;
-  extern __shared__ __align__(16) float sm[];
-  const int tid = threadIdx.x;
+  extern __shared__ __align__(128) unsigned char rt_raw[];
+  // [0, 128): stage barriers (full) and release counters
+  uint64_t* full = reinterpret_cast<uint64_t*>(rt_raw);
+  unsigned* done = reinterpret_cast<unsigned*>(rt_raw + 64);
+  float* sm = reinterpret_cast<float*>(rt_raw + 128);
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int nwarps = kRtThreads / 32;
   const int kc = A.H < kRtKC ? A.H : kRtKC;
   const int nkc = (A.H + kRtKC - 1) / kRtKC;
   const int W2s = odd_stride(A.W2);
   const int np = A.t.np;
   float* Ht = sm;                                          // [H][RT]
-  float* Wt = Ht + static_cast<size_t>(A.H) * RT;          // [2][kc][UT]
-  float* angt = Wt + 2 * kc * UT;                          // [RT][W2s]
+  float* Wt = Ht + static_cast<size_t>(A.H) * RT;          // [kRtStages][kc][UT]
+  float* angt = Wt + kRtStages * kc * UT;                  // [RT][W2s]
   float* coef = angt + RT * W2s;                           // [np][8]
   float* dyacc = coef + np * 8;                            // [RT][W2s] (dx mode)
   float* fend = dyacc + (MODE == kRtDx ? RT * W2s : 0);
@@ -285,20 +292,36 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
   }
   if (MODE == kRtDx)
     for (int idx = tid; idx < RT * W2s; idx += kRtThreads) dyacc[idx] = 0.f;
+  // columns of a weight chunk past the copied channels stay zero
+  const int ucopy = A.Up - ub < UT ? A.Up - ub : UT;
+  if (ucopy < UT)
+    for (int idx = tid; idx < kRtStages * kc * UT; idx += kRtThreads) Wt[idx] = 0.f;
+  if (tid == 0) {
+    for (int st = 0; st < kRtStages; ++st) {
+      mbar_init(&full[st], 1);
+      done[st] = 0;
+    }
+    fence_mbarrier_init();
+  }
   __syncthreads();
 
   const int tc = tid % TC, tr = tid / TC;
   const int e0 = tr * 4;
   const int ntiles = np * nkc;
-  auto issue = [&](int T, int buf) {
+  // One thread copies weight chunk T (rows k0.. of alpha_p, channels ub..) into
+  // stage st with bulk asynchronous copies: one copy when the chunk's rows are
+  // contiguous (Up == UT), else one per row.
+  auto issue = [&](int T, int st) {
     const int p = order[T / nkc], k0 = (T % nkc) * kRtKC;
-    float* dst = Wt + buf * kc * UT;
-    for (int q = tid; q < kc * (UT / 4); q += kRtThreads) {
-      const int kr = q / (UT / 4), c4 = q - kr * (UT / 4);
-      const int k = k0 + kr, u = ub + c4 * 4;
-      const bool valid = k < A.H && u < A.Up;
-      const float* src = valid ? A.at + (static_cast<int64_t>(p) * A.H + k) * A.Up + u : A.at;
-      rt_cp_async16(dst + kr * UT + c4 * 4, src, valid);
+    const int kn = A.H - k0 < kRtKC ? A.H - k0 : kRtKC;
+    float* dst = Wt + st * kc * UT;
+    const float* src = A.at + (static_cast<int64_t>(p) * A.H + k0) * A.Up + ub;
+    const uint32_t row_bytes = static_cast<uint32_t>(ucopy) * 4u;
+    mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(kn) * row_bytes);
+    if (ucopy == UT && A.Up == UT) {
+      bulk_g2s(dst, src, static_cast<uint32_t>(kn) * row_bytes, &full[st]);
+    } else {
+      for (int k = 0; k < kn; ++k) bulk_g2s(dst + k * UT, src + k * A.Up, row_bytes, &full[st]);
     }
   };
 
@@ -309,13 +332,14 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
 #pragma unroll
     for (int b = 0; b < 8; ++b) res[a][b][0] = res[a][b][1] = 0.f;
 
-  if (ntiles > 0) issue(0, 0);
-  asm volatile("cp.async.commit_group;" ::: "memory");
-  for (int T = 0; T < ntiles; ++T) {
-    if (T + 1 < ntiles) issue(T + 1, (T + 1) & 1);
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_group 1;" ::: "memory");
-    __syncthreads();
+  if (tid == 0)
+    for (int T = 0; T < kRtStages && T < ntiles; ++T) issue(T, T);
+  bool ok = true;
+  for (int T = 0; T < ntiles && ok; ++T) {
+    const int st = T % kRtStages;
+    const uint32_t round = static_cast<uint32_t>(T / kRtStages);
+    ok = mbar_wait(&full[st], round & 1, 5);
+    if (!ok) break;
     const int pos = T / nkc, ck = T - pos * nkc;
     const int p = order[pos];
     if (ck == 0) {
@@ -325,7 +349,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
         for (int b = 0; b < 8; ++b) acc[a][b] = 0.f;
     }
     const int kn = A.H - ck * kRtKC < kRtKC ? A.H - ck * kRtKC : kRtKC;
-    const float* Wb = Wt + (T & 1) * kc * UT;
+    const float* Wb = Wt + st * kc * UT;
     const float* Hb = Ht + static_cast<size_t>(ck) * kRtKC * RT;
     auto kstep = [&](int k) {
       const float4 a4 = *reinterpret_cast<const float4*>(Hb + k * RT + e0);
@@ -343,6 +367,19 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
       for (int k = 0; k < kRtKC; ++k) kstep(k);
     } else {
       for (int k = 0; k < kn; ++k) kstep(k);
+    }
+    // release the stage; the last warp out refills it (no warp waits here)
+    __syncwarp();
+    if (lane == 0) {
+      unsigned prev;
+      asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+                   : "=r"(prev)
+                   : "r"(smem_addr(&done[st]))
+                   : "memory");
+      if (prev + 1 == static_cast<unsigned>(nwarps) * (round + 1)) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        if (T + kRtStages < ntiles) issue(T + kRtStages, st);
+      }
     }
     if (ck == nkc - 1) {
       const int4 pt = paths[p];
@@ -456,9 +493,13 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
         }
       }
     }
-    __syncthreads();  // weight buffer T & 1 is refilled at T + 2
+  }
+  if (!ok && tid == 0) {
+    // a wait ran out: let copies already issued land before the CTA exits
+    for (int st = 0; st < kRtStages; ++st) mbar_wait(&full[st], 0, 6);
   }
   if (MODE == kRtDx) {
+    __syncthreads();
     for (int idx = tid; idx < RT * A.W2; idx += kRtThreads) {
       const int r = idx / A.W2, col = idx - r * A.W2;
       const int64_t row = row0 + r;
