@@ -543,8 +543,8 @@ def run_gpu(args) -> dict | None:
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # dominant kernels from ncu captures, scaled to the bench launch by units
 # processed (profiles/tp_*_c128_m6_full.md give the commands and the raw figures:
-# 1,063.0 MB and 626.1 MB at 16,384 rows, x4 for the 65,536-row bench launch).
-TRAFFIC = {"tp_backward": 4.252e9, "tp_forward": 2.504e9}
+# 1,063.0 MB and 624.5 MB at 16,384 rows, x4 for the 65,536-row bench launch).
+TRAFFIC = {"tp_backward": 4.252e9, "tp_forward": 2.498e9}
 
 
 def _leaves(value):
