@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "rowtile.cuh"
+#include "tma.cuh"
 #include "uvu_table.cuh"
 
 namespace ictc {
@@ -268,6 +269,8 @@ __global__ void __launch_bounds__(256)
       if (u < U && v < V) out[static_cast<int64_t>(u) * V + v] = acc[a][b];
     }
 }
+
+#include "uvu_tile.cuh"
 
 // dst[i] = sum over chunks (fixed order) of partial[chunk][i].
 __global__ void sum_chunks(const float* __restrict__ partial, float* __restrict__ dst,
@@ -610,9 +613,15 @@ extern "C" int32_t ictc_o2_uvu_forward(const float* left, const float* right, co
     if (!aligned(workspace, 16)) return fail(ICTC_ERR_INVALID, "workspace must be 16-byte aligned");
     float* wt = static_cast<float*>(workspace);
     transpose_weights<<<1024, 256, 0, s>>>(weight, wt, l.np, c.U, Up, c.V);
-    RowtileArgs ra{left, nullptr, right, nullptr, wt, nullptr, output, nullptr, rows,
-                   c.U, Up, c.V, W1, W2, W2, t};
-    if ((st = launch_rowtile<kUvuFwd>(ra, s)) != ICTC_OK) return st;
+    const bool vec = (W1 % 4 == 0) && (c.U % 4 == 0) && aligned(left, 16) && aligned(output, 16);
+    UvuTileArgs ua{left, right, wt, output, rows, c.U, Up, c.V, W1, W2, t, vec};
+    st = launch_uvu_tile<kUtFwd>(ua, s);
+    if (st == ICTC_ERR_UNSUPPORTED) {  // second input too wide for the resident tile
+      RowtileArgs ra{left, nullptr, right, nullptr, wt, nullptr, output, nullptr, rows,
+                     c.U, Up, c.V, W1, W2, W2, t};
+      st = launch_rowtile<kUvuFwd>(ra, s);
+    }
+    if (st != ICTC_OK) return st;
   }
   e = cudaGetLastError();
   return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "uvu forward launch");
@@ -675,9 +684,16 @@ extern "C" int32_t ictc_o2_uvu_backward(const float* left, const float* right, c
   float* partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + wt_bytes);
   if (needed & 1) {
     transpose_weights<<<1024, 256, 0, s>>>(weight, wt, l.np, c.U, Up, c.V);
-    RowtileArgs ra{grad_output, nullptr, right, nullptr, wt, nullptr, grad_left, nullptr, rows,
-                   c.U, Up, c.V, W1, W2, W2, t};
-    if ((st = launch_rowtile<kUvuDx>(ra, s)) != ICTC_OK) return st;
+    const bool vec = (W1 % 4 == 0) && (c.U % 4 == 0) && aligned(grad_output, 16) &&
+                     aligned(grad_left, 16);
+    UvuTileArgs ua{grad_output, right, wt, grad_left, rows, c.U, Up, c.V, W1, W2, t, vec};
+    st = launch_uvu_tile<kUtDx>(ua, s);
+    if (st == ICTC_ERR_UNSUPPORTED) {
+      RowtileArgs ra{grad_output, nullptr, right, nullptr, wt, nullptr, grad_left, nullptr, rows,
+                     c.U, Up, c.V, W1, W2, W2, t};
+      st = launch_rowtile<kUvuDx>(ra, s);
+    }
+    if (st != ICTC_OK) return st;
   }
   if (needed & 2) {
     const size_t smem = 128 * kDpStride * sizeof(float) > 4 * 64 * 32 * sizeof(float)
