@@ -271,6 +271,7 @@ __global__ void __launch_bounds__(256)
 }
 
 #include "uvu_tile.cuh"
+#include "uvu_rowstream.cuh"
 
 // dst[i] = sum over chunks (fixed order) of partial[chunk][i].
 __global__ void sum_chunks(const float* __restrict__ partial, float* __restrict__ dst,
@@ -577,6 +578,27 @@ int rowwise_grid(int device, int64_t rows) {
   return static_cast<int>(rows < cap ? rows : cap);
 }
 
+// Streams per-row weights with uvu_rowstream<MODE>; ICTC_ERR_UNSUPPORTED when the
+// shape or alignment does not suit it (nothing launched).
+template <int MODE>
+int launch_rowstream(const RowStreamArgs& ra, int device, cudaStream_t s) {
+  if (!rowstream_fits(ra.U, ra.V, ra.W1, ra.W2, ra.t.n1) || !aligned(ra.w, 16) ||
+      (MODE == kRsBwd && (ra.needed & 4) && !aligned(ra.dw, 16)))
+    return ICTC_ERR_UNSUPPORTED;
+  const size_t smem = rowstream_smem(ra.U, ra.W2, ra.t.n1);
+  const void* fn = reinterpret_cast<const void*>(&uvu_rowstream<MODE>);
+  int st = allow_smem(fn, smem);
+  if (st != ICTC_OK) return st;
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kRsThreads, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  int64_t grid = static_cast<int64_t>(sm_count(device)) * (per_sm > 0 ? per_sm : 1);
+  if (grid > ra.rows) grid = ra.rows;
+  uvu_rowstream<MODE><<<static_cast<unsigned>(grid), kRsThreads, smem, s>>>(ra);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "uvu row stream launch");
+}
+
 }  // namespace
 
 extern "C" int32_t ictc_o2_uvu_forward(const float* left, const float* right, const float* weight,
@@ -599,6 +621,11 @@ extern "C" int32_t ictc_o2_uvu_forward(const float* left, const float* right, co
   const int W1 = th.width1, W2 = th.width2;
   const int64_t Wn = static_cast<int64_t>(l.np) * c.U * c.V;
   if (!shared) {
+    RowStreamArgs ra{left, right, weight, nullptr, output, nullptr, nullptr, rows,
+                     static_cast<int64_t>(l.np) * c.U * c.V, c.U, c.V, W1, W2, t, 0};
+    st = launch_rowstream<kRsFwd>(ra, device, s);
+    if (st == ICTC_OK) return ICTC_OK;
+    if (st != ICTC_ERR_UNSUPPORTED) return st;
     const int bd = ((c.U + 31) / 32) * 32;
     const size_t smem = (((W2 + 3) & ~3) + 4 * l.n1 * bd) * sizeof(float);
     if ((st = allow_smem(reinterpret_cast<const void*>(&uvu_fwd_rowwise), smem)) != ICTC_OK)
@@ -660,6 +687,11 @@ extern "C" int32_t ictc_o2_uvu_backward(const float* left, const float* right, c
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   const int W1 = th.width1, W2 = th.width2;
   if (!shared) {
+    RowStreamArgs ra{left, right, weight, grad_output, grad_left, grad_right, grad_weight, rows,
+                     Wn, c.U, c.V, W1, W2, t, needed};
+    st = launch_rowstream<kRsBwd>(ra, device, s);
+    if (st == ICTC_OK) return ICTC_OK;
+    if (st != ICTC_ERR_UNSUPPORTED) return st;
     const int bd = ((c.U + 31) / 32) * 32;
     const int W2a = (W2 + 3) & ~3;
     const size_t smem = (W2a + 6 * l.n1 * bd + (bd / 32) * W2a) * sizeof(float);

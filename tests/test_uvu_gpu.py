@@ -53,6 +53,9 @@ CASES = [
     (130, 40, 1, "full", 1, "full", "component", "none", True, 33),   # U > 128, V > 32
     (5, 3, 4, "full", 2, "canonical", "component", "element", True, 65),
     (1, 1, 0, "full", 0, "full", "component", "none", True, 3),
+    (16, 8, 2, "canonical", 2, "full", "component", "none", False, 21),   # streamed per row
+    (200, 16, 1, "full", 1, "full", "norm", "none", False, 5),       # two channel chunks
+    (96, 64, 2, "full", 1, "canonical", "component", "path", False, 4),  # V = 64
 ]
 
 
@@ -112,3 +115,17 @@ def test_compile_and_double_backward(cuda_device):
     want = torch.autograd.grad(dxc.sum(), (yc, wc))
     for a, b in zip(second, want):
         assert O.max_error(a.cpu().numpy(), b.numpy()) <= TOL
+
+
+def test_per_row_role_pruning(cuda_device):
+    """Per-row weights: each subset of requested gradients equals the full VJP."""
+    from ictc_o2_hp_b200 import UvuTensorProduct
+    torch.manual_seed(3)
+    tp = UvuTensorProduct(32, 8, 2, shared_weights=False).to(cuda_device)
+    x = torch.randn(11, tp.input1_dimension, device=cuda_device, requires_grad=True)
+    y = torch.randn(11, tp.input2_dimension, device=cuda_device, requires_grad=True)
+    w = torch.randn(11, tp.weight_numel, device=cuda_device, requires_grad=True)
+    full = torch.autograd.grad(tp(x, y, w).square().sum(), (x, y, w))
+    for i, t in enumerate((x, y, w)):
+        (only,) = torch.autograd.grad(tp(x, y, w).square().sum(), (t,))
+        assert torch.equal(only, full[i])
