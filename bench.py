@@ -45,6 +45,8 @@ FP32_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 METRICS = {
     "tp": "fwd+VJP rows/s, TensorProduct C128 m6 full N=65536; % HBM peak; 1–8 GPU",
     "uvu": "fwd+VJP rows/s, UvuTensorProduct C128 V32 m3 full shared weights N=131072",
+    "uvu_rowwise": "fwd+VJP rows/s, UvuTensorProduct C128 V32 m3 full per-row weights, "
+                   "16384 rows per GPU",
     "radial": "fwd+VJP edges/s, RadialUvuTensorProduct C64 m3 radial MLP 8-64-64, E=1048576",
 }
 # A100 published fwd+VJP for config 2 (benchmarks/eqx/results/complete_matrix.csv:383)
@@ -67,14 +69,16 @@ def _cpu_worker(task):
         g = np.ones_like(x)
         start = time.perf_counter()
         oracle.vjp(x, y, w, g)
-    elif workload == "uvu":
+    elif workload in ("uvu", "uvu_rowwise"):
+        shared = workload == "uvu"
         oracle = O.UvuOracle(128, 32, 3)
         x = rng.standard_normal((rows, oracle.width1), dtype=np.float32)
         y = rng.standard_normal((rows, oracle.width2), dtype=np.float32)
-        w = (rng.standard_normal(oracle.weight_numel) / np.sqrt(32)).astype(np.float32)
+        wshape = (oracle.weight_numel,) if shared else (rows, oracle.weight_numel)
+        w = (rng.standard_normal(wshape) / np.sqrt(32)).astype(np.float32)
         g = np.ones_like(x)
         start = time.perf_counter()
-        oracle.vjp(x, y, w, g, shared=True)
+        oracle.vjp(x, y, w, g, shared=shared)
     else:
         uvu = O.UvuOracle(64, 1, 3, "full", "canonical")
         radial = O.RadialOracle(uvu)
@@ -111,7 +115,7 @@ def cpu_units_per_second(workload: str, rows_per_worker: int, steps: int, warmup
                       f"{steps} steps"}
 
 
-CPU_ROWS = {"tp": 1024, "uvu": 16, "radial": 256}
+CPU_ROWS = {"tp": 1024, "uvu": 16, "uvu_rowwise": 4, "radial": 256}
 
 
 # ------------------------------------------------------------------ clocks
@@ -179,7 +183,15 @@ def peaks() -> tuple[dict, str]:
 
 # ------------------------------------------------------------------ workloads
 
-class TpWorkload:
+class Workload:
+    """Common parts of the bench workloads."""
+
+    def e2e_outputs(self, results):
+        """Results read back to the host in the end-to-end figure (all of them)."""
+        return _leaves(results)
+
+
+class TpWorkload(Workload):
     """Config 2: TensorProduct(128, 6, 'full') fwd + VJP, 65,536 rows per GPU."""
 
     name, scaling, unit = "tp", "weak", "rows/s"
@@ -234,7 +246,7 @@ class TpWorkload:
         return 32 * self.W * self.rows
 
 
-class UvuWorkload:
+class UvuWorkload(Workload):
     """Config 4 (shared weights): UvuTensorProduct(128, 32, 3) fwd + VJP."""
 
     name, scaling, unit = "uvu", "weak", "rows/s"
@@ -292,7 +304,71 @@ class UvuWorkload:
         return (3 * self.tp.input1_dimension + self.tp.input2_dimension) * 4 * self.rows * 2
 
 
-class RadialWorkload:
+class UvuRowWorkload(UvuWorkload):
+    """Config 4 (per-row weights): UvuTensorProduct(128, 32, 3), an (N, weight_numel)
+    weight tensor ~ N(0,1)/sqrt(32); 16,384 rows per GPU (the full N = 131,072 needs
+    318 GB of weights: it runs 8-way sharded, 16,384 rows per GPU)."""
+
+    name, scaling, unit = "uvu_rowwise", "weak", "rows/s"
+
+    def __init__(self, args, device, rank, world):
+        import torch
+        from ictc_o2_hp_b200 import UvuTensorProduct, ops
+        self.ops, self.torch, self.world = ops, torch, world
+        self.rows = args.rows or 16384
+        self.tp = UvuTensorProduct(128, 32, 3, shared_weights=False).to(device)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(4000 + rank)
+        self.x = torch.randn(self.rows, self.tp.input1_dimension, device=device, generator=gen)
+        self.y = torch.randn(self.rows, self.tp.input2_dimension, device=device, generator=gen)
+        self.w = torch.randn(self.rows, self.tp.weight_numel, device=device,
+                             generator=gen) / 32 ** 0.5
+        self.g = torch.ones(self.rows, self.tp.input1_dimension, device=device)
+        self.units = self.rows
+        self.launches = 2
+
+    def step(self, x=None, y=None, g=None):
+        torch = self.torch
+        x = (self.x if x is None else x).detach().requires_grad_(True)
+        y = (self.y if y is None else y).detach().requires_grad_(True)
+        w = self.w.detach().requires_grad_(True)
+        out = self.tp(x, y, w)
+        dx, dy, dw = torch.autograd.grad(out, (x, y, w), self.g if g is None else g)
+        return out, dx, dy, dw
+
+    def kernels(self, time_op):
+        ops, tp = self.ops, self.tp
+        fwd = time_op(lambda: ops.uvu_forward(self.x, self.y, self.w, tp._table, tp._config,
+                                              False))
+        bwd = time_op(lambda: ops.uvu_backward(self.x, self.y, self.w, self.g, tp._table,
+                                               tp._config, False, 7))
+        wbytes = 4 * self.tp.weight_numel * self.rows
+        act = 4 * (self.tp.input1_dimension + self.tp.input2_dimension) * self.rows
+        # forward: read w, x, y, write out; VJP: read w, x, y, g, write dw, dx, dy
+        return {"uvu_forward": (fwd, wbytes + act + 4 * self.tp.input1_dimension * self.rows),
+                "uvu_backward": (bwd, 2 * wbytes + 2 * act + 4 * self.tp.input1_dimension
+                                 * self.rows)}, "hbm"
+
+    def host_inputs(self):
+        return (self.x, self.y, self.g)
+
+    def e2e_outputs(self, results):
+        # out, dx and dy; dw (2.4 MB per row, like the weights) stays on the device
+        return results[:3]
+
+    def config(self):
+        return {"workload": f"UvuTensorProduct(128, 32, 3, parity='full') per-row weights, "
+                            f"forward + VJP (dx, dy, dw), {self.rows} rows per GPU",
+                "rows_per_gpu": self.rows, "weight_numel": self.tp.weight_numel,
+                "l2": "inputs larger than L2 (weights 2.4 MB per row)",
+                "parallelism": f"row shards on {self.world} GPU(s), no collective (per-row "
+                               "weights)"}
+
+    def step_bytes(self):
+        return 3 * 4 * self.tp.weight_numel * self.rows
+
+
+class RadialWorkload(Workload):
     """Config 5: 1,048,576 edges over 65,536 nodes, sharded over the ranks."""
 
     name, scaling, unit = "radial", "strong", "edges/s"
@@ -386,7 +462,8 @@ class RadialWorkload:
         return (3 * 896 + 2 * 7 + 64 * 2) * 4 * self.edges
 
 
-WORKLOADS = {"tp": TpWorkload, "uvu": UvuWorkload, "radial": RadialWorkload}
+WORKLOADS = {"tp": TpWorkload, "uvu": UvuWorkload, "uvu_rowwise": UvuRowWorkload,
+             "radial": RadialWorkload}
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -463,13 +540,13 @@ def run_gpu(args) -> dict | None:
             h.copy_(d)
         staged = [torch.empty_like(d) for d in dev_in]
         results = wl.step()
-        flat_results = [t for t in _leaves(results)]
+        flat_results = list(wl.e2e_outputs(results))
         host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in flat_results]
 
         def e2e_step():
             for s, h in zip(staged, host_in):
                 s.copy_(h, non_blocking=True)
-            res = list(_leaves(wl.step(*staged)))
+            res = list(wl.e2e_outputs(wl.step(*staged)))
             for h, t in zip(host_out, res):
                 h.copy_(t.detach(), non_blocking=True)
 
