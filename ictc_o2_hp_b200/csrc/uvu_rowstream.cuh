@@ -49,6 +49,7 @@ __host__ __device__ inline int rowstream_chunk_u(int U, int V) {
 
 inline bool rowstream_fits(int U, int V, int W1, int W2, int n1) {
   (void)W1;
+  // float4 runs of y_j: V a multiple of 8 keeps every entry offset 16-byte aligned
   if (V % 8 != 0 || V > kRsChunk) return false;
   const size_t smem = 128 + (static_cast<size_t>(kRsStages) * kRsChunk + ((W2 + 3) & ~3) +
                              6 * static_cast<size_t>(n1) * U + 2 * 128 +
@@ -63,7 +64,7 @@ inline size_t rowstream_smem(int U, int W2, int n1) {
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kRsThreads, 1) uvu_rowstream(RowStreamArgs A) {
+__global__ void __launch_bounds__(kRsThreads, 2) uvu_rowstream(RowStreamArgs A) {
   extern __shared__ __align__(128) unsigned char rs_raw[];
   uint64_t* full = reinterpret_cast<uint64_t*>(rs_raw);
   unsigned* done = reinterpret_cast<unsigned*>(rs_raw + 64);
@@ -144,81 +145,111 @@ __global__ void __launch_bounds__(kRsThreads, 1) uvu_rowstream(RowStreamArgs A) 
       const int uw = warp * 16 + ul;        // channel within the chunk
       const bool act = uw < ncu;
       const int u = u0 + uw;
-      // proj[b] over this thread's half of v, rotated float4 order
-      float p0 = 0.f, p1 = 0.f;
-      if (act) {
-        for (int s2 = 0; s2 < nv4; s2 += 2) {
-          const int f = (s2 + half + 2 * ul) % nv4;
-          const float4 w4 = *reinterpret_cast<const float4*>(wc + uw * A.V + f * 4);
-          const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int v = f * 4 + k;
-            p0 = fmaf(wv[k], ys[ej.x + v * ej.y], p0);
-            if (ej.y == 2) p1 = fmaf(wv[k], ys[ej.x + v * 2 + 1], p1);
+      // y_j as float4 runs: entry offsets are multiples of V (a multiple of 8)
+      auto body = [&]<int D2>() {
+        const float* yj = ys + ej.x;
+        // proj[b] over this thread's half of v, rotated float4 order, two chains
+        float pa0 = 0.f, pa1 = 0.f, pb0 = 0.f, pb1 = 0.f;
+        if (act) {
+          int f = half + 2 * ul;
+          f = f % nv4;
+          for (int s2 = 0; s2 < nv4; s2 += 2) {
+            const float4 w4 = *reinterpret_cast<const float4*>(wc + uw * A.V + f * 4);
+            if (D2 == 2) {
+              const float4 y0 = *reinterpret_cast<const float4*>(yj + f * 8);
+              const float4 y1 = *reinterpret_cast<const float4*>(yj + f * 8 + 4);
+              pa0 = fmaf(w4.x, y0.x, pa0); pa1 = fmaf(w4.x, y0.y, pa1);
+              pb0 = fmaf(w4.y, y0.z, pb0); pb1 = fmaf(w4.y, y0.w, pb1);
+              pa0 = fmaf(w4.z, y1.x, pa0); pa1 = fmaf(w4.z, y1.y, pa1);
+              pb0 = fmaf(w4.w, y1.z, pb0); pb1 = fmaf(w4.w, y1.w, pb1);
+            } else {
+              const float4 y0 = *reinterpret_cast<const float4*>(yj + f * 4);
+              pa0 = fmaf(w4.x, y0.x, pa0); pb0 = fmaf(w4.y, y0.y, pb0);
+              pa0 = fmaf(w4.z, y0.z, pa0); pb0 = fmaf(w4.w, y0.w, pb0);
+            }
+            f += 2;
+            if (f >= nv4) f -= nv4;
           }
         }
-      }
-      p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
-      p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
-      float s0 = 0.f, s1 = 0.f;
-      if (act) {
-        const float c0 = __ldg(cf), c1 = __ldg(cf + 1), c2 = __ldg(cf + 2), c3 = __ldg(cf + 3);
-        const float c4 = __ldg(cf + 4), c5 = __ldg(cf + 5), c6 = __ldg(cf + 6), c7 = __ldg(cf + 7);
-        const float x0 = xs[(2 * pt.x) * A.U + u], x1 = xs[(2 * pt.x + 1) * A.U + u];
-        if (MODE == kRsFwd) {
+        float p0 = pa0 + pb0, p1 = pa1 + pb1;
+        p0 += __shfl_xor_sync(0xffffffffu, p0, 1);
+        p1 += __shfl_xor_sync(0xffffffffu, p1, 1);
+        float s0 = 0.f, s1 = 0.f;
+        if (act) {
+          const float c0 = __ldg(cf), c1 = __ldg(cf + 1), c2 = __ldg(cf + 2), c3 = __ldg(cf + 3);
+          const float c4 = __ldg(cf + 4), c5 = __ldg(cf + 5), c6 = __ldg(cf + 6), c7 = __ldg(cf + 7);
+          const float x0 = xs[(2 * pt.x) * A.U + u], x1 = xs[(2 * pt.x + 1) * A.U + u];
+          if (MODE == kRsFwd) {
+            if (half == 0) {
+              os[(2 * pt.z) * A.U + u] += x0 * fmaf(c1, p1, c0 * p0) + x1 * fmaf(c3, p1, c2 * p0);
+              os[(2 * pt.z + 1) * A.U + u] +=
+                  x0 * fmaf(c5, p1, c4 * p0) + x1 * fmaf(c7, p1, c6 * p0);
+            }
+          } else {
+            const float g0 = gs[(2 * pt.z) * A.U + u], g1 = gs[(2 * pt.z + 1) * A.U + u];
+            if (want_dx && half == 0) {
+              os[(2 * pt.x) * A.U + u] += g0 * fmaf(c1, p1, c0 * p0) + g1 * fmaf(c5, p1, c4 * p0);
+              os[(2 * pt.x + 1) * A.U + u] +=
+                  g0 * fmaf(c3, p1, c2 * p0) + g1 * fmaf(c7, p1, c6 * p0);
+            }
+            // s[b] = sum_{kc,a} c[4 kc + 2 a + b] g[kc] x[a]
+            s0 = g0 * fmaf(c2, x1, c0 * x0) + g1 * fmaf(c6, x1, c4 * x0);
+            s1 = g0 * fmaf(c3, x1, c1 * x0) + g1 * fmaf(c7, x1, c5 * x0);
+          }
+        }
+        if (MODE == kRsBwd && (want_dw || want_dy)) {
+          float* swarp = sb + warp * 32;  // [16 channels][2] of this warp
           if (half == 0) {
-            os[(2 * pt.z) * A.U + u] += x0 * fmaf(c1, p1, c0 * p0) + x1 * fmaf(c3, p1, c2 * p0);
-            os[(2 * pt.z + 1) * A.U + u] += x0 * fmaf(c5, p1, c4 * p0) + x1 * fmaf(c7, p1, c6 * p0);
+            swarp[2 * ul] = s0;
+            swarp[2 * ul + 1] = s1;
           }
-        } else {
-          const float g0 = gs[(2 * pt.z) * A.U + u], g1 = gs[(2 * pt.z + 1) * A.U + u];
-          if (want_dx && half == 0) {
-            os[(2 * pt.x) * A.U + u] += g0 * fmaf(c1, p1, c0 * p0) + g1 * fmaf(c5, p1, c4 * p0);
-            os[(2 * pt.x + 1) * A.U + u] += g0 * fmaf(c3, p1, c2 * p0) + g1 * fmaf(c7, p1, c6 * p0);
-          }
-          // s[b] = sum_{kc,a} c[4 kc + 2 a + b] g[kc] x[a]
-          s0 = g0 * fmaf(c2, x1, c0 * x0) + g1 * fmaf(c6, x1, c4 * x0);
-          s1 = g0 * fmaf(c3, x1, c1 * x0) + g1 * fmaf(c7, x1, c5 * x0);
-        }
-      }
-      if (MODE == kRsBwd && (want_dw || want_dy)) {
-        float* swarp = sb + warp * 32;  // [16 channels][2] of this warp
-        if (half == 0) {
-          swarp[2 * ul] = s0;
-          swarp[2 * ul + 1] = s1;
-        }
-        __syncwarp();
-        const int nu = ncu - warp * 16 < 16 ? ncu - warp * 16 : 16;
-        if (want_dw && nu > 0) {
-          float* dst = A.dw + row * A.Wn + (static_cast<int64_t>(p) * A.U + u0 + warp * 16) * A.V;
-          for (int q = lane; q < nu * nv4; q += 32) {
-            const int uu = q / nv4, f = q - uu * nv4;
-            const float a0 = swarp[2 * uu], a1 = swarp[2 * uu + 1];
-            float o[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int v = f * 4 + k;
-              o[k] = a0 * ys[ej.x + v * ej.y];
-              if (ej.y == 2) o[k] = fmaf(a1, ys[ej.x + v * 2 + 1], o[k]);
+          __syncwarp();
+          const int nu = ncu - warp * 16 < 16 ? ncu - warp * 16 : 16;
+          if (want_dw && nu > 0) {
+            float* dst = A.dw + row * A.Wn + (static_cast<int64_t>(p) * A.U + u0 + warp * 16) * A.V;
+            for (int q = lane; q < nu * nv4; q += 32) {
+              const int uu = q / nv4, fq = q - uu * nv4;
+              const float a0 = swarp[2 * uu], a1 = swarp[2 * uu + 1];
+              float4 o;
+              if (D2 == 2) {
+                const float4 y0 = *reinterpret_cast<const float4*>(yj + fq * 8);
+                const float4 y1 = *reinterpret_cast<const float4*>(yj + fq * 8 + 4);
+                o.x = fmaf(a1, y0.y, a0 * y0.x);
+                o.y = fmaf(a1, y0.w, a0 * y0.z);
+                o.z = fmaf(a1, y1.y, a0 * y1.x);
+                o.w = fmaf(a1, y1.w, a0 * y1.z);
+              } else {
+                const float4 y0 = *reinterpret_cast<const float4*>(yj + fq * 4);
+                o = make_float4(a0 * y0.x, a0 * y0.y, a0 * y0.z, a0 * y0.w);
+              }
+              reinterpret_cast<float4*>(dst + uu * A.V)[fq] = o;
             }
-            reinterpret_cast<float4*>(dst + uu * A.V)[f] = make_float4(o[0], o[1], o[2], o[3]);
           }
-        }
-        if (want_dy && nu > 0) {
-          for (int v = lane; v < A.V; v += 32) {
-            float d0 = 0.f, d1 = 0.f;
-            for (int uu = 0; uu < nu; ++uu) {
-              const float wv = wc[(warp * 16 + uu) * A.V + v];
-              d0 = fmaf(wv, swarp[2 * uu], d0);
-              d1 = fmaf(wv, swarp[2 * uu + 1], d1);
+          if (want_dy && nu > 0) {
+            for (int v = lane; v < A.V; v += 32) {
+              float d0a = 0.f, d1a = 0.f, d0b = 0.f, d1b = 0.f;
+              const float* wcol = wc + (warp * 16) * A.V + v;
+              int uu = 0;
+              for (; uu + 1 < nu; uu += 2) {
+                const float w0 = wcol[uu * A.V], w1 = wcol[(uu + 1) * A.V];
+                d0a = fmaf(w0, swarp[2 * uu], d0a);
+                d1a = fmaf(w0, swarp[2 * uu + 1], d1a);
+                d0b = fmaf(w1, swarp[2 * uu + 2], d0b);
+                d1b = fmaf(w1, swarp[2 * uu + 3], d1b);
+              }
+              if (uu < nu) {
+                const float w0 = wcol[uu * A.V];
+                d0a = fmaf(w0, swarp[2 * uu], d0a);
+                d1a = fmaf(w0, swarp[2 * uu + 1], d1a);
+              }
+              yp[warp * W2a + ej.x + v * D2] += d0a + d0b;
+              if (D2 == 2) yp[warp * W2a + ej.x + v * 2 + 1] += d1a + d1b;
             }
-            yp[warp * W2a + ej.x + v * ej.y] += d0;
-            if (ej.y == 2) yp[warp * W2a + ej.x + v * 2 + 1] += d1;
           }
+          __syncwarp();
         }
-        __syncwarp();
-      }
+      };
+      if (ej.y == 2) body.template operator()<2>(); else body.template operator()<1>();
       // release the stage; the last warp out refills it
       __syncwarp();
       if (lane == 0) {
