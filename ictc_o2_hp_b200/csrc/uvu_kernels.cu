@@ -272,6 +272,7 @@ __global__ void __launch_bounds__(256)
 
 #include "uvu_tile.cuh"
 #include "uvu_rowstream.cuh"
+#include "uvu_dy.cuh"
 
 // dst[i] = sum over chunks (fixed order) of partial[chunk][i].
 __global__ void sum_chunks(const float* __restrict__ partial, float* __restrict__ dst,
@@ -727,7 +728,14 @@ extern "C" int32_t ictc_o2_uvu_backward(const float* left, const float* right, c
     }
     if (st != ICTC_OK) return st;
   }
-  if (needed & 2) {
+  if ((needed & 2) && uvu_dy_stage_fits(c.U, c.V, W1, aligned(left, 16) &&
+                                                     aligned(grad_output, 16) &&
+                                                     aligned(weight, 16))) {
+    const void* fn = reinterpret_cast<const void*>(&uvu_dy_stage);
+    if ((st = allow_smem(fn, sizeof(DySmem))) != ICTC_OK) return st;
+    DyArgs da{left, grad_output, weight, grad_right, rows, c.U, c.V, W1, W2, t};
+    uvu_dy_stage<<<static_cast<unsigned>(ceil_div(rows, kDyRows)), 256, sizeof(DySmem), s>>>(da);
+  } else if (needed & 2) {
     const size_t smem = 128 * kDpStride * sizeof(float) > 4 * 64 * 32 * sizeof(float)
                             ? 128 * kDpStride * sizeof(float)
                             : 4 * 64 * 32 * sizeof(float);
