@@ -1,0 +1,140 @@
+// Shared-weight uvu dw: uvu_dw_stage.
+//
+//   dw_p[u,v] = sum_r sum_b s_p[r,u,b] y_j[r,v,b],
+//   s_p[r,u,b] = sum_{kc,a} c_p[kc][a][b] g_k[r,u,kc] x_i[r,u,a]
+//
+// A CTA (256 threads) owns one path and one chunk of rows.  It walks the rows in
+// steps of 32: the slices x_i, g_k [32 rows][U d] and y_j [32 rows][V d2] arrive
+// by cp.async one step ahead (double buffer); s is built from shared memory into
+// S[(row, b)][u] and y into Y[(row, b)][v]; then the GEMM over K = (row, b)
+// accumulates dw_p (4 u x 4 v per thread).  Chunks are summed in a fixed order
+// afterwards.  Needs U <= 128, V <= 32 and 16-byte aligned rows.
+//
+// This header is included inside the anonymous namespace of uvu_kernels.cu.
+#pragma once
+
+constexpr int kDwRows = 32;
+constexpr int kDwU = 128;
+constexpr int kDwV = 32;
+constexpr int kDwLdS = kDwU + 4;  // S row stride (floats)
+constexpr int kDwLdY = kDwV + 4;  // Y row stride (floats)
+
+struct DwArgs {
+  const float* x; const float* y; const float* g; float* dst;  // dst: [chunks][Wn]
+  int64_t rows, chunk_rows, Wn;
+  int U, V, W1, W2;
+  UvuDev t;
+};
+
+struct DwSmem {
+  float xs[2][kDwRows][kDwU * 2];
+  float gs[2][kDwRows][kDwU * 2];
+  float ys[2][kDwRows][kDwV * 2];
+  float S[2 * kDwRows][kDwLdS];
+  float Y[2 * kDwRows][kDwLdY];
+};
+
+inline bool uvu_dw_stage_fits(int U, int V, int W1, int W2, bool aligned_rows) {
+  return U <= kDwU && V <= kDwV && U % 4 == 0 && V % 4 == 0 && W1 % 4 == 0 && W2 % 4 == 0 &&
+         aligned_rows;
+}
+
+__global__ void __launch_bounds__(256, 1) uvu_dw_stage(DwArgs A) {
+  extern __shared__ __align__(16) unsigned char dw_raw[];
+  DwSmem& S = *reinterpret_cast<DwSmem*>(dw_raw);
+  const int tid = threadIdx.x;
+  const int p = blockIdx.x;
+  const int4 pt = A.t.paths[p];
+  const int2 ei = A.t.in1[pt.x], ej = A.t.in2[pt.y], ek = A.t.in1[pt.z];
+  float c[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) c[e] = __ldg(A.t.coef + 8 * p + e);
+  const int64_t rbeg = static_cast<int64_t>(blockIdx.y) * A.chunk_rows;
+  const int64_t rend = rbeg + A.chunk_rows < A.rows ? rbeg + A.chunk_rows : A.rows;
+  const int64_t nsteps = rend > rbeg ? (rend - rbeg + kDwRows - 1) / kDwRows : 0;
+  const int nx = A.U * ei.y / 4, ng = A.U * ek.y / 4, ny = A.V * ej.y / 4;  // float4 per row
+  auto issue = [&](int64_t step, int buf) {
+    if (step < nsteps) {
+      const int64_t r0 = rbeg + step * kDwRows;
+      const int nv = rend - r0 < kDwRows ? static_cast<int>(rend - r0) : kDwRows;
+      for (int q = tid; q < kDwRows * nx; q += 256) {
+        const int r = q / nx, cc = q - r * nx;
+        const bool ok = r < nv;
+        dy_cp16(&S.xs[buf][r][cc * 4], ok ? A.x + (r0 + r) * A.W1 + ei.x + cc * 4 : A.x, ok);
+      }
+      for (int q = tid; q < kDwRows * ng; q += 256) {
+        const int r = q / ng, cc = q - r * ng;
+        const bool ok = r < nv;
+        dy_cp16(&S.gs[buf][r][cc * 4], ok ? A.g + (r0 + r) * A.W1 + ek.x + cc * 4 : A.g, ok);
+      }
+      for (int q = tid; q < kDwRows * ny; q += 256) {
+        const int r = q / ny, cc = q - r * ny;
+        const bool ok = r < nv;
+        dy_cp16(&S.ys[buf][r][cc * 4], ok ? A.y + (r0 + r) * A.W2 + ej.x + cc * 4 : A.y, ok);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  for (int q = tid; q < 2 * kDwRows * kDwU * 2; q += 256) {
+    (&S.xs[0][0][0])[q] = 0.f;
+    (&S.gs[0][0][0])[q] = 0.f;
+  }
+  for (int q = tid; q < 2 * kDwRows * kDwV * 2; q += 256) (&S.ys[0][0][0])[q] = 0.f;
+  __syncthreads();
+  issue(0, 0);
+  // generation: channel gu, rows gh*16 .. +15; y: (row, b) gr, v quad gv
+  const int gu = tid & 127, gh = tid >> 7;
+  // GEMM: u quad uq (0..31), v quad vq (0..7)
+  const int uq = tid >> 3, vq = tid & 7;
+  float acc[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+  for (int64_t step = 0; step < nsteps; ++step) {
+    const int buf = static_cast<int>(step & 1);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // slices of step visible; previous GEMM done with S and Y
+    issue(step + 1, buf ^ 1);
+#pragma unroll 4
+    for (int rr = 0; rr < 16; ++rr) {
+      const int r = gh * 16 + rr;
+      const float* xr = &S.xs[buf][r][gu * ei.y];
+      const float* gr = &S.gs[buf][r][gu * ek.y];
+      const float x0 = xr[0], x1 = ei.y == 2 ? xr[1] : 0.f;
+      const float g0 = gr[0], g1 = ek.y == 2 ? gr[1] : 0.f;
+      S.S[2 * r][gu] = g0 * fmaf(c[2], x1, c[0] * x0) + g1 * fmaf(c[6], x1, c[4] * x0);
+      S.S[2 * r + 1][gu] = g0 * fmaf(c[3], x1, c[1] * x0) + g1 * fmaf(c[7], x1, c[5] * x0);
+    }
+    // Y[(r, b)][v] = y_j[r, v, b] (zero for b >= d2)
+    for (int q = tid; q < 2 * kDwRows * kDwV; q += 256) {
+      const int rb = q / kDwV, v = q - rb * kDwV;
+      const int r = rb >> 1, b = rb & 1;
+      S.Y[rb][v] = (b < ej.y && v < A.V) ? S.ys[buf][r][v * ej.y + b] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < 2 * kDwRows; ++k) {
+      const float4 a4 = *reinterpret_cast<const float4*>(&S.S[k][uq * 4]);
+      const float4 b4 = *reinterpret_cast<const float4*>(&S.Y[k][vq * 4]);
+      const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+      const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  float* out = A.dst + static_cast<int64_t>(blockIdx.y) * A.Wn + static_cast<int64_t>(p) * A.U * A.V;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int u = uq * 4 + i;
+    if (u >= A.U) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int v = vq * 4 + j;
+      if (v < A.V) out[static_cast<int64_t>(u) * A.V + v] = acc[i][j];
+    }
+  }
+}

@@ -273,6 +273,7 @@ __global__ void __launch_bounds__(256)
 #include "uvu_tile.cuh"
 #include "uvu_rowstream.cuh"
 #include "uvu_dy.cuh"
+#include "uvu_dw.cuh"
 
 // dst[i] = sum over chunks (fixed order) of partial[chunk][i].
 __global__ void sum_chunks(const float* __restrict__ partial, float* __restrict__ dst,
@@ -745,7 +746,18 @@ extern "C" int32_t ictc_o2_uvu_backward(const float* left, const float* right, c
     uvu_dy_tile<<<grid, 256, smem, s>>>(left, grad_output, weight, grad_right, rows, c.U, c.V, W1,
                                         W2, t, wvec);
   }
-  if (needed & 4) {
+  if ((needed & 4) && uvu_dw_stage_fits(c.U, c.V, W1, W2, aligned(left, 16) &&
+                                                             aligned(right, 16) &&
+                                                             aligned(grad_output, 16))) {
+    const void* fn = reinterpret_cast<const void*>(&uvu_dw_stage);
+    if ((st = allow_smem(fn, sizeof(DwSmem))) != ICTC_OK) return st;
+    const int64_t chunk_rows = ((ceil_div(rows, chunks) + kDwRows - 1) / kDwRows) * kDwRows;
+    float* dst = chunks > 1 ? partial : grad_weight;
+    DwArgs wa{left, right, grad_output, dst, rows, chunk_rows, Wn, c.U, c.V, W1, W2, t};
+    const dim3 grid(static_cast<unsigned>(l.np), static_cast<unsigned>(chunks));
+    uvu_dw_stage<<<grid, 256, sizeof(DwSmem), s>>>(wa);
+    if (chunks > 1) sum_chunks<<<1024, 256, 0, s>>>(partial, grad_weight, Wn, static_cast<int>(chunks));
+  } else if (needed & 4) {
     const size_t smem = (kRT * 2 * 128 + kRT * 2 * 32) * sizeof(float);
     if ((st = allow_smem(reinterpret_cast<const void*>(&uvu_dw_tile), smem)) != ICTC_OK) return st;
     const int64_t chunk_rows = ((ceil_div(rows, chunks) + kRT - 1) / kRT) * kRT;
