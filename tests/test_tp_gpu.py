@@ -257,25 +257,3 @@ def test_no_device_error_flag(cuda_device):
     from ictc_o2_hp_b200 import _lib
     assert _lib.device_error() == 0
 
-
-@pytest.mark.parametrize("channels,m_max,parity", [(128, 6, "full"), (64, 3, "full"),
-                                                   (32, 2, "canonical"), (48, 5, "full"),
-                                                   (100, 4, "canonical"), (7, 1, "full")])
-def test_backward_split_agrees(channels, m_max, parity, cuda_device, monkeypatch):
-    """The path-split backward (two warps per channel group, ICTC_TP_BACKWARD=split)
-    matches the default kernel and the oracle."""
-    from ictc_o2_hp_b200 import TensorProduct
-    torch.manual_seed(channels + 10 * m_max)
-    tp = TensorProduct(channels, m_max, parity=parity).to(cuda_device)
-    x = torch.randn(517, tp.representation_dimension, device=cuda_device)
-    y = torch.randn_like(x)
-    g = torch.randn_like(x)
-    ref = run_tp(tp, x, y, g, cuda_device)
-    monkeypatch.setenv("ICTC_TP_BACKWARD", "split")
-    got = run_tp(tp, x, y, g, cuda_device)
-    monkeypatch.delenv("ICTC_TP_BACKWARD")
-    oracle = O.TpOracle(channels, m_max, parity)
-    want = oracle.vjp(*(t.detach().cpu().double().numpy() for t in (x, y, tp.weight, g)))
-    for a, b, w in zip(got, ref, want):
-        assert O.max_error(a, b) < 1e-6
-        assert O.max_error(a, w) <= TOL
