@@ -18,6 +18,7 @@
 
 #include "common.cuh"
 #include "rowtile.cuh"
+#include "sgemm.cuh"
 #include "tma.cuh"
 #include "uvu_table.cuh"
 
@@ -116,6 +117,22 @@ __device__ __forceinline__ void gw8_compute(const GwRegs& r, const float (&c)[8]
     } else {
       out[u] = g0 * t0;
     }
+  }
+}
+
+// Loads 4 channels x D values of one entry row segment (zeros past U).
+template <int D>
+__device__ __forceinline__ void ut_like_load(float (&v)[4 * D], const float* __restrict__ src,
+                                             int u, int U, bool vec) {
+  if (vec && u + 3 < U) {
+#pragma unroll
+    for (int q = 0; q < D; ++q) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(src) + q);
+      v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4 * D; ++q) v[q] = u + q / D < U ? __ldg(src + q) : 0.f;
   }
 }
 
@@ -761,6 +778,90 @@ __global__ void __launch_bounds__(128, 4) radial_dalpha(DaArgs A) {
   with_dims(d1, d3, [&]<int D1, int D3>() { radial_dalpha_body<D1, D3>(A, gwt, ht, red); });
 }
 
+// ------------------------------------------------------------ materialized gw
+//
+// radial_gw: gw[e, p*U + u] = sum_{kc,a,b} c_p[kc][a][b] g_k[e,u,kc] x_i[e,u,a] y_j[e,b]
+// for one block of edges, written row-major [E][Wn] so that dhidden = gw alpha and
+// dalpha = gw^T hidden run as plain GEMMs (sgemm_tile).  A CTA takes 16 edges; per
+// path each thread writes 4 consecutive channels of one edge (one float4 store),
+// reading x and g through L1 (the CTA's rows are re-read by every path).
+constexpr int kGwEdges = 16;
+
+struct GwArgs {
+  const float* x; const float* ang; const float* g; float* gw;
+  int64_t rows; int U, W1, W2; int64_t Wn; UvuDev t; bool vec;
+};
+
+__global__ void __launch_bounds__(256) radial_gw(GwArgs A) {
+  extern __shared__ float gys[];  // [kGwEdges][W2]
+  const int tid = threadIdx.x;
+  const int64_t e0 = static_cast<int64_t>(blockIdx.x) * kGwEdges;
+  for (int q = tid; q < kGwEdges * A.W2; q += 256) {
+    const int r = q / A.W2, c = q - r * A.W2;
+    gys[q] = e0 + r < A.rows ? __ldg(A.ang + (e0 + r) * A.W2 + c) : 0.f;
+  }
+  __syncthreads();
+  const int nuq = (A.U + 3) / 4;                 // channel quads per path
+  const int per_path = kGwEdges * nuq;
+  for (int p = 0; p < A.t.np; ++p) {
+    const int4 pt = A.t.paths[p];
+    const int2 ei = A.t.in1[pt.x], ej = A.t.in2[pt.y], ek = A.t.in1[pt.z];
+    float c[8];
+    load_coef(A.t, p, c);
+    for (int q = tid; q < per_path; q += 256) {
+      const int r = q / nuq, u0 = (q - r * nuq) * 4;
+      const int64_t e = e0 + r;
+      if (e >= A.rows) continue;
+      const float y0 = gys[r * A.W2 + ej.x], y1 = ej.y == 2 ? gys[r * A.W2 + ej.x + 1] : 0.f;
+      const float c00 = fmaf(c[0], y0, c[1] * y1), c01 = fmaf(c[2], y0, c[3] * y1);
+      const float c10 = fmaf(c[4], y0, c[5] * y1), c11 = fmaf(c[6], y0, c[7] * y1);
+      const float* xs = A.x + e * A.W1 + ei.x + u0 * ei.y;
+      const float* gs = A.g + e * A.W1 + ek.x + u0 * ek.y;
+      float out[4];
+      with_dims(ei.y, ek.y, [&]<int D1, int D3>() {
+        float xv[4 * D1], gv[4 * D3];
+        ut_like_load<D1>(xv, xs, u0, A.U, A.vec);
+        ut_like_load<D3>(gv, gs, u0, A.U, A.vec);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float x0 = xv[k * D1], x1 = D1 == 2 ? xv[k * D1 + 1] : 0.f;
+          const float g0 = gv[k * D3], g1 = D3 == 2 ? gv[k * D3 + 1] : 0.f;
+          float t0 = c00 * x0;
+          if (D1 == 2) t0 = fmaf(c01, x1, t0);
+          if (D3 == 2) {
+            float t1 = c10 * x0;
+            if (D1 == 2) t1 = fmaf(c11, x1, t1);
+            out[k] = fmaf(g0, t0, g1 * t1);
+          } else {
+            out[k] = g0 * t0;
+          }
+        }
+      });
+      float* dst = A.gw + e * A.Wn + static_cast<int64_t>(p) * A.U + u0;
+      if (A.vec && u0 + 3 < A.U) {
+        *reinterpret_cast<float4*>(dst) = make_float4(out[0], out[1], out[2], out[3]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (u0 + k < A.U) dst[k] = out[k];
+      }
+    }
+  }
+}
+
+// Column sums of rows [r0, r1) of a [rows][n] matrix into dst[blockIdx.y][n]
+// (row chunks summed in a fixed order by radial_sum_chunks).
+__global__ void column_sums(const float* __restrict__ src, float* __restrict__ dst, int64_t rows,
+                            int64_t n, int64_t chunk_rows) {
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (col >= n) return;
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * chunk_rows;
+  const int64_t r1 = r0 + chunk_rows < rows ? r0 + chunk_rows : rows;
+  float s = 0.f;
+  for (int64_t r = r0; r < r1; ++r) s += src[r * n + col];
+  dst[static_cast<int64_t>(blockIdx.y) * n + col] = s;
+}
+
 __global__ void radial_sum_chunks(const float* __restrict__ partial, float* __restrict__ dst,
                                   int64_t numel, int chunks) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < numel;
@@ -784,6 +885,36 @@ int radial_validate(const RadialConfig& c) {
     return fail(ICTC_ERR_UNSUPPORTED, "radial fusion supports channels <= %d (got %d)", kUT, c.U);
   if (c.M > 32 || c.M2 > 32) return fail(ICTC_ERR_UNSUPPORTED, "m_max above 32");
   return ICTC_OK;
+}
+
+// Weight gradients through a materialized gw: edges in blocks of at most
+// kGwBlock (gw block = kGwBlock x Wn floats), dalpha split over kchunks K ranges
+// per block; partials summed in a fixed order at the end.
+constexpr int64_t kGwBlock = 262144;
+
+struct GwPlan {
+  bool ok;
+  int64_t blk, nblocks, kchunks, k_chunk;
+  size_t gw_bytes, da_part_bytes, db_part_bytes;
+};
+
+GwPlan radial_gw_plan(int device, int64_t rows, int64_t Wn, int U, int H) {
+  GwPlan g{};
+  if (rows <= 0 || Wn % 4 != 0 || U % 4 != 0 || H % 4 != 0) return g;
+  g.blk = rows < kGwBlock ? rows : kGwBlock;
+  g.nblocks = (rows + g.blk - 1) / g.blk;
+  const int64_t tiles = ((Wn + kGemmBM - 1) / kGemmBM) * ((H + kGemmBN - 1) / kGemmBN);
+  int64_t kc = (16 * static_cast<int64_t>(sm_count(device)) + tiles - 1) / tiles;
+  const int64_t max_kc = (g.blk + 1023) / 1024;
+  if (kc > max_kc) kc = max_kc;
+  if (kc < 1) kc = 1;
+  g.k_chunk = (((g.blk + kc - 1) / kc) + kGemmBK - 1) / kGemmBK * kGemmBK;
+  g.kchunks = (g.blk + g.k_chunk - 1) / g.k_chunk;
+  g.gw_bytes = static_cast<size_t>(g.blk) * Wn * sizeof(float);
+  g.da_part_bytes = static_cast<size_t>(g.nblocks * g.kchunks) * Wn * H * sizeof(float);
+  g.db_part_bytes = static_cast<size_t>(g.nblocks * g.kchunks) * Wn * sizeof(float);
+  g.ok = true;
+  return g;
 }
 
 int64_t radial_chunks(int device, int64_t rows, int P, int U, int H) {
@@ -850,7 +981,12 @@ extern "C" int32_t ictc_o2_radial_workspace(ICTC_RADIAL_ARGS, int64_t rows, int3
   }
   const int64_t chunks = radial_chunks(device, rows, static_cast<int>(P), c.U, c.H);
   const size_t Wn = static_cast<size_t>(P) * c.U;
-  const size_t part = chunks > 1 ? static_cast<size_t>(chunks) * (Wn * c.H + Wn) * sizeof(float) : 0;
+  size_t part = chunks > 1 ? static_cast<size_t>(chunks) * (Wn * c.H + Wn) * sizeof(float) : 0;
+  const GwPlan gp = radial_gw_plan(device, rows, static_cast<int64_t>(Wn), c.U, c.H);
+  if (gp.ok) {
+    const size_t gwb = gp.gw_bytes + gp.da_part_bytes + gp.db_part_bytes;
+    if (gwb > part) part = gwb;
+  }
   *forward_bytes = at;
   *backward_bytes = at + part;
   return ICTC_OK;
@@ -947,32 +1083,93 @@ extern "C" int32_t ictc_o2_radial_backward(
                    rows, c.U, Up, c.H, W1, W2, t, tvec};
     if ((st = launch_radial_tile<kRtDx>(ra, s)) != ICTC_OK) return st;
   }
-  const bool vec = (W1 % 4 == 0) && (c.U % 8 == 0) && aligned(left, 16) && aligned(grad_output, 16);
-  if (needed & 4) {
-    DhArgs da{left, angular, grad_output, alpha, grad_hidden, rows, c.U, c.H, W1, W2, t, vec,
-              (c.H % 4 == 0) && aligned(alpha, 16)};
-    const dim3 grid(static_cast<unsigned>(ceil_div(rows, kDhE)), (c.H + kDhH - 1) / kDhH);
-    radial_dhidden<<<grid, 128, 0, s>>>(da);
-  }
-  if (needed & 24) {
-    // grad_alpha doubles as scratch when only the bias gradient is requested
-    if (!grad_alpha) return fail(ICTC_ERR_INVALID, "grad_alpha is required when dbias is");
-    const int64_t chunk_rows = ((ceil_div(rows, chunks) + kDaE - 1) / kDaE) * kDaE;
-    const dim3 grid(static_cast<unsigned>(l.np),
-                    ((c.U + kDaU - 1) / kDaU) * ((c.H + kDaH - 1) / kDaH),
-                    static_cast<unsigned>(chunks));
-    const int64_t da_numel = Wn * c.H;
-    float* da = chunks > 1 ? partial : grad_alpha;
-    float* db = chunks > 1 ? partial + chunks * da_numel : ((needed & 16) ? grad_bias : nullptr);
-    DaArgs aa{left, angular, grad_output, radial_hidden, da, db, rows, chunk_rows, da_numel, Wn,
-              c.U, c.H, W1, W2, t, vec, (c.H % 4 == 0) && aligned(radial_hidden, 16)};
-    radial_dalpha<<<grid, 128, 0, s>>>(aa);
-    if (chunks > 1) {
-      radial_sum_chunks<<<1024, 256, 0, s>>>(partial, grad_alpha, da_numel,
-                                             static_cast<int>(chunks));
-      if (needed & 16)
-        radial_sum_chunks<<<256, 256, 0, s>>>(partial + chunks * da_numel, grad_bias, Wn,
-                                              static_cast<int>(chunks));
+  const GwPlan gp = radial_gw_plan(device, rows, Wn, c.U, c.H);
+  const bool gw_path = (needed & 28) && gp.ok && aligned(alpha, 16) && aligned(radial_hidden, 16) &&
+                       (!(needed & 4) || aligned(grad_hidden, 16)) &&
+                       workspace_bytes >= at_bytes + gp.gw_bytes + gp.da_part_bytes +
+                                              gp.db_part_bytes;
+  if (gw_path) {
+    // gw blocks in the workspace, then dhidden = gw alpha and dalpha = gw^T hidden
+    float* gw = partial;
+    float* dapart = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(gw) + gp.gw_bytes);
+    float* dbpart =
+        reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(dapart) + gp.da_part_bytes);
+    const bool gvec = (W1 % 4 == 0) && aligned(left, 16) && aligned(grad_output, 16);
+    const int64_t nparts = gp.nblocks * gp.kchunks;
+    for (int64_t blk = 0; blk < gp.nblocks; ++blk) {
+      const int64_t r0 = blk * gp.blk;
+      const int64_t nb = rows - r0 < gp.blk ? rows - r0 : gp.blk;
+      GwArgs ga{left + r0 * W1, angular + r0 * W2, grad_output + r0 * W1, gw, nb, c.U, W1, W2, Wn,
+                t, gvec};
+      radial_gw<<<static_cast<unsigned>(ceil_div(nb, kGwEdges)), 256,
+                  static_cast<size_t>(kGwEdges) * W2 * sizeof(float), s>>>(ga);
+      if (needed & 4) {
+        SgemmArgs g{gw, alpha, grad_hidden + r0 * c.H, nb, c.H, Wn, Wn, c.H, c.H, Wn, 0};
+        const dim3 grid(static_cast<unsigned>(ceil_div(nb, kGemmBM)),
+                        static_cast<unsigned>(ceil_div(c.H, kGemmBN)), 1);
+        sgemm_tile<false><<<grid, kGemmThreads, 0, s>>>(g);
+      }
+      if (needed & 8) {
+        SgemmArgs g{gw, radial_hidden + r0 * c.H, dapart + blk * gp.kchunks * Wn * c.H, Wn, c.H,
+                    nb, Wn, c.H, c.H, gp.k_chunk, Wn * c.H};
+        const dim3 grid(static_cast<unsigned>(ceil_div(Wn, kGemmBM)),
+                        static_cast<unsigned>(ceil_div(c.H, kGemmBN)),
+                        static_cast<unsigned>(ceil_div(nb, gp.k_chunk)));
+        sgemm_tile<true><<<grid, kGemmThreads, 0, s>>>(g);
+      }
+      if (needed & 16) {
+        const dim3 grid(static_cast<unsigned>(ceil_div(Wn, 256)),
+                        static_cast<unsigned>(ceil_div(nb, gp.k_chunk)));
+        column_sums<<<grid, 256, 0, s>>>(gw, dbpart + blk * gp.kchunks * Wn, nb, Wn, gp.k_chunk);
+      }
+      // a last block shorter than the others leaves its unused chunks at zero
+      const int64_t used = ceil_div(nb, gp.k_chunk);
+      if (used < gp.kchunks) {
+        if (needed & 8) {
+          e = cudaMemsetAsync(dapart + (blk * gp.kchunks + used) * Wn * c.H, 0,
+                              static_cast<size_t>(gp.kchunks - used) * Wn * c.H * sizeof(float), s);
+          if (e != cudaSuccess) return cuda_fail(e, "memset");
+        }
+        if (needed & 16) {
+          e = cudaMemsetAsync(dbpart + (blk * gp.kchunks + used) * Wn, 0,
+                              static_cast<size_t>(gp.kchunks - used) * Wn * sizeof(float), s);
+          if (e != cudaSuccess) return cuda_fail(e, "memset");
+        }
+      }
+    }
+    if (needed & 8)
+      radial_sum_chunks<<<1024, 256, 0, s>>>(dapart, grad_alpha, Wn * c.H,
+                                             static_cast<int>(nparts));
+    if (needed & 16)
+      radial_sum_chunks<<<256, 256, 0, s>>>(dbpart, grad_bias, Wn, static_cast<int>(nparts));
+  } else {
+    const bool vec = (W1 % 4 == 0) && (c.U % 8 == 0) && aligned(left, 16) && aligned(grad_output, 16);
+    if (needed & 4) {
+      DhArgs da{left, angular, grad_output, alpha, grad_hidden, rows, c.U, c.H, W1, W2, t, vec,
+                (c.H % 4 == 0) && aligned(alpha, 16)};
+      const dim3 grid(static_cast<unsigned>(ceil_div(rows, kDhE)), (c.H + kDhH - 1) / kDhH);
+      radial_dhidden<<<grid, 128, 0, s>>>(da);
+    }
+    if (needed & 24) {
+      // grad_alpha doubles as scratch when only the bias gradient is requested
+      if (!grad_alpha) return fail(ICTC_ERR_INVALID, "grad_alpha is required when dbias is");
+      const int64_t chunk_rows = ((ceil_div(rows, chunks) + kDaE - 1) / kDaE) * kDaE;
+      const dim3 grid(static_cast<unsigned>(l.np),
+                      ((c.U + kDaU - 1) / kDaU) * ((c.H + kDaH - 1) / kDaH),
+                      static_cast<unsigned>(chunks));
+      const int64_t da_numel = Wn * c.H;
+      float* da = chunks > 1 ? partial : grad_alpha;
+      float* db = chunks > 1 ? partial + chunks * da_numel : ((needed & 16) ? grad_bias : nullptr);
+      DaArgs aa{left, angular, grad_output, radial_hidden, da, db, rows, chunk_rows, da_numel, Wn,
+                c.U, c.H, W1, W2, t, vec, (c.H % 4 == 0) && aligned(radial_hidden, 16)};
+      radial_dalpha<<<grid, 128, 0, s>>>(aa);
+      if (chunks > 1) {
+        radial_sum_chunks<<<1024, 256, 0, s>>>(partial, grad_alpha, da_numel,
+                                               static_cast<int>(chunks));
+        if (needed & 16)
+          radial_sum_chunks<<<256, 256, 0, s>>>(partial + chunks * da_numel, grad_bias, Wn,
+                                                static_cast<int>(chunks));
+      }
     }
   }
   e = cudaGetLastError();
