@@ -205,6 +205,8 @@ struct RadTileArgs {
   int U, Up, H, W1, W2;
   UvuDev t;
   bool vec;  // 16-byte access to 4-channel groups of opnd / x / out
+  float* gw = nullptr;  // dx mode, optional: edge-weight gradient [rows][Wn]
+  int64_t Wn = 0;
 };
 
 template <int UT>
@@ -441,6 +443,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
                         A.U, A.vec);
               load4<D1>(xv, A.x + row * A.W1 + ei.x + static_cast<int64_t>(u) * D1, row_ok, u,
                         A.U, A.vec);
+              float gwv[4];
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 float w = acc[ee][half * 4 + q];
@@ -466,6 +469,18 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
                 }
                 dyp0 = fmaf(w, d0, dyp0);
                 dyp1 = fmaf(w, d1, dyp1);
+                // gw = sum_b y_b sum_{kc,a} c[kc][a][b] g[kc] x[a]
+                gwv[q] = fmaf(y0, d0, y1 * d1);
+              }
+              if (A.gw != nullptr && row_ok) {
+                float* dst = A.gw + row * A.Wn + static_cast<int64_t>(p) * A.U + u;
+                if (A.vec && u + 3 < A.U) {
+                  *reinterpret_cast<float4*>(dst) = make_float4(gwv[0], gwv[1], gwv[2], gwv[3]);
+                } else {
+#pragma unroll
+                  for (int q = 0; q < 4; ++q)
+                    if (u + q < A.U) dst[q] = gwv[q];
+                }
               }
             }
           }
@@ -529,9 +544,7 @@ template <int MODE>
 int launch_radial_tile(const RadTileArgs& ra, cudaStream_t s) {
   const int ut = ra.U <= 64 ? 64 : 128;
   const size_t smem = radial_tile_smem(ut, ra.H, ra.W2, ra.t.np, ra.t.n1, ra.t.n2, MODE == kRtDx);
-  if (smem > 225 * 1024)
-    return fail(ICTC_ERR_UNSUPPORTED, "radial tile needs %zu bytes of shared memory (hidden %d)",
-                smem, ra.H);
+  if (smem > 225 * 1024) return ICTC_ERR_UNSUPPORTED;  // caller falls back to the row tile
   const void* fn = ut == 64 ? reinterpret_cast<const void*>(&radial_tile<MODE, 64>)
                             : reinterpret_cast<const void*>(&radial_tile<MODE, 128>);
   const int st = allow_smem(fn, smem);
@@ -1019,7 +1032,14 @@ extern "C" int32_t ictc_o2_radial_forward(const float* left, const float* angula
                    aligned(output, 16);
   RadTileArgs ra{left, nullptr, radial_hidden, angular, at, bias, output, nullptr, rows,
                  c.U, Up, c.H, th.width1, th.width2, t, vec};
-  return launch_radial_tile<kRtFwd>(ra, s);
+  st = launch_radial_tile<kRtFwd>(ra, s);
+  if (st == ICTC_ERR_UNSUPPORTED) {
+    // hidden tile too large to stay resident: the generic row tile streams it
+    RowtileArgs rr{left, nullptr, radial_hidden, angular, at, bias, output, nullptr, rows,
+                   c.U, Up, c.H, th.width1, c.H, th.width2, t};
+    st = launch_rowtile<kRadFwd>(rr, s);
+  }
+  return st;
 }
 
 extern "C" int32_t ictc_o2_radial_backward(
@@ -1070,6 +1090,13 @@ extern "C" int32_t ictc_o2_radial_backward(
   const int W1 = th.width1, W2 = th.width2;
   float* at = static_cast<float*>(workspace);
   float* partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + at_bytes);
+  const GwPlan gp = radial_gw_plan(device, rows, Wn, c.U, c.H);
+  const bool gw_path = (needed & 28) && gp.ok && aligned(alpha, 16) && aligned(radial_hidden, 16) &&
+                       (!(needed & 4) || aligned(grad_hidden, 16)) &&
+                       workspace_bytes >= at_bytes + gp.gw_bytes + gp.da_part_bytes +
+                                              gp.db_part_bytes;
+  const bool tvec = (W1 % 4 == 0) && (c.U % 4 == 0) && aligned(left, 16) &&
+                    aligned(grad_output, 16) && aligned(grad_left, 16);
   if (needed & 3) {
     // dx and dy together: both need the regenerated edge weights
     transpose_alpha<<<1024, 256, 0, s>>>(alpha, at, l.np, c.U, Up, c.H);
@@ -1077,17 +1104,18 @@ extern "C" int32_t ictc_o2_radial_backward(
     // alias inputs; the caller passes both buffers (see the Python wrapper)
     if (!grad_left || !grad_angular)
       return fail(ICTC_ERR_INVALID, "dx and dy buffers are both required when either is");
-    const bool tvec = (W1 % 4 == 0) && (c.U % 4 == 0) && aligned(left, 16) &&
-                      aligned(grad_output, 16) && aligned(grad_left, 16);
-    RadTileArgs ra{grad_output, left, radial_hidden, angular, at, bias, grad_left, grad_angular,
-                   rows, c.U, Up, c.H, W1, W2, t, tvec};
-    if ((st = launch_radial_tile<kRtDx>(ra, s)) != ICTC_OK) return st;
+    if (!gw_path) {
+      RadTileArgs ra{grad_output, left, radial_hidden, angular, at, bias, grad_left,
+                     grad_angular, rows, c.U, Up, c.H, W1, W2, t, tvec};
+      st = launch_radial_tile<kRtDx>(ra, s);
+      if (st == ICTC_ERR_UNSUPPORTED) {
+        RowtileArgs rr{grad_output, left, radial_hidden, angular, at, bias, grad_left,
+                       grad_angular, rows, c.U, Up, c.H, W1, c.H, W2, t};
+        st = launch_rowtile<kRadDx>(rr, s);
+      }
+      if (st != ICTC_OK) return st;
+    }
   }
-  const GwPlan gp = radial_gw_plan(device, rows, Wn, c.U, c.H);
-  const bool gw_path = (needed & 28) && gp.ok && aligned(alpha, 16) && aligned(radial_hidden, 16) &&
-                       (!(needed & 4) || aligned(grad_hidden, 16)) &&
-                       workspace_bytes >= at_bytes + gp.gw_bytes + gp.da_part_bytes +
-                                              gp.db_part_bytes;
   if (gw_path) {
     // gw blocks in the workspace, then dhidden = gw alpha and dalpha = gw^T hidden
     float* gw = partial;
@@ -1099,10 +1127,31 @@ extern "C" int32_t ictc_o2_radial_backward(
     for (int64_t blk = 0; blk < gp.nblocks; ++blk) {
       const int64_t r0 = blk * gp.blk;
       const int64_t nb = rows - r0 < gp.blk ? rows - r0 : gp.blk;
-      GwArgs ga{left + r0 * W1, angular + r0 * W2, grad_output + r0 * W1, gw, nb, c.U, W1, W2, Wn,
-                t, gvec};
-      radial_gw<<<static_cast<unsigned>(ceil_div(nb, kGwEdges)), 256,
-                  static_cast<size_t>(kGwEdges) * W2 * sizeof(float), s>>>(ga);
+      bool gw_done = false;
+      if (needed & 3) {
+        // dx, dy of the block; the tile also writes the block's gw
+        RadTileArgs ra{grad_output + r0 * W1, left + r0 * W1, radial_hidden + r0 * c.H,
+                       angular + r0 * W2, at, bias, grad_left + r0 * W1, grad_angular + r0 * W2,
+                       nb, c.U, Up, c.H, W1, W2, t, tvec};
+        ra.gw = gw;
+        ra.Wn = Wn;
+        st = launch_radial_tile<kRtDx>(ra, s);
+        if (st == ICTC_ERR_UNSUPPORTED) {  // hidden tile too large: row tile, gw separately
+          RowtileArgs rr{grad_output + r0 * W1, left + r0 * W1, radial_hidden + r0 * c.H,
+                         angular + r0 * W2, at, bias, grad_left + r0 * W1,
+                         grad_angular + r0 * W2, nb, c.U, Up, c.H, W1, c.H, W2, t};
+          st = launch_rowtile<kRadDx>(rr, s);
+        } else {
+          gw_done = st == ICTC_OK;
+        }
+        if (st != ICTC_OK) return st;
+      }
+      if (!gw_done) {
+        GwArgs ga{left + r0 * W1, angular + r0 * W2, grad_output + r0 * W1, gw, nb, c.U, W1, W2,
+                  Wn, t, gvec};
+        radial_gw<<<static_cast<unsigned>(ceil_div(nb, kGwEdges)), 256,
+                    static_cast<size_t>(kGwEdges) * W2 * sizeof(float), s>>>(ga);
+      }
       if (needed & 4) {
         SgemmArgs g{gw, alpha, grad_hidden + r0 * c.H, nb, c.H, Wn, Wn, c.H, c.H, Wn, 0};
         const dim3 grid(static_cast<unsigned>(ceil_div(nb, kGemmBM)),
