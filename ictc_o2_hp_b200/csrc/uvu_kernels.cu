@@ -17,6 +17,7 @@
 // one thread per u, weights read once, weight gradients written once.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -272,6 +273,7 @@ __global__ void __launch_bounds__(256)
 
 #include "uvu_tile.cuh"
 #include "uvu_rowstream.cuh"
+#include "uvu_rowquad.cuh"
 #include "uvu_dy.cuh"
 #include "uvu_dw.cuh"
 
@@ -601,6 +603,63 @@ int launch_rowstream(const RowStreamArgs& ra, int device, cudaStream_t s) {
   return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "uvu row stream launch");
 }
 
+template <int MODE, int NQ, int R>
+int launch_rowquad_shape(const RowStreamArgs& ra, int device, size_t smem, cudaStream_t s) {
+  const void* fn = reinterpret_cast<const void*>(&uvu_rowquad<MODE, NQ, R>);
+  int st = allow_smem(fn, smem);
+  if (st != ICTC_OK) return st;
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kRsThreads, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+  int64_t grid = static_cast<int64_t>(sm_count(device)) * (per_sm > 0 ? per_sm : 1);
+  if (grid > ra.rows) grid = ra.rows;
+  uvu_rowquad<MODE, NQ, R><<<static_cast<unsigned>(grid), kRsThreads, smem, s>>>(ra);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "uvu row quad launch");
+}
+
+template <int MODE, int NQ>
+int launch_rowquad_nq(const RowStreamArgs& ra, int device, size_t smem, cudaStream_t s) {
+  using Sh = RqShape<NQ>;
+  const int r = rowquad_rows_per_lane<NQ>(ra.U);
+  if (r == 1) return launch_rowquad_shape<MODE, NQ, 1>(ra, device, smem, s);
+  if constexpr (Sh::L >= 2 && 2 * Sh::QT <= 4)
+    if (r == 2) return launch_rowquad_shape<MODE, NQ, 2>(ra, device, smem, s);
+  if constexpr (Sh::L >= 4 && Sh::QT == 1)
+    if (r == 4) return launch_rowquad_shape<MODE, NQ, 4>(ra, device, smem, s);
+  return ICTC_ERR_UNSUPPORTED;
+}
+
+// Per-row weights with uvu_rowquad<MODE> (V in {8, 16, 32, 64});
+// ICTC_ERR_UNSUPPORTED when the shape or alignment does not suit it.
+template <int MODE>
+int launch_rowquad(const RowStreamArgs& ra, int device, cudaStream_t s) {
+  if (!rowstream_fits(ra.U, ra.V, ra.W1, ra.W2, ra.t.n1) || !aligned(ra.w, 16) ||
+      (MODE == kRsBwd && (ra.needed & 4) && !aligned(ra.dw, 16)))
+    return ICTC_ERR_UNSUPPORTED;
+  const size_t smem = rowstream_smem(ra.U, ra.W2, ra.t.n1);
+  switch (ra.V) {
+    case 8: return launch_rowquad_nq<MODE, 2>(ra, device, smem, s);
+    case 16: return launch_rowquad_nq<MODE, 4>(ra, device, smem, s);
+    case 32: return launch_rowquad_nq<MODE, 8>(ra, device, smem, s);
+    case 64: return launch_rowquad_nq<MODE, 16>(ra, device, smem, s);
+    default: return ICTC_ERR_UNSUPPORTED;
+  }
+}
+
+// Per-row-weight kernels in order of preference; ICTC_UVU_ROW_KERNEL = "quad",
+// "stream" or "rowwise" starts the chain further down (tests cover each).
+template <int MODE>
+int launch_per_row(const RowStreamArgs& ra, int device, cudaStream_t s) {
+  const char* pick = getenv("ICTC_UVU_ROW_KERNEL");
+  const bool skip_quad = pick != nullptr && (strcmp(pick, "stream") == 0 || strcmp(pick, "rowwise") == 0);
+  const bool skip_stream = pick != nullptr && strcmp(pick, "rowwise") == 0;
+  int st = ICTC_ERR_UNSUPPORTED;
+  if (!skip_quad) st = launch_rowquad<MODE>(ra, device, s);
+  if (st == ICTC_ERR_UNSUPPORTED && !skip_stream) st = launch_rowstream<MODE>(ra, device, s);
+  return st;
+}
+
 }  // namespace
 
 extern "C" int32_t ictc_o2_uvu_forward(const float* left, const float* right, const float* weight,
@@ -625,7 +684,7 @@ extern "C" int32_t ictc_o2_uvu_forward(const float* left, const float* right, co
   if (!shared) {
     RowStreamArgs ra{left, right, weight, nullptr, output, nullptr, nullptr, rows,
                      static_cast<int64_t>(l.np) * c.U * c.V, c.U, c.V, W1, W2, t, 0};
-    st = launch_rowstream<kRsFwd>(ra, device, s);
+    st = launch_per_row<kRsFwd>(ra, device, s);
     if (st == ICTC_OK) return ICTC_OK;
     if (st != ICTC_ERR_UNSUPPORTED) return st;
     const int bd = ((c.U + 31) / 32) * 32;
@@ -691,7 +750,7 @@ extern "C" int32_t ictc_o2_uvu_backward(const float* left, const float* right, c
   if (!shared) {
     RowStreamArgs ra{left, right, weight, grad_output, grad_left, grad_right, grad_weight, rows,
                      Wn, c.U, c.V, W1, W2, t, needed};
-    st = launch_rowstream<kRsBwd>(ra, device, s);
+    st = launch_per_row<kRsBwd>(ra, device, s);
     if (st == ICTC_OK) return ICTC_OK;
     if (st != ICTC_ERR_UNSUPPORTED) return st;
     const int bd = ((c.U + 31) / 32) * 32;

@@ -117,11 +117,31 @@ def test_compile_and_double_backward(cuda_device):
         assert O.max_error(a.cpu().numpy(), b.numpy()) <= TOL
 
 
-def test_per_row_role_pruning(cuda_device):
+# Per-row-weight cases, each run on every per-row kernel the C-ABI can pick:
+# "quad" (V in {8, 16, 32, 64}), "stream" (V a multiple of 8) and "rowwise"
+# (any shape); a kernel that does not fit the shape hands over to the next.
+PER_ROW = [c for c in CASES if not c[8]] + [
+    (160, 32, 1, "full", 1, "full", "component", "none", False, 6),  # two channel chunks
+    (64, 16, 2, "full", 2, "full", "norm", "path", False, 7),
+]
+ROW_KERNELS = ["quad", "stream", "rowwise"]
+
+
+@pytest.mark.parametrize("kernel", ROW_KERNELS)
+@pytest.mark.parametrize("case", PER_ROW)
+def test_per_row_kernels(kernel, case, cuda_device, monkeypatch):
+    monkeypatch.setenv("ICTC_UVU_ROW_KERNEL", kernel)
+    test_against_oracle(case, cuda_device)
+
+
+@pytest.mark.parametrize("kernel", ROW_KERNELS)
+@pytest.mark.parametrize("U,V", [(32, 8), (128, 32), (96, 64)])
+def test_per_row_role_pruning(kernel, U, V, cuda_device, monkeypatch):
     """Per-row weights: each subset of requested gradients equals the full VJP."""
     from ictc_o2_hp_b200 import UvuTensorProduct
+    monkeypatch.setenv("ICTC_UVU_ROW_KERNEL", kernel)
     torch.manual_seed(3)
-    tp = UvuTensorProduct(32, 8, 2, shared_weights=False).to(cuda_device)
+    tp = UvuTensorProduct(U, V, 2, shared_weights=False).to(cuda_device)
     x = torch.randn(11, tp.input1_dimension, device=cuda_device, requires_grad=True)
     y = torch.randn(11, tp.input2_dimension, device=cuda_device, requires_grad=True)
     w = torch.randn(11, tp.weight_numel, device=cuda_device, requires_grad=True)
