@@ -6,10 +6,12 @@
 // with a thread layout that keeps every operand but the weights in registers:
 //
 //   * a lane owns one float4 column q of V (QT columns when V = 64) of R channel
-//     rows of the chunk: rows r * G + group, with G channel-row groups per CTA.
-//     A warp instruction therefore reads 512 contiguous bytes of the stage
-//     (no bank conflicts without any rotation), and the lane releases the stage
-//     as soon as its R x QT float4 are in registers;
+//     rows of the chunk (rows group * R + r when a row spans 8 lanes, else
+//     r * G + group, G channel-row groups per CTA).  Each 8-lane phase of a warp
+//     read covers 128 contiguous bytes of the stage (no bank conflicts without
+//     any rotation), the rows owned after the proj reduction are consecutive
+//     channels (conflict-free slot accesses), and the lane releases the stage as
+//     soon as its R x QT float4 are in registers;
 //   * y_j[v, b] of the lane's columns sits in registers for the path;
 //   * proj[u, b] = sum_v w[u, v] y_j[v, b] is reduced over the L lanes of a row
 //     group by a reduce-scatter (each lane ends with one channel row);
@@ -32,7 +34,23 @@ struct RqShape {
   static constexpr int QT = NQ / L;          // float4 columns per lane
   static constexpr int GW = 32 / L;          // channel-row groups per warp
   static constexpr int G = 8 * GW;           // channel-row groups per CTA (8 warps)
+  // chunk row of (group, r): group-major when a row spans 8 lanes (one 8-lane
+  // phase per row either way; consecutive channels for the row owners)
+  static constexpr bool kGroupMajor = L == 8;
+  template <int R>
+  __device__ __forceinline__ static int row(int group, int r) {
+    return kGroupMajor ? group * R + r : r * G + group;
+  }
 };
+
+// Shared memory of uvu_rowquad: barriers, ring, y, x / g / out slots, per-warp
+// dy partials, per-path records.
+inline size_t rowquad_smem(int U, int W2, int n1, int np) {
+  const size_t w2a = static_cast<size_t>((W2 + 3) & ~3);
+  const size_t before = static_cast<size_t>(kRsStages) * kRsChunk + 9 * w2a +
+                        6 * static_cast<size_t>(n1) * U;
+  return 128 + (((before + 3) & ~size_t(3)) + 4 * static_cast<size_t>(np)) * 4;
+}
 
 // Reduce-scatter of v over the lanes lane ^ m for m = M, M / 2, ..., S: while more
 // than MINB values remain, each level keeps one half (the upper half on lanes
@@ -116,6 +134,9 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
   float* gs = xs + 2 * n1 * U;              // [2 n1][U] g slots (VJP)
   float* os = gs + 2 * n1 * U;              // [2 n1][U] out / dx
   float* yp = os + 2 * n1 * U;              // [8 warps][W2a] dy partials
+  // per path: x slot offset, out / g slot offset, y_j offset, y_j dim (16-byte aligned)
+  int4* meta = reinterpret_cast<int4*>(
+      ring + ((kRsStages * kRsChunk + 9 * W2a + 6 * n1 * U + 3) & ~3));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ql = lane % L;
   const int grp = warp * GW + lane / L;
@@ -127,6 +148,12 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
   // the channel row a lane owns after the proj reduction, and whether it writes
   const int rl = ql / (L / R);
   const bool leader = (ql % (L / R)) == 0;
+  const int own = Sh::template row<R>(grp, rl);  // chunk row this lane owns
+  for (int q = tid; q < np; q += kRsThreads) {
+    const int4 pt = __ldg(A.t.paths + q);
+    const int2 ej = __ldg(A.t.in2 + pt.y);
+    meta[q] = make_int4(2 * pt.x * U, 2 * pt.z * U, ej.x, ej.y);
+  }
   const int64_t my_rows = A.rows > blockIdx.x ? (A.rows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int64_t nitems = my_rows * per_row;
   // item -> (row, chunk c, path p), chunk-major within a row
@@ -172,6 +199,9 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
     int c = 0, p = 0;
     for (int item = 0; item < per_row; ++item, ++it) {
       const int st = static_cast<int>(it & (kRsStages - 1));
+      // c[kc * 4 + a * 2 + b]; in flight while the stage lands
+      const float4 ca = __ldg(reinterpret_cast<const float4*>(A.t.coef + 8 * p));
+      const float4 cb = __ldg(reinterpret_cast<const float4*>(A.t.coef + 8 * p + 4));
       ok = mbar_wait(&full[st], static_cast<uint32_t>(it / kRsStages) & 1u, 11);
       if (!ok) break;
       const int u0 = c * CU;
@@ -180,7 +210,7 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
       float4 w[R][QT];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        const int uu = r * G + grp;
+        const int uu = Sh::template row<R>(grp, r);
 #pragma unroll
         for (int t = 0; t < QT; ++t)
           w[r][t] = uu < ncu ? *reinterpret_cast<const float4*>(wc + uu * V + (ql + L * t) * 4)
@@ -199,15 +229,13 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
           if (it + kRsStages < nitems) issue(it + kRsStages, st);
         }
       }
-      const int4 pt = __ldg(A.t.paths + p);
-      const int2 ej = __ldg(A.t.in2 + pt.y);
-      const float4 ca = __ldg(reinterpret_cast<const float4*>(A.t.coef + 8 * p));
-      const float4 cb = __ldg(reinterpret_cast<const float4*>(A.t.coef + 8 * p + 4));
-      // c[kc * 4 + a * 2 + b]
+      const int4 pm = meta[p];
+      const int xo = pm.x, zo = pm.y;  // slot offsets of x_i and of out_k / g_k
+      const int2 ej = make_int2(pm.z, pm.w);
       const float c0 = ca.x, c1 = ca.y, c2 = ca.z, c3 = ca.w;
       const float c4 = cb.x, c5 = cb.y, c6 = cb.z, c7 = cb.w;
-      const int uown = u0 + rl * G + grp;  // channel of the row this lane owns
-      const bool own_ok = rl * G + grp < ncu;
+      const int uown = u0 + own;  // channel of the row this lane owns
+      const bool own_ok = own < ncu;
       auto body = [&]<int D2>() {
         float yv[QT][4][2];
 #pragma unroll
@@ -232,15 +260,13 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
           const float p0 = pv[0], p1 = pv[1];
           if (leader && own_ok) {
             if (MODE == kRsFwd) {
-              const float x0 = xs[(2 * pt.x) * U + uown], x1 = xs[(2 * pt.x + 1) * U + uown];
-              os[(2 * pt.z) * U + uown] += x0 * fmaf(c1, p1, c0 * p0) + x1 * fmaf(c3, p1, c2 * p0);
-              os[(2 * pt.z + 1) * U + uown] +=
-                  x0 * fmaf(c5, p1, c4 * p0) + x1 * fmaf(c7, p1, c6 * p0);
+              const float x0 = xs[xo + uown], x1 = xs[xo + U + uown];
+              os[zo + uown] += x0 * fmaf(c1, p1, c0 * p0) + x1 * fmaf(c3, p1, c2 * p0);
+              os[zo + U + uown] += x0 * fmaf(c5, p1, c4 * p0) + x1 * fmaf(c7, p1, c6 * p0);
             } else {
-              const float g0 = gs[(2 * pt.z) * U + uown], g1 = gs[(2 * pt.z + 1) * U + uown];
-              os[(2 * pt.x) * U + uown] += g0 * fmaf(c1, p1, c0 * p0) + g1 * fmaf(c5, p1, c4 * p0);
-              os[(2 * pt.x + 1) * U + uown] +=
-                  g0 * fmaf(c3, p1, c2 * p0) + g1 * fmaf(c7, p1, c6 * p0);
+              const float g0 = gs[zo + uown], g1 = gs[zo + U + uown];
+              os[xo + uown] += g0 * fmaf(c1, p1, c0 * p0) + g1 * fmaf(c5, p1, c4 * p0);
+              os[xo + U + uown] += g0 * fmaf(c3, p1, c2 * p0) + g1 * fmaf(c7, p1, c6 * p0);
             }
           }
         }
@@ -248,8 +274,8 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
           // s of the owned row, then gathered for the lane's R rows
           float s0 = 0.f, s1 = 0.f;
           if (own_ok) {
-            const float x0 = xs[(2 * pt.x) * U + uown], x1 = xs[(2 * pt.x + 1) * U + uown];
-            const float g0 = gs[(2 * pt.z) * U + uown], g1 = gs[(2 * pt.z + 1) * U + uown];
+            const float x0 = xs[xo + uown], x1 = xs[xo + U + uown];
+            const float g0 = gs[zo + uown], g1 = gs[zo + U + uown];
             s0 = g0 * fmaf(c2, x1, c0 * x0) + g1 * fmaf(c6, x1, c4 * x0);
             s1 = g0 * fmaf(c3, x1, c1 * x0) + g1 * fmaf(c7, x1, c5 * x0);
           }
@@ -264,7 +290,7 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
             float* dst = A.dw + row * A.Wn + (static_cast<int64_t>(p) * U + u0) * V;
 #pragma unroll
             for (int r = 0; r < R; ++r) {
-              const int uu = r * G + grp;
+              const int uu = Sh::template row<R>(grp, r);
               if (uu < ncu) {
 #pragma unroll
                 for (int t = 0; t < QT; ++t) {
