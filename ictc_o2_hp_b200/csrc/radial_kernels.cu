@@ -227,6 +227,10 @@ inline size_t radial_tile_smem(int ut, int H, int W2, int np, int n1, int n2, bo
   return 128 + (aligned_floats + ints) * 4;
 }
 
+__device__ __forceinline__ void prefetch_l1(const float* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
 // Loads 4 channels x D values of one entry of one row (zeros past U or rows).
 template <int D>
 __device__ __forceinline__ void load4(float (&v)[4 * D], const float* __restrict__ src,
@@ -366,6 +370,25 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
       for (int a = 0; a < 4; ++a)
 #pragma unroll
         for (int b = 0; b < 8; ++b) acc[a][b] = 0.f;
+      // Pull the path's epilogue operands (x_i; g_k in dx mode) of this thread's
+      // four edges toward L1 while the path's product runs: lane tc takes line tc
+      // of each edge's slice, lines that start inside the valid channels only.
+      const int4 pt = paths[p];
+      const int2 ea = in1[pt.x], eb = in1[pt.z];
+      const int uspan = A.U - ub < UT ? A.U - ub : UT;
+#pragma unroll
+      for (int ee = 0; ee < 4; ++ee) {
+        const int64_t row = row0 + e0 + ee;
+        if (row < A.rows) {
+          const float* xr = (MODE == kRtFwd ? A.opnd : A.x) + row * A.W1 + ea.x +
+                            static_cast<int64_t>(ub) * ea.y;
+          if (tc * 32 < uspan * ea.y) prefetch_l1(xr + tc * 32);
+          if (MODE == kRtDx) {
+            const float* gr = A.opnd + row * A.W1 + eb.x + static_cast<int64_t>(ub) * eb.y;
+            if (tc * 32 < uspan * eb.y) prefetch_l1(gr + tc * 32);
+          }
+        }
+      }
     }
     const int kn = A.H - ck * kRtKC < kRtKC ? A.H - ck * kRtKC : kRtKC;
     const float* Wb = Wt + st * kc * UT;
@@ -473,13 +496,15 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
                 gwv[q] = fmaf(y0, d0, y1 * d1);
               }
               if (A.gw != nullptr && row_ok) {
+                // streaming stores (evict first): the gw block is far larger than L2
+                // and would otherwise push out the x rows the later paths re-read
                 float* dst = A.gw + row * A.Wn + static_cast<int64_t>(p) * A.U + u;
                 if (A.vec && u + 3 < A.U) {
-                  *reinterpret_cast<float4*>(dst) = make_float4(gwv[0], gwv[1], gwv[2], gwv[3]);
+                  __stcs(reinterpret_cast<float4*>(dst), make_float4(gwv[0], gwv[1], gwv[2], gwv[3]));
                 } else {
 #pragma unroll
                   for (int q = 0; q < 4; ++q)
-                    if (u + q < A.U) dst[q] = gwv[q];
+                    if (u + q < A.U) __stcs(dst + q, gwv[q]);
                 }
               }
             }

@@ -637,7 +637,7 @@ int launch_rowquad(const RowStreamArgs& ra, int device, cudaStream_t s) {
   if (!rowstream_fits(ra.U, ra.V, ra.W1, ra.W2, ra.t.n1) || !aligned(ra.w, 16) ||
       (MODE == kRsBwd && (ra.needed & 4) && !aligned(ra.dw, 16)))
     return ICTC_ERR_UNSUPPORTED;
-  const size_t smem = rowquad_smem(ra.U, ra.W2, ra.t.n1, ra.t.np);
+  const size_t smem = rowquad_smem<MODE>(ra.U, ra.W2, ra.t.n1, ra.t.np);
   if (smem > 220 * 1024) return ICTC_ERR_UNSUPPORTED;
   switch (ra.V) {
     case 8: return launch_rowquad_nq<MODE, 2>(ra, device, smem, s);

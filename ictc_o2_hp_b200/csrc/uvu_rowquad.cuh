@@ -1,8 +1,9 @@
 // Per-row-weight uvu forward and VJP for V in {8, 16, 32, 64}: uvu_rowquad<MODE, NQ, R>.
 //
 // Same stream as uvu_rowstream (persistent CTAs take rows in turn; each row's
-// [P][U][V] weights arrive as chunks of whole [u][v] rows through a 4-stage ring
-// of bulk asynchronous copies, refilled by the last warp that releases a stage),
+// [P][U][V] weights arrive as chunks of whole [u][v] rows through a ring of bulk
+// asynchronous copies (4 stages), refilled by the last warp that releases a
+// stage),
 // with a thread layout that keeps every operand but the weights in registers:
 //
 //   * a lane owns one float4 column q of V (QT columns when V = 64) of R channel
@@ -25,7 +26,7 @@
 // per lane (R <= lanes per row, R x QT <= 4 so a chunk fits one ring stage).
 //
 // This header is included inside the anonymous namespace of uvu_kernels.cu,
-// after uvu_rowstream.cuh (RowStreamArgs, kRsStages, kRsChunk).
+// after uvu_rowstream.cuh (RowStreamArgs, kRsChunk, kRsThreads).
 #pragma once
 
 template <int NQ>
@@ -43,12 +44,19 @@ struct RqShape {
   }
 };
 
-// Shared memory of uvu_rowquad: barriers, ring, y, x / g / out slots, per-warp
-// dy partials, per-path records.
+// Ring depth (a fifth forward stage, which fits at two CTAs per SM, measured no
+// faster).
+template <int MODE>
+constexpr int rq_stages() { return 4; }
+
+// Shared memory of uvu_rowquad: barriers, ring, y, x (/ g) / out slots, per-warp
+// dy partials (VJP), per-path records.
+template <int MODE>
 inline size_t rowquad_smem(int U, int W2, int n1, int np) {
   const size_t w2a = static_cast<size_t>((W2 + 3) & ~3);
-  const size_t before = static_cast<size_t>(kRsStages) * kRsChunk + 9 * w2a +
-                        6 * static_cast<size_t>(n1) * U;
+  const size_t slots = (MODE == kRsFwd ? 4 : 6) * static_cast<size_t>(n1) * U;
+  const size_t before = static_cast<size_t>(rq_stages<MODE>()) * kRsChunk + w2a + slots +
+                        (MODE == kRsFwd ? 0 : 8 * w2a);
   return 128 + (((before + 3) & ~size_t(3)) + 4 * static_cast<size_t>(np)) * 4;
 }
 
@@ -122,21 +130,22 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
   constexpr int L = Sh::L, QT = Sh::QT, GW = Sh::GW, G = Sh::G;
   constexpr int V = 4 * NQ;
   constexpr int CU = G * R;  // channel rows per chunk
+  constexpr int NS = rq_stages<MODE>();
   static_assert(R <= L && R * QT <= 4 && CU * V <= kRsChunk, "chunk shape");
   extern __shared__ __align__(128) unsigned char rq_raw[];
   uint64_t* full = reinterpret_cast<uint64_t*>(rq_raw);
   unsigned* done = reinterpret_cast<unsigned*>(rq_raw + 64);
-  float* ring = reinterpret_cast<float*>(rq_raw + 128);  // [kRsStages][kRsChunk]
+  float* ring = reinterpret_cast<float*>(rq_raw + 128);  // [NS][kRsChunk]
   const int W2a = (A.W2 + 3) & ~3;
   const int n1 = A.t.n1, np = A.t.np, U = A.U;
-  float* ys = ring + kRsStages * kRsChunk;  // [W2a]
-  float* xs = ys + W2a;                     // [2 n1][U] x slots
-  float* gs = xs + 2 * n1 * U;              // [2 n1][U] g slots (VJP)
-  float* os = gs + 2 * n1 * U;              // [2 n1][U] out / dx
-  float* yp = os + 2 * n1 * U;              // [8 warps][W2a] dy partials
+  float* ys = ring + NS * kRsChunk;  // [W2a]
+  float* xs = ys + W2a;              // [2 n1][U] x slots
+  float* gs = xs + 2 * n1 * U;       // [2 n1][U] g slots (VJP only)
+  float* os = gs + (MODE == kRsBwd ? 2 * n1 * U : 0);  // [2 n1][U] out / dx
+  float* yp = os + 2 * n1 * U;       // [8 warps][W2a] dy partials (VJP only)
   // per path: x slot offset, out / g slot offset, y_j offset, y_j dim (16-byte aligned)
   int4* meta = reinterpret_cast<int4*>(
-      ring + ((kRsStages * kRsChunk + 9 * W2a + 6 * n1 * U + 3) & ~3));
+      ring + ((static_cast<int>(yp - ring) + (MODE == kRsBwd ? 8 * W2a : 0) + 3) & ~3));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ql = lane % L;
   const int grp = warp * GW + lane / L;
@@ -170,12 +179,12 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
              bytes, &full[st]);
   };
   if (tid == 0) {
-    for (int st = 0; st < kRsStages; ++st) {
+    for (int st = 0; st < NS; ++st) {
       mbar_init(&full[st], 1);
       done[st] = 0;
     }
     fence_mbarrier_init();
-    for (int st = 0; st < kRsStages && st < nitems; ++st) issue(st, st);
+    for (int st = 0; st < NS && st < nitems; ++st) issue(st, st);
   }
   bool ok = true;
   int64_t it = 0;
@@ -198,11 +207,11 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
     __syncthreads();
     int c = 0, p = 0;
     for (int item = 0; item < per_row; ++item, ++it) {
-      const int st = static_cast<int>(it & (kRsStages - 1));
+      const int st = static_cast<int>(it % NS);
       // c[kc * 4 + a * 2 + b]; in flight while the stage lands
       const float4 ca = __ldg(reinterpret_cast<const float4*>(A.t.coef + 8 * p));
       const float4 cb = __ldg(reinterpret_cast<const float4*>(A.t.coef + 8 * p + 4));
-      ok = mbar_wait(&full[st], static_cast<uint32_t>(it / kRsStages) & 1u, 11);
+      ok = mbar_wait(&full[st], static_cast<uint32_t>(it / NS) & 1u, 11);
       if (!ok) break;
       const int u0 = c * CU;
       const int ncu = U - u0 < CU ? U - u0 : CU;
@@ -224,9 +233,9 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
                      : "=r"(prev)
                      : "r"(smem_addr(&done[st]))
                      : "memory");
-        if (prev + 1 == 8u * static_cast<unsigned>(it / kRsStages + 1)) {
+        if (prev + 1 == 8u * static_cast<unsigned>(it / NS + 1)) {
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          if (it + kRsStages < nitems) issue(it + kRsStages, st);
+          if (it + NS < nitems) issue(it + NS, st);
         }
       }
       const int4 pm = meta[p];
@@ -363,7 +372,7 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
   }
   if (!ok && tid == 0) {
     // a wait ran out: let copies already issued land before the CTA exits
-    for (int st = 0; st < kRsStages; ++st) mbar_wait(&full[st], 0, 12);
+    for (int st = 0; st < NS; ++st) mbar_wait(&full[st], 0, 12);
   }
 }
 
