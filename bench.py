@@ -48,9 +48,15 @@ METRICS = {
     "uvu_rowwise": "fwd+VJP rows/s, UvuTensorProduct C128 V32 m3 full per-row weights, "
                    "16384 rows per GPU",
     "radial": "fwd+VJP edges/s, RadialUvuTensorProduct C64 m3 radial MLP 8-64-64, E=1048576",
+    "radial_m6": "fwd+VJP edges/s, RadialUvuTensorProduct C64 m6 full / angular canonical, "
+                 "radial MLP 16-64-64, E=131072",
 }
 # A100 published fwd+VJP for config 2 (benchmarks/eqx/results/complete_matrix.csv:383)
 A100_TP_ROWS_PER_S = 65536 / 30.087e-3
+# A100 published full VJP of the radial chain C64 m6, N = 131,072 edges
+# (docs/RADIAL_PERFORMANCE.md:9)
+A100_RADIAL_M6_EDGES_PER_S = 131072 / 114.167e-3
+PUBLISHED = {"tp": A100_TP_ROWS_PER_S, "radial_m6": A100_RADIAL_M6_EDGES_PER_S}
 
 
 # ------------------------------------------------------------------ CPU baseline
@@ -80,7 +86,7 @@ def _cpu_worker(task):
         start = time.perf_counter()
         oracle.vjp(x, y, w, g, shared=shared)
     else:
-        uvu = O.UvuOracle(64, 1, 3, "full", "canonical")
+        uvu = O.UvuOracle(64, 1, 6 if workload == "radial_m6" else 3, "full", "canonical")
         radial = O.RadialOracle(uvu)
         x = rng.standard_normal((rows, uvu.width1), dtype=np.float32)
         y = rng.standard_normal((rows, uvu.width2), dtype=np.float32)
@@ -108,14 +114,14 @@ def cpu_units_per_second(workload: str, rows_per_worker: int, steps: int, warmup
             elapsed = max(pool.map(_cpu_worker, tasks))
             if step >= warmup:
                 values.append(rows_per_worker * cores / elapsed)
-    unit = "edges/s" if workload == "radial" else "rows/s"
+    unit = "edges/s" if workload.startswith("radial") else "rows/s"
     return {"value": statistics.median(values), "unit": unit, "cores": cores, "kind": "port",
             "sample": f"{rows_per_worker} rows x {cores} processes per step (float32 numpy "
                       f"oracle of the reference algorithm, {workload} fwd+VJP), median of "
                       f"{steps} steps"}
 
 
-CPU_ROWS = {"tp": 1024, "uvu": 16, "uvu_rowwise": 4, "radial": 256}
+CPU_ROWS = {"tp": 1024, "uvu": 16, "uvu_rowwise": 4, "radial": 256, "radial_m6": 64}
 
 
 # ------------------------------------------------------------------ clocks
@@ -462,8 +468,95 @@ class RadialWorkload(Workload):
         return (3 * 896 + 2 * 7 + 64 * 2) * 4 * self.edges
 
 
+class RadialM6Workload(Workload):
+    """The reference's published radial chain (docs/RADIAL_PERFORMANCE.md:6-12): radial
+    features [N, 16] -> Linear(16,64) -> SiLU -> Linear(64,64) -> SiLU -> fused
+    Linear(64, P*C, bias=False) + V=1 uvu, C64, m_max 6, first input / output full,
+    angular canonical; N = 131,072 edges; the full VJP covers the three inputs and every
+    network parameter."""
+
+    name, scaling, unit = "radial_m6", "strong", "edges/s"
+    EDGES = 131072
+
+    def __init__(self, args, device, rank, world):
+        import torch
+        from ictc_o2_hp_b200 import RadialUvuTensorProduct, UvuTensorProduct, ops
+        from ictc_o2_hp_b200.parallel import shard_bounds
+        self.ops, self.torch, self.world = ops, torch, world
+        total = args.rows or self.EDGES
+        start, stop = shard_bounds(total, world, rank)
+        self.total, self.edges = total, stop - start
+        torch.manual_seed(0)
+        tp = UvuTensorProduct(64, 1, 6, parity="full", parity_in2="canonical",
+                              shared_weights=False)
+        self.trunk = torch.nn.Sequential(torch.nn.Linear(16, 64), torch.nn.SiLU(),
+                                         torch.nn.Linear(64, 64), torch.nn.SiLU()).to(device)
+        self.model = RadialUvuTensorProduct(
+            tp, torch.nn.Linear(64, tp.weight_numel, bias=False)).to(device)
+        gen = torch.Generator(device=device)
+        gen.manual_seed(4000)
+        x = torch.randn(total, tp.input1_dimension, device=device, generator=gen)
+        feat = torch.randn(total, 16, device=device, generator=gen)
+        theta = torch.rand(total, device=device, generator=gen) * 2 * math.pi
+        sl = slice(start, stop)
+        self.x = x[sl].contiguous()
+        self.feat = feat[sl].contiguous()
+        th = theta[sl]
+        self.angular = torch.stack([torch.ones_like(th)] + [
+            f(m * th) for m in range(1, 7) for f in (torch.cos, torch.sin)], dim=-1).contiguous()
+        self.g = torch.ones(self.edges, tp.input1_dimension, device=device)
+        self.units = self.edges
+        self.launches = 6
+        self.params = list(self.trunk.parameters()) + list(self.model.parameters())
+
+    def step(self, x=None, y=None, f=None, g=None):
+        torch = self.torch
+        x = (self.x if x is None else x).detach().requires_grad_(True)
+        ang = (self.angular if y is None else y).detach().requires_grad_(True)
+        feat = (self.feat if f is None else f).detach().requires_grad_(True)
+        out = self.model(x, ang, self.trunk(feat))
+        grads = torch.autograd.grad(out, [x, ang, feat] + self.params,
+                                    self.g if g is None else g)
+        if self.world > 1:
+            flat = torch.cat([t.reshape(-1) for t in grads[3:]])
+            torch.distributed.all_reduce(flat)
+        return out, grads
+
+    def kernels(self, time_op):
+        ops, m = self.ops, self.model
+        torch = self.torch
+        with torch.no_grad():
+            hidden = self.trunk(self.feat).contiguous()
+        alpha = m.radial_out.weight.detach()
+        empty = alpha.new_empty(0)
+        rc = m._rconfig()
+        fwd = time_op(lambda: ops.radial_forward(self.x, self.angular, hidden, alpha, empty,
+                                                 m.tp._table, rc, False))
+        bwd = time_op(lambda: ops.radial_backward(self.x, self.angular, hidden, alpha, empty,
+                                                  self.g, m.tp._table, rc, False, 15))
+        flops = 2 * m.tp.weight_numel * 64 * self.edges  # affine regeneration per edge
+        return {"radial_forward": (fwd, flops), "radial_backward": (bwd, 3 * flops)}, "fp32"
+
+    def host_inputs(self):
+        return (self.x, self.angular, self.feat, self.g)
+
+    def config(self):
+        return {"workload": "reference's published radial chain: radial features [N,16] -> "
+                            "MLP 16-64-64 SiLU -> fused affine (bias=False) + V=1 uvu C64 m6 "
+                            "full / angular canonical m6, forward + full VJP (x, angular, "
+                            "features, every parameter)",
+                "edges_total": self.total, "edges_per_gpu": self.edges,
+                "l2": "inputs larger than L2 (per-edge features 0.9 GB, gw block 8.4 GB)",
+                "parallelism": f"edge shards on {self.world} GPU(s), one NCCL all_reduce of all "
+                               "parameter gradients"}
+
+    def step_bytes(self):
+        w1 = self.x.shape[1]
+        return (3 * w1 + 2 * 13 + 2 * 16 + 64 * 2) * 4 * self.edges
+
+
 WORKLOADS = {"tp": TpWorkload, "uvu": UvuWorkload, "uvu_rowwise": UvuRowWorkload,
-             "radial": RadialWorkload}
+             "radial": RadialWorkload, "radial_m6": RadialM6Workload}
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -601,7 +694,7 @@ def run_gpu(args) -> dict | None:
         "ms_per_step": ms,
         "higher_is_better": True,
         "scaling": wl.scaling,
-        "vs_baseline": value / A100_TP_ROWS_PER_S if wl.name == "tp" else None,
+        "vs_baseline": value / PUBLISHED[wl.name] if wl.name in PUBLISHED else None,
         "dtype": "f32",
         "data": "synthetic (seeded iid N(0,1) inputs, seeded init, ones cotangent)",
         "config": wl.config(),

@@ -69,4 +69,10 @@ inline Mags tp_mags(int normalization) {
   return g;
 }
 
+// Prefetch of the 128-byte line holding p into L1 (a hint; p must be a valid
+// address of the tensor it points into).
+__device__ __forceinline__ void prefetch_l1(const float* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
 }  // namespace ictc

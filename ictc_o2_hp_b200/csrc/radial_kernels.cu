@@ -227,10 +227,6 @@ inline size_t radial_tile_smem(int ut, int H, int W2, int np, int n1, int n2, bo
   return 128 + (aligned_floats + ints) * 4;
 }
 
-__device__ __forceinline__ void prefetch_l1(const float* p) {
-  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
-}
-
 // Loads 4 channels x D values of one entry of one row (zeros past U or rows).
 template <int D>
 __device__ __forceinline__ void load4(float (&v)[4 * D], const float* __restrict__ src,
