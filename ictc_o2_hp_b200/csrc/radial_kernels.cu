@@ -290,7 +290,12 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
   int2* in2 = in1 + A.t.n1;
   int* order = reinterpret_cast<int*>(in2 + A.t.n2);
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * RT;
-  const int ub = blockIdx.y * UT;
+  // Channel tiles: the forward spreads them over blockIdx.y; the dx mode walks them
+  // inside the CTA (dy sums over every channel, so one CTA owns an edge's dy).
+  const int nub = MODE == kRtDx ? (A.U + UT - 1) / UT : 1;
+  auto tile_ub = [&](int T) {
+    return MODE == kRtDx ? (T / (np * nkc)) * UT : static_cast<int>(blockIdx.y) * UT;
+  };
 
   for (int q = tid; q < np; q += kRtThreads) {
     paths[q] = A.t.paths[q];
@@ -311,9 +316,9 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
   }
   if (MODE == kRtDx)
     for (int idx = tid; idx < RT * W2s; idx += kRtThreads) dyacc[idx] = 0.f;
-  // columns of a weight chunk past the copied channels stay zero
-  const int ucopy = A.Up - ub < UT ? A.Up - ub : UT;
-  if (ucopy < UT)
+  // columns of a weight chunk past the copied channels (a partial last channel
+  // tile) hold zeros or finite weights of an earlier tile; the epilogue masks them
+  if (A.Up % UT != 0)
     for (int idx = tid; idx < kRtStages * kc * UT; idx += kRtThreads) Wt[idx] = 0.f;
   if (tid == 0) {
     for (int st = 0; st < kRtStages; ++st) {
@@ -326,12 +331,14 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
 
   const int tc = tid % TC, tr = tid / TC;
   const int e0 = tr * 4;
-  const int ntiles = np * nkc;
+  const int ntiles = nub * np * nkc;
   // One thread copies weight chunk T (rows k0.. of alpha_p, channels ub..) into
   // stage st with bulk asynchronous copies: one copy when the chunk's rows are
   // contiguous (Up == UT), else one per row.
   auto issue = [&](int T, int st) {
-    const int p = order[T / nkc], k0 = (T % nkc) * kRtKC;
+    const int p = order[(T / nkc) % np], k0 = (T % nkc) * kRtKC;
+    const int ub = tile_ub(T);
+    const int ucopy = A.Up - ub < UT ? A.Up - ub : UT;
     const int kn = A.H - k0 < kRtKC ? A.H - k0 : kRtKC;
     float* dst = Wt + st * kc * UT;
     const float* src = A.at + (static_cast<int64_t>(p) * A.H + k0) * A.Up + ub;
@@ -359,7 +366,8 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
     const uint32_t round = static_cast<uint32_t>(T / kRtStages);
     ok = mbar_wait(&full[st], round & 1, 5);
     if (!ok) break;
-    const int pos = T / nkc, ck = T - pos * nkc;
+    const int pos = (T / nkc) % np, ck = T % nkc;
+    const int ub = tile_ub(T);
     const int p = order[pos];
     if (ck == 0) {
 #pragma unroll
@@ -915,8 +923,6 @@ struct RadialConfig {
 int radial_validate(const RadialConfig& c) {
   if (c.U < 1 || c.H < 1) return fail(ICTC_ERR_INVALID, "channels and hidden must be >= 1");
   if (c.M < 0 || c.M2 < 0) return fail(ICTC_ERR_INVALID, "m_max must be >= 0");
-  if (c.U > kUT)
-    return fail(ICTC_ERR_UNSUPPORTED, "radial fusion supports channels <= %d (got %d)", kUT, c.U);
   if (c.M > 32 || c.M2 > 32) return fail(ICTC_ERR_UNSUPPORTED, "m_max above 32");
   return ICTC_OK;
 }
@@ -1130,6 +1136,10 @@ extern "C" int32_t ictc_o2_radial_backward(
                      grad_angular, rows, c.U, Up, c.H, W1, W2, t, tvec};
       st = launch_radial_tile<kRtDx>(ra, s);
       if (st == ICTC_ERR_UNSUPPORTED) {
+        if (c.U > kUT)
+          return fail(ICTC_ERR_UNSUPPORTED,
+                      "radial dx/dy: hidden width %d with more than %d channels does not fit the "
+                      "edge tile", c.H, kUT);
         RowtileArgs rr{grad_output, left, radial_hidden, angular, at, bias, grad_left,
                        grad_angular, rows, c.U, Up, c.H, W1, c.H, W2, t};
         st = launch_rowtile<kRadDx>(rr, s);
@@ -1158,6 +1168,10 @@ extern "C" int32_t ictc_o2_radial_backward(
         ra.Wn = Wn;
         st = launch_radial_tile<kRtDx>(ra, s);
         if (st == ICTC_ERR_UNSUPPORTED) {  // hidden tile too large: row tile, gw separately
+          if (c.U > kUT)
+            return fail(ICTC_ERR_UNSUPPORTED,
+                        "radial dx/dy: hidden width %d with more than %d channels does not fit "
+                        "the edge tile", c.H, kUT);
           RowtileArgs rr{grad_output + r0 * W1, left + r0 * W1, radial_hidden + r0 * c.H,
                          angular + r0 * W2, at, bias, grad_left + r0 * W1,
                          grad_angular + r0 * W2, nb, c.U, Up, c.H, W1, c.H, W2, t};

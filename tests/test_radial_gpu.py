@@ -60,6 +60,8 @@ def test_golden(name, cuda_device):
     (16, 5, 12, True, 45),     # second input wider than 8 values
     (72, 2, 64, False, 130),   # two channel tiles in the weight gradient
     (32, 2, 512, True, 150),   # hidden too wide to stay resident: row-tile fallback
+    (160, 2, 24, True, 70),    # two channel tiles, the last one partial
+    (256, 1, 16, False, 50),   # two full channel tiles
 ])
 def test_against_oracle(u, m_max, hidden, bias, rows, cuda_device):
     oracle_tp = O.UvuOracle(u, 1, m_max, "full", "canonical")
