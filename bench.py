@@ -48,22 +48,21 @@ METRICS = {
     "uvu_rowwise": "fwd+VJP rows/s, UvuTensorProduct C128 V32 m3 full per-row weights, "
                    "16384 rows per GPU",
     "radial": "fwd+VJP edges/s, RadialUvuTensorProduct C64 m3 radial MLP 8-64-64, E=1048576",
-    "radial_m6": "fwd+VJP edges/s, RadialUvuTensorProduct C64 m6 full / angular canonical, "
-                 "radial MLP 16-64-64, E=131072",
+    "radial_m6": "fwd+VJP edges/s, RadialUvuTensorProduct C{channels} m6 full / angular "
+                 "canonical, radial MLP 16-64-64, E=131072",
 }
 # A100 published fwd+VJP for config 2 (benchmarks/eqx/results/complete_matrix.csv:383)
 A100_TP_ROWS_PER_S = 65536 / 30.087e-3
-# A100 published full VJP of the radial chain C64 m6, N = 131,072 edges
-# (docs/RADIAL_PERFORMANCE.md:9)
-A100_RADIAL_M6_EDGES_PER_S = 131072 / 114.167e-3
-PUBLISHED = {"tp": A100_TP_ROWS_PER_S, "radial_m6": A100_RADIAL_M6_EDGES_PER_S}
+# A100 published full VJP of the radial chain m6, N = 131,072 edges, by channel count
+# (docs/RADIAL_PERFORMANCE.md:9, :59, :15)
+A100_RADIAL_M6_MS = {64: 114.167, 128: 208.039, 256: 410.604}
 
 
 # ------------------------------------------------------------------ CPU baseline
 
 def _cpu_worker(task):
     """Oracle fwd + VJP (float32) on `rows` seeded rows of a workload; returns s."""
-    workload, rows, seed = task
+    workload, rows, seed, channels = task
     import numpy as np
     from oracle import o2_oracle as O
     rng = np.random.default_rng(seed)
@@ -86,7 +85,8 @@ def _cpu_worker(task):
         start = time.perf_counter()
         oracle.vjp(x, y, w, g, shared=shared)
     else:
-        uvu = O.UvuOracle(64, 1, 6 if workload == "radial_m6" else 3, "full", "canonical")
+        uvu = O.UvuOracle(channels if workload == "radial_m6" else 64, 1,
+                          6 if workload == "radial_m6" else 3, "full", "canonical")
         radial = O.RadialOracle(uvu)
         x = rng.standard_normal((rows, uvu.width1), dtype=np.float32)
         y = rng.standard_normal((rows, uvu.width2), dtype=np.float32)
@@ -102,7 +102,8 @@ def _pin_single_thread():
     os.environ["OMP_NUM_THREADS"] = "1"
 
 
-def cpu_units_per_second(workload: str, rows_per_worker: int, steps: int, warmup: int) -> dict:
+def cpu_units_per_second(workload: str, rows_per_worker: int, steps: int, warmup: int,
+                         channels: int = 64) -> dict:
     """Times the CPU oracle on all host cores (one spawned process per core)."""
     import multiprocessing as mp
     cores = os.cpu_count() or 1
@@ -110,7 +111,7 @@ def cpu_units_per_second(workload: str, rows_per_worker: int, steps: int, warmup
     values = []
     with ctx.Pool(cores, initializer=_pin_single_thread) as pool:
         for step in range(warmup + steps):
-            tasks = [(workload, rows_per_worker, 1000 * step + i) for i in range(cores)]
+            tasks = [(workload, rows_per_worker, 1000 * step + i, channels) for i in range(cores)]
             elapsed = max(pool.map(_cpu_worker, tasks))
             if step >= warmup:
                 values.append(rows_per_worker * cores / elapsed)
@@ -478,6 +479,11 @@ class RadialM6Workload(Workload):
     name, scaling, unit = "radial_m6", "strong", "edges/s"
     EDGES = 131072
 
+    @staticmethod
+    def published(args):
+        ms = A100_RADIAL_M6_MS.get(args.channels)
+        return None if ms is None or (args.rows or 131072) != 131072 else 131072 / (ms * 1e-3)
+
     def __init__(self, args, device, rank, world):
         import torch
         from ictc_o2_hp_b200 import RadialUvuTensorProduct, UvuTensorProduct, ops
@@ -487,7 +493,8 @@ class RadialM6Workload(Workload):
         start, stop = shard_bounds(total, world, rank)
         self.total, self.edges = total, stop - start
         torch.manual_seed(0)
-        tp = UvuTensorProduct(64, 1, 6, parity="full", parity_in2="canonical",
+        self.channels = args.channels
+        tp = UvuTensorProduct(self.channels, 1, 6, parity="full", parity_in2="canonical",
                               shared_weights=False)
         self.trunk = torch.nn.Sequential(torch.nn.Linear(16, 64), torch.nn.SiLU(),
                                          torch.nn.Linear(64, 64), torch.nn.SiLU()).to(device)
@@ -542,9 +549,10 @@ class RadialM6Workload(Workload):
 
     def config(self):
         return {"workload": "reference's published radial chain: radial features [N,16] -> "
-                            "MLP 16-64-64 SiLU -> fused affine (bias=False) + V=1 uvu C64 m6 "
-                            "full / angular canonical m6, forward + full VJP (x, angular, "
-                            "features, every parameter)",
+                            f"MLP 16-64-64 SiLU -> fused affine (bias=False) + V=1 uvu "
+                            f"C{self.channels} m6 full / angular canonical m6, forward + full "
+                            "VJP (x, angular, features, every parameter)",
+                "channels": self.channels,
                 "edges_total": self.total, "edges_per_gpu": self.edges,
                 "l2": "inputs larger than L2 (per-edge features 0.9 GB, gw block 8.4 GB)",
                 "parallelism": f"edge shards on {self.world} GPU(s), one NCCL all_reduce of all "
@@ -685,7 +693,7 @@ def run_gpu(args) -> dict | None:
     total_units = wl.units * world if wl.scaling == "weak" else wl.total
     value = total_units / (ms * 1e-3)
     result = {
-        "metric": METRICS[wl.name],
+        "metric": METRICS[wl.name].format(channels=args.channels),
         "value": value,
         "unit": wl.unit,
         "n_gpus": world,
@@ -694,7 +702,7 @@ def run_gpu(args) -> dict | None:
         "ms_per_step": ms,
         "higher_is_better": True,
         "scaling": wl.scaling,
-        "vs_baseline": value / PUBLISHED[wl.name] if wl.name in PUBLISHED else None,
+        "vs_baseline": vs_baseline(wl, args, value),
         "dtype": "f32",
         "data": "synthetic (seeded iid N(0,1) inputs, seeded init, ones cotangent)",
         "config": wl.config(),
@@ -717,6 +725,17 @@ def run_gpu(args) -> dict | None:
 TRAFFIC = {"tp_backward": 4.252e9, "tp_forward": 2.498e9}
 
 
+def vs_baseline(wl, args, value):
+    """value / the reference's published number for this exact metric and config."""
+    if hasattr(wl, "published"):
+        ref = wl.published(args)
+    elif wl.name == "tp" and args.rows in (0, 65536):
+        ref = A100_TP_ROWS_PER_S
+    else:
+        ref = None
+    return value / ref if ref else None
+
+
 def _leaves(value):
     import torch
     if isinstance(value, torch.Tensor):
@@ -732,10 +751,12 @@ def run_reference(args) -> dict | None:
     if int(os.environ.get("RANK", "0")) != 0:
         return None
     rows = args.cpu_rows or CPU_ROWS[args.workload]
-    base = cpu_units_per_second(args.workload, rows, args.steps, max(1, min(args.warmup, 1)))
+    base = cpu_units_per_second(args.workload, rows, args.steps, max(1, min(args.warmup, 1)),
+                                args.channels)
     value = base["value"]
     return {
-        "metric": METRICS[args.workload], "impl": "reference", "value": value,
+        "metric": METRICS[args.workload].format(channels=args.channels), "impl": "reference",
+        "value": value,
         "unit": base["unit"], "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": rows * base["cores"] / value * 1e3, "higher_is_better": True,
@@ -760,6 +781,8 @@ def main(argv=None) -> int:
     parser.add_argument("--workload", choices=tuple(WORKLOADS), default="tp")
     parser.add_argument("--rows", type=int, default=0,
                         help="rows per GPU (tp, uvu) or total edges (radial); 0 = config")
+    parser.add_argument("--channels", type=int, default=64,
+                        help="radial_m6: channels C of the published chain (64, 128, 256)")
     parser.add_argument("--cpu-rows", type=int, default=0,
                         help="rows per host core per CPU-baseline step; 0 = default")
     parser.add_argument("--no-e2e", action="store_true")
@@ -779,7 +802,8 @@ def main(argv=None) -> int:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         # The process pool starts before the first CUDA call (spawned workers).
-        cpu = cpu_units_per_second(args.workload, args.cpu_rows or CPU_ROWS[args.workload], 3, 1)
+        cpu = cpu_units_per_second(args.workload, args.cpu_rows or CPU_ROWS[args.workload], 3, 1,
+                                   args.channels)
     result = run_gpu(args)
     if result is not None:
         if cpu is not None:

@@ -42,17 +42,29 @@ UvuDev radial_dev(const void* table, const UvuLayout& l) {
 }
 
 // at[p][h][u] (u padded to Up) <- alpha[p*U + u][h]
+// alpha [P * U, H] -> at [P][nt][H][TW]: channel tiles of width TW, zero past U.
+// nt = 1, TW = Up is the plain [P][H][Up] layout of the row tile; the edge tile
+// takes TW = its channel tile so each weight chunk is one contiguous copy.
 __global__ void transpose_alpha(const float* __restrict__ a, float* __restrict__ at, int P, int U,
-                                int Up, int H) {
-  const int64_t total = static_cast<int64_t>(P) * H * Up;
+                                int TW, int nt, int H) {
+  const int64_t total = static_cast<int64_t>(P) * nt * H * TW;
   for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int u = static_cast<int>(idx % Up);
-    const int64_t ph = idx / Up;
-    const int h = static_cast<int>(ph % H);
-    const int64_t p = ph / H;
+    const int c = static_cast<int>(idx % TW);
+    const int64_t rest = idx / TW;
+    const int h = static_cast<int>(rest % H);
+    const int64_t pt = rest / H;
+    const int u = static_cast<int>(pt % nt) * TW + c;
+    const int64_t p = pt / nt;
     at[idx] = u < U ? a[(p * U + u) * H + h] : 0.0f;
   }
+}
+
+// Channel tile of the edge tile kernel and the transposed-alpha width it needs.
+inline int radial_ut(int U) { return U <= 64 ? 64 : 128; }
+inline int radial_tiles(int U) { return (U + radial_ut(U) - 1) / radial_ut(U); }
+inline size_t radial_at_bytes(int64_t P, int U, int H) {
+  return static_cast<size_t>(P) * H * radial_tiles(U) * radial_ut(U) * sizeof(float);
 }
 
 // ------------------------------------------------------------ edge-weight gradient
@@ -316,10 +328,6 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
   }
   if (MODE == kRtDx)
     for (int idx = tid; idx < RT * W2s; idx += kRtThreads) dyacc[idx] = 0.f;
-  // columns of a weight chunk past the copied channels (a partial last channel
-  // tile) hold zeros or finite weights of an earlier tile; the epilogue masks them
-  if (A.Up % UT != 0)
-    for (int idx = tid; idx < kRtStages * kc * UT; idx += kRtThreads) Wt[idx] = 0.f;
   if (tid == 0) {
     for (int st = 0; st < kRtStages; ++st) {
       mbar_init(&full[st], 1);
@@ -332,23 +340,19 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
   const int tc = tid % TC, tr = tid / TC;
   const int e0 = tr * 4;
   const int ntiles = nub * np * nkc;
-  // One thread copies weight chunk T (rows k0.. of alpha_p, channels ub..) into
-  // stage st with bulk asynchronous copies: one copy when the chunk's rows are
-  // contiguous (Up == UT), else one per row.
+  // One thread copies weight chunk T (rows k0.. of alpha_p, channel tile ub / UT)
+  // into stage st: alpha is laid out [P][channel tiles][H][UT] (zero past U), so a
+  // chunk is one contiguous bulk asynchronous copy.
+  const int ntl = (A.U + UT - 1) / UT;
   auto issue = [&](int T, int st) {
     const int p = order[(T / nkc) % np], k0 = (T % nkc) * kRtKC;
-    const int ub = tile_ub(T);
-    const int ucopy = A.Up - ub < UT ? A.Up - ub : UT;
     const int kn = A.H - k0 < kRtKC ? A.H - k0 : kRtKC;
     float* dst = Wt + st * kc * UT;
-    const float* src = A.at + (static_cast<int64_t>(p) * A.H + k0) * A.Up + ub;
-    const uint32_t row_bytes = static_cast<uint32_t>(ucopy) * 4u;
-    mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(kn) * row_bytes);
-    if (ucopy == UT && A.Up == UT) {
-      bulk_g2s(dst, src, static_cast<uint32_t>(kn) * row_bytes, &full[st]);
-    } else {
-      for (int k = 0; k < kn; ++k) bulk_g2s(dst + k * UT, src + k * A.Up, row_bytes, &full[st]);
-    }
+    const float* src =
+        A.at + ((static_cast<int64_t>(p) * ntl + tile_ub(T) / UT) * A.H + k0) * UT;
+    const uint32_t bytes = static_cast<uint32_t>(kn) * UT * 4u;
+    mbar_arrive_expect_tx(&full[st], bytes);
+    bulk_g2s(dst, src, bytes, &full[st]);
   };
 
   float acc[4][8];
@@ -569,9 +573,15 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
   }
 }
 
+// Whether the edge tile's shared memory (resident hidden tile, weight ring, path
+// metadata) fits; otherwise the row tile runs, on the [P][H][Up] alpha layout.
+inline bool radial_tile_fits(int U, int H, int W2, int np, int n1, int n2, bool dx) {
+  return radial_tile_smem(radial_ut(U), H, W2, np, n1, n2, dx) <= 225 * 1024;
+}
+
 template <int MODE>
 int launch_radial_tile(const RadTileArgs& ra, cudaStream_t s) {
-  const int ut = ra.U <= 64 ? 64 : 128;
+  const int ut = radial_ut(ra.U);
   const size_t smem = radial_tile_smem(ut, ra.H, ra.W2, ra.t.np, ra.t.n1, ra.t.n2, MODE == kRtDx);
   if (smem > 225 * 1024) return ICTC_ERR_UNSUPPORTED;  // caller falls back to the row tile
   const void* fn = ut == 64 ? reinterpret_cast<const void*>(&radial_tile<MODE, 64>)
@@ -1012,8 +1022,7 @@ extern "C" int32_t ictc_o2_radial_workspace(ICTC_RADIAL_ARGS, int64_t rows, int3
   const UvuTableH th = build_uvu_table(c.U, 1, c.M, c.full1, c.M2, c.full2, c.component,
                                        path_normalization != 0);
   const int64_t P = static_cast<int64_t>(th.paths.size());
-  const int Up = (c.U + 3) & ~3;
-  const size_t at = static_cast<size_t>(P) * c.H * Up * sizeof(float);
+  const size_t at = radial_at_bytes(P, c.U, c.H);
   if (rows <= 0) {
     *forward_bytes = 0;
     *backward_bytes = 0;
@@ -1047,13 +1056,18 @@ extern "C" int32_t ictc_o2_radial_forward(const float* left, const float* angula
   if (!left || !angular || !radial_hidden || !alpha || !output)
     return fail(ICTC_ERR_INVALID, "null tensor pointer");
   const int Up = (c.U + 3) & ~3;
-  const size_t need = static_cast<size_t>(l.np) * c.H * Up * sizeof(float);
+  const size_t need = radial_at_bytes(l.np, c.U, c.H);
   if (workspace_bytes < need || !workspace || !aligned(workspace, 16))
     return fail(ICTC_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu (16-byte aligned)",
                 workspace_bytes, need);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   float* at = static_cast<float*>(workspace);
-  transpose_alpha<<<1024, 256, 0, s>>>(alpha, at, l.np, c.U, Up, c.H);
+  const bool tile = radial_tile_fits(c.U, c.H, th.width2, l.np, l.n1, l.n2, false);
+  if (tile)
+    transpose_alpha<<<1024, 256, 0, s>>>(alpha, at, l.np, c.U, radial_ut(c.U),
+                                         radial_tiles(c.U), c.H);
+  else
+    transpose_alpha<<<1024, 256, 0, s>>>(alpha, at, l.np, c.U, Up, 1, c.H);
   const UvuDev t = radial_dev(device_table, l);
   const bool vec = (th.width1 % 4 == 0) && (c.U % 4 == 0) && aligned(left, 16) &&
                    aligned(output, 16);
@@ -1106,7 +1120,7 @@ extern "C" int32_t ictc_o2_radial_backward(
   e = cudaGetDevice(&device);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   const int Up = (c.U + 3) & ~3;
-  const size_t at_bytes = static_cast<size_t>(l.np) * c.H * Up * sizeof(float);
+  const size_t at_bytes = radial_at_bytes(l.np, c.U, c.H);
   const int64_t chunks = radial_chunks(device, rows, l.np, c.U, c.H);
   const size_t part_bytes =
       chunks > 1 ? static_cast<size_t>(chunks) * (Wn * c.H + Wn) * sizeof(float) : 0;
@@ -1126,7 +1140,11 @@ extern "C" int32_t ictc_o2_radial_backward(
                     aligned(grad_output, 16) && aligned(grad_left, 16);
   if (needed & 3) {
     // dx and dy together: both need the regenerated edge weights
-    transpose_alpha<<<1024, 256, 0, s>>>(alpha, at, l.np, c.U, Up, c.H);
+    if (radial_tile_fits(c.U, c.H, W2, l.np, l.n1, l.n2, true))
+      transpose_alpha<<<1024, 256, 0, s>>>(alpha, at, l.np, c.U, radial_ut(c.U),
+                                           radial_tiles(c.U), c.H);
+    else
+      transpose_alpha<<<1024, 256, 0, s>>>(alpha, at, l.np, c.U, Up, 1, c.H);
     // scratch outputs when only one of dx / dy is requested are not allowed to
     // alias inputs; the caller passes both buffers (see the Python wrapper)
     if (!grad_left || !grad_angular)
