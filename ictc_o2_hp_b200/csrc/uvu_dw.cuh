@@ -4,7 +4,8 @@
 //   s_p[r,u,b] = sum_{kc,a} c_p[kc][a][b] g_k[r,u,kc] x_i[r,u,a]
 //
 // A CTA (256 threads) owns one path and one chunk of rows.  It walks the rows in
-// steps of 32: the slices x_i, g_k [32 rows][U d] and y_j [32 rows][V d2] arrive
+// steps of 16 (about 95 KB of shared memory, two CTAs per SM): the slices x_i,
+// g_k [16 rows][U d] and y_j [16 rows][V d2] arrive
 // by cp.async one step ahead (double buffer); s is built from shared memory into
 // S[(row, b)][u] and y into Y[(row, b)][v]; then the GEMM over K = (row, b)
 // accumulates dw_p (4 u x 4 v per thread).  Chunks are summed in a fixed order
@@ -13,7 +14,7 @@
 // This header is included inside the anonymous namespace of uvu_kernels.cu.
 #pragma once
 
-constexpr int kDwRows = 32;
+constexpr int kDwRows = 16;
 constexpr int kDwU = 128;
 constexpr int kDwV = 32;
 constexpr int kDwLdS = kDwU + 4;  // S row stride (floats)
@@ -82,7 +83,7 @@ __global__ void __launch_bounds__(256, 1) uvu_dw_stage(DwArgs A) {
   for (int q = tid; q < 2 * kDwRows * kDwV * 2; q += 256) (&S.ys[0][0][0])[q] = 0.f;
   __syncthreads();
   issue(0, 0);
-  // generation: channel gu, rows gh*16 .. +15; y: (row, b) gr, v quad gv
+  // generation: channel gu, rows gh * kDwRows / 2 .. +kDwRows / 2 - 1; y: (row, b) gr, v quad gv
   const int gu = tid & 127, gh = tid >> 7;
   // GEMM: u quad uq (0..31), v quad vq (0..7)
   const int uq = tid >> 3, vq = tid & 7;
@@ -97,8 +98,8 @@ __global__ void __launch_bounds__(256, 1) uvu_dw_stage(DwArgs A) {
     __syncthreads();  // slices of step visible; previous GEMM done with S and Y
     issue(step + 1, buf ^ 1);
 #pragma unroll 4
-    for (int rr = 0; rr < 16; ++rr) {
-      const int r = gh * 16 + rr;
+    for (int rr = 0; rr < kDwRows / 2; ++rr) {
+      const int r = gh * (kDwRows / 2) + rr;
       const float* xr = &S.xs[buf][r][gu * ei.y];
       const float* gr = &S.gs[buf][r][gu * ek.y];
       const float x0 = xr[0], x1 = ei.y == 2 ? xr[1] : 0.f;
