@@ -3,21 +3,22 @@
 //   dy_j[r,v,b] = sum_{p: j_p = j} sum_u w_p[u,v] s_p[r,u,b],
 //   s_p[r,u,b]  = sum_{kc,a} c_p[kc][a][b] g_k[r,u,kc] x_i[r,u,a]
 //
-// A CTA (256 threads) owns 32 rows and walks the paths grouped by second entry
-// j.  For each path the slices x_i[32 rows][U d1], g_k[32 rows][U d3] and the
-// weights w_p[U][V] arrive by cp.async one path ahead (double buffer); s_p is
-// built from shared memory into S[u][(row, b)] and then contracted over u
-// (GEMM: 4 (row, b) x 4 v per thread, the u range split in two halves that are
-// summed in a fixed order when the j group ends).  Needs U <= 128, V <= 32 and
+// A CTA (256 threads) owns 16 rows and walks the paths grouped by second entry
+// j.  For each path the slices x_i[16 rows][U d1], g_k[16 rows][U d3] and the
+// weights w_p[U][V] arrive by cp.async one path ahead; s_p is built from shared
+// memory into S[u][(row, b)] and then contracted over u (GEMM: 4 (row, b) x 4 v
+// per thread, the u range split in four quarters that are summed in a fixed
+// order when the j group ends).  Needs U <= 128, V <= 32 and
 // 16-byte aligned rows; other shapes use uvu_dy_tile.
 //
 // This header is included inside the anonymous namespace of uvu_kernels.cu.
 #pragma once
 
-constexpr int kDyRows = 32;
+constexpr int kDyRows = 16;
 constexpr int kDyU = 128;
 constexpr int kDyV = 32;
-constexpr int kDyLd = 2 * kDyRows + 4;  // S row stride (floats): 64 (row, b) + pad
+constexpr int kDyLd = 2 * kDyRows + 4;  // S row stride (floats): 32 (row, b) + pad
+constexpr int kDyKs = 4;                // u range split over thread quarters
 
 struct DyArgs {
   const float* x; const float* g; const float* w; float* dy;
@@ -26,9 +27,12 @@ struct DyArgs {
   UvuDev t;
 };
 
+// About 82 KB: two CTAs per SM.  x / g slices are single-buffered (the next path's
+// slices are copied while this path's GEMM runs, after S has been built from
+// them); the weights are double-buffered.
 struct DySmem {
-  float xs[2][kDyRows][kDyU * 2];
-  float gs[2][kDyRows][kDyU * 2];
+  float xs[kDyRows][kDyU * 2];
+  float gs[kDyRows][kDyU * 2];
   float wp[2][kDyU][kDyV];
   float S[kDyU][kDyLd];
 };
@@ -44,15 +48,15 @@ __device__ __forceinline__ void dy_cp16(void* smem, const void* gmem, bool valid
                : "memory");
 }
 
-__global__ void __launch_bounds__(256, 1) uvu_dy_stage(DyArgs A) {
+__global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
   extern __shared__ __align__(16) unsigned char dy_raw[];
   DySmem& S = *reinterpret_cast<DySmem*>(dy_raw);
   const int tid = threadIdx.x;
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kDyRows;
   const int nvalid = A.rows - row0 < kDyRows ? static_cast<int>(A.rows - row0) : kDyRows;
   const int np = A.t.np;
-  // operand slices of path position pos into buffer buf (zero-filled past the rows)
-  auto issue = [&](int pos, int buf) {
+  // x / g slices of path position pos (zero-filled past the rows)
+  auto issue_xg = [&](int pos) {
     if (pos < np) {
       const int p = A.t.by_j[pos];
       const int4 pt = A.t.paths[p];
@@ -61,13 +65,19 @@ __global__ void __launch_bounds__(256, 1) uvu_dy_stage(DyArgs A) {
       for (int q = tid; q < kDyRows * nx; q += 256) {
         const int r = q / nx, c = q - r * nx;
         const bool ok = r < nvalid;
-        dy_cp16(&S.xs[buf][r][c * 4], ok ? A.x + (row0 + r) * A.W1 + ei.x + c * 4 : A.x, ok);
+        dy_cp16(&S.xs[r][c * 4], ok ? A.x + (row0 + r) * A.W1 + ei.x + c * 4 : A.x, ok);
       }
       for (int q = tid; q < kDyRows * ng; q += 256) {
         const int r = q / ng, c = q - r * ng;
         const bool ok = r < nvalid;
-        dy_cp16(&S.gs[buf][r][c * 4], ok ? A.g + (row0 + r) * A.W1 + ek.x + c * 4 : A.g, ok);
+        dy_cp16(&S.gs[r][c * 4], ok ? A.g + (row0 + r) * A.W1 + ek.x + c * 4 : A.g, ok);
       }
+    }
+  };
+  // weights w_p [U][V] of path position pos into buffer buf
+  auto issue_w = [&](int pos, int buf) {
+    if (pos < np) {
+      const int p = A.t.by_j[pos];
       const int nw = A.U * A.V / 4;
       const float* wsrc = A.w + static_cast<int64_t>(p) * A.U * A.V;
       for (int q = tid; q < nw; q += 256) {
@@ -75,20 +85,22 @@ __global__ void __launch_bounds__(256, 1) uvu_dy_stage(DyArgs A) {
         dy_cp16(&S.wp[buf][u][v], wsrc + q * 4, true);
       }
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
   };
   // zero the parts of the buffers that copies do not cover (channels >= U, v >= V)
-  for (int q = tid; q < 2 * kDyRows * kDyU * 2; q += 256) {
-    (&S.xs[0][0][0])[q] = 0.f;
-    (&S.gs[0][0][0])[q] = 0.f;
+  for (int q = tid; q < kDyRows * kDyU * 2; q += 256) {
+    (&S.xs[0][0])[q] = 0.f;
+    (&S.gs[0][0])[q] = 0.f;
   }
   for (int q = tid; q < 2 * kDyU * kDyV; q += 256) (&S.wp[0][0][0])[q] = 0.f;
   __syncthreads();
-  issue(0, 0);
-  // generation: channel gu, rows gh*16 .. +15
+  issue_xg(0);
+  issue_w(0, 0);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  // generation: channel gu, rows gh * 8 .. +7
   const int gu = tid & 127, gh = tid >> 7;
-  // GEMM: (row, b) quad rq (0..15), v quad vq (0..7), channel half ug
-  const int ug = tid >> 7, rq = (tid & 127) >> 3, vq = tid & 7;
+  // GEMM: (row, b) quad rq (0..7), v quad vq (0..7), u quarter ug (0..3)
+  const int ug = tid >> 6, rq = (tid & 63) >> 3, vq = tid & 7;
+  constexpr int kUq = kDyU / kDyKs;
   float acc[4][4];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
@@ -97,8 +109,7 @@ __global__ void __launch_bounds__(256, 1) uvu_dy_stage(DyArgs A) {
   for (int pos = 0; pos < np; ++pos) {
     const int buf = pos & 1;
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();  // slices of pos visible; previous GEMM done with S and buffer buf ^ 1
-    issue(pos + 1, buf ^ 1);
+    __syncthreads();  // slices of pos visible; previous GEMM done with S and wp[buf ^ 1]
     const int p = A.t.by_j[pos];
     const int4 pt = A.t.paths[p];
     const int2 ei = A.t.in1[pt.x], ej = A.t.in2[pt.y], ek = A.t.in1[pt.z];
@@ -107,22 +118,24 @@ __global__ void __launch_bounds__(256, 1) uvu_dy_stage(DyArgs A) {
     for (int e = 0; e < 8; ++e) c[e] = __ldg(A.t.coef + 8 * p + e);
     // s[b] = sum_{kc,a} c[4 kc + 2 a + b] g[kc] x[a]
 #pragma unroll 4
-    for (int rr = 0; rr < 16; ++rr) {
-      const int r = gh * 16 + rr;
-      const float* xr = &S.xs[buf][r][gu * ei.y];
-      const float* gr = &S.gs[buf][r][gu * ek.y];
+    for (int rr = 0; rr < kDyRows / 2; ++rr) {
+      const int r = gh * (kDyRows / 2) + rr;
+      const float* xr = &S.xs[r][gu * ei.y];
+      const float* gr = &S.gs[r][gu * ek.y];
       const float x0 = xr[0], x1 = ei.y == 2 ? xr[1] : 0.f;
       const float g0 = gr[0], g1 = ek.y == 2 ? gr[1] : 0.f;
       const float s0 = g0 * fmaf(c[2], x1, c[0] * x0) + g1 * fmaf(c[6], x1, c[4] * x0);
       const float s1 = g0 * fmaf(c[3], x1, c[1] * x0) + g1 * fmaf(c[7], x1, c[5] * x0);
-      S.S[gu][2 * r] = s0;
-      S.S[gu][2 * r + 1] = s1;
+      *reinterpret_cast<float2*>(&S.S[gu][2 * r]) = make_float2(s0, s1);
     }
-    __syncthreads();
-    // dy[(r,b)][v] += sum_u S[u][(r,b)] w[u][v] over this thread's channel half
-    const int ubeg = ug * 64;
+    __syncthreads();  // S built; x / g free for the next path
+    issue_xg(pos + 1);
+    issue_w(pos + 1, buf ^ 1);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    // dy[(r,b)][v] += sum_u S[u][(r,b)] w[u][v] over this thread's channel quarter
+    const int ubeg = ug * kUq;
 #pragma unroll 8
-    for (int uu = 0; uu < 64; ++uu) {
+    for (int uu = 0; uu < kUq; ++uu) {
       const int u = ubeg + uu;
       const float4 a4 = *reinterpret_cast<const float4*>(&S.S[u][rq * 4]);
       const float4 b4 = *reinterpret_cast<const float4*>(&S.wp[buf][u][vq * 4]);
@@ -135,14 +148,14 @@ __global__ void __launch_bounds__(256, 1) uvu_dy_stage(DyArgs A) {
     }
     const bool last = pos + 1 == np || A.t.paths[A.t.by_j[pos + 1]].y != pt.y;
     if (last) {
-      // sum the two channel halves in order: half 1 parks its sums, half 0 adds
+      // sum the channel quarters in order: quarters 1..3 park their sums, 0 adds
       __syncthreads();  // every thread is done reading S
-      float* red = &S.S[0][0];  // [128 threads][16]
-      if (ug == 1) {
+      float* red = &S.S[0][0];  // [3 quarters][64 threads][16]
+      if (ug > 0) {
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int k = 0; k < 4; ++k) red[(tid & 127) * 16 + i * 4 + k] = acc[i][k];
+          for (int k = 0; k < 4; ++k) red[((ug - 1) * 64 + (tid & 63)) * 16 + i * 4 + k] = acc[i][k];
       }
       __syncthreads();
       if (ug == 0) {
@@ -155,9 +168,10 @@ __global__ void __launch_bounds__(256, 1) uvu_dy_stage(DyArgs A) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const int v = vq * 4 + k;
-              if (v < A.V)
-                A.dy[row * A.W2 + ej.x + v * ej.y + b] =
-                    acc[i][k] + red[(tid & 127) * 16 + i * 4 + k];
+              float sum = acc[i][k];
+#pragma unroll
+              for (int q = 0; q < kDyKs - 1; ++q) sum += red[(q * 64 + tid) * 16 + i * 4 + k];
+              if (v < A.V) A.dy[row * A.W2 + ej.x + v * ej.y + b] = sum;
             }
           }
         }
