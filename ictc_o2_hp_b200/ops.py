@@ -96,8 +96,9 @@ tp_forward.register_autograd(_tp_autograd, setup_context=_tp_setup)
 
 
 def torch_tp_flat(left: Tensor, right: Tensor, weight: Tensor, plan: TpPlan) -> Tensor:
-    """Differentiable PyTorch formula of the same map, used for second derivatives
-    only (the role of triton_o2.py:969-1032)."""
+    """Differentiable PyTorch formula of the same map (the role of
+    triton_o2.py:969-1032); run in float64 on the CPU it is the reference the
+    second-derivative tests check the kernels against."""
     n, C = left.shape[0], plan.channels
     offsets = plan.key_offsets()
     mags = MAGNITUDES[plan.normalization]
@@ -145,21 +146,48 @@ def _tp_backward_setup(ctx, inputs, output):
     ctx.set_materialize_grads(False)
 
 
+def _accumulate(total, term):
+    return term if total is None else total + term
+
+
 def _tp_double_backward(ctx, dd_left, dd_right, dd_weight):
+    """Second derivatives through the same kernels (the reference recomputes them in
+    PyTorch, triton_o2.py:1041-1069).  With B(x, y; w) the trilinear map and
+    dx = B_x^T(g; y, w), dy = B_y^T(g; x, w), dw = B_w^T(g; x, y), the cotangents
+    (ddx, ddy, ddw) contract to <B(ddx, y; w) + B(x, ddy; w) + B(x, y; ddw), g>, so
+      d left   = B_x^T(g; ddy, w) + B_x^T(g; y, ddw)
+      d right  = B_y^T(g; ddx, w) + B_y^T(g; x, ddw)
+      d weight = B_w^T(g; ddx, y) + B_w^T(g; x, ddy)
+      d g      = B(ddx, y; w) + B(x, ddy; w) + B(x, y; ddw):
+    three backward calls (operands swapped in) and up to three forward calls."""
     left, right, weight, grad_output = ctx.saved_tensors
-    selected = [(i, c) for i, c in enumerate((dd_left, dd_right, dd_weight)) if c is not None]
-    if not selected:
-        return (None,) * 8
-    plan = tp_plan(*ctx.config)
-    with torch.enable_grad():
-        operands = tuple(v.detach().requires_grad_(True)
-                         for v in (left, right, weight, grad_output))
-        value = torch_tp_flat(*operands[:3], plan)
-        first = torch.autograd.grad(value, operands[:3], operands[3], create_graph=True)
-        second = torch.autograd.grad(tuple(first[i] for i, _ in selected), operands,
-                                     grad_outputs=tuple(c for _, c in selected),
-                                     allow_unused=True)
-    return (*second, None, None, None, None)
+    cfg = ctx.config
+    need_x, need_y, need_w, need_g = ctx.needs_input_grad[:4]
+    d_left = d_right = d_weight = d_g = None
+    if dd_left is not None and (need_y or need_w):
+        _, gy, gw = tp_backward(dd_left, right, weight, grad_output, *cfg)
+        d_right = gy if need_y else None
+        d_weight = gw if need_w else None
+    if dd_right is not None and (need_x or need_w):
+        gx, _, gw = tp_backward(left, dd_right, weight, grad_output, *cfg)
+        if need_x:
+            d_left = _accumulate(d_left, gx)
+        if need_w:
+            d_weight = _accumulate(d_weight, gw)
+    if dd_weight is not None and (need_x or need_y):
+        gx, gy, _ = tp_backward(left, right, dd_weight, grad_output, *cfg)
+        if need_x:
+            d_left = _accumulate(d_left, gx)
+        if need_y:
+            d_right = _accumulate(d_right, gy)
+    if need_g:
+        if dd_left is not None:
+            d_g = _accumulate(d_g, tp_forward(dd_left, right, weight, *cfg))
+        if dd_right is not None:
+            d_g = _accumulate(d_g, tp_forward(left, dd_right, weight, *cfg))
+        if dd_weight is not None:
+            d_g = _accumulate(d_g, tp_forward(left, right, dd_weight, *cfg))
+    return d_left, d_right, d_weight, d_g, None, None, None, None
 
 
 tp_backward.register_autograd(_tp_double_backward, setup_context=_tp_backward_setup)
@@ -240,7 +268,8 @@ def torch_uvu_flat(left: Tensor, right: Tensor, weight: Tensor, entries_in1, ent
                    paths, coefficients: Tensor, channels: int, channels_in2: int,
                    shared: bool) -> Tensor:
     """Differentiable PyTorch formula of the uvu map (the role of the reference's
-    torch_uvu_forward, uvu_o2.py:50-73); used for second derivatives only."""
+    torch_uvu_forward, uvu_o2.py:50-73); run in float64 on the CPU it is the
+    reference the second-derivative tests check the kernels against."""
     rows = left.shape[0]
     values = [None] * len(entries_in1)
     for p, (i, j, k) in enumerate(paths):
@@ -349,3 +378,54 @@ def _radial_autograd(ctx, grad_output):
 
 
 radial_forward.register_autograd(_radial_autograd, setup_context=_radial_setup)
+
+
+def _radial_backward_setup(ctx, inputs, output):
+    left, angular, hidden, alpha, bias, grad_output, table, rconfig, has_bias, needed = inputs
+    ctx.save_for_backward(left, angular, hidden, alpha, bias, grad_output, table)
+    ctx.rconfig, ctx.has_bias = rconfig, has_bias
+    ctx.set_materialize_grads(False)
+
+
+def _radial_double_backward(ctx, d_left, d_angular, d_hidden, d_alpha, d_bias):
+    """Second derivatives through the same kernels (reference
+    radial_streamed.py:173-207).  With out = F(x, y, r, a) + G(x, y, b) (F the
+    product with the regenerated weights r a^T, G the one with the bias), each
+    cotangent contracts with its gradient to <product with that operand swapped in,
+    g>: <dx, gx> = <out(dx, y, r, a, b), g>, <dr, gr> = <F(x, y, dr, a), g>,
+    <da, ga> + <db, gb> = <out(x, y, r, da, db), g>.  Each term is one role-masked
+    backward call for the other operands and one forward call for g."""
+    left, angular, hidden, alpha, bias, grad_output, table = ctx.saved_tensors
+    need = list(ctx.needs_input_grad[:6])
+    if not ctx.has_bias:
+        need[4] = False
+    acc = [None] * 6
+    empty = alpha.new_empty(0)
+
+    def add(operands, roles, has_bias):
+        selected = [r for r in roles if need[r] and (r != 4 or has_bias)]
+        if selected:
+            mask = sum(1 << r for r in selected)
+            grads = radial_backward(*operands, grad_output, table, ctx.rconfig, has_bias, mask)
+            for r in selected:
+                acc[r] = grads[r] if acc[r] is None else acc[r] + grads[r]
+        if need[5]:
+            value = radial_forward(*operands, table, ctx.rconfig, has_bias)
+            acc[5] = value if acc[5] is None else acc[5] + value
+
+    bias_operand = bias if ctx.has_bias else empty
+    if d_left is not None and d_left.numel():
+        add((d_left, angular, hidden, alpha, bias_operand), (1, 2, 3, 4), ctx.has_bias)
+    if d_angular is not None and d_angular.numel():
+        add((left, d_angular, hidden, alpha, bias_operand), (0, 2, 3, 4), ctx.has_bias)
+    if d_hidden is not None and d_hidden.numel():
+        add((left, angular, d_hidden, alpha, empty), (0, 1, 3), False)
+    has_da = d_alpha is not None and d_alpha.numel() > 0
+    has_db = ctx.has_bias and d_bias is not None and d_bias.numel() > 0
+    if has_da or has_db:
+        add((left, angular, hidden, d_alpha if has_da else torch.zeros_like(alpha),
+             d_bias if has_db else empty), (0, 1, 2), has_db)
+    return (*acc, None, None, None, None)
+
+
+radial_backward.register_autograd(_radial_double_backward, setup_context=_radial_backward_setup)

@@ -11,9 +11,6 @@ uvu_o2.py:153-156).  Non-CUDA or non-float32 operands raise instead of falling b
 
 from __future__ import annotations
 
-from functools import lru_cache
-
-import numpy as np
 import torch
 
 from . import _lib, ops
@@ -28,16 +25,6 @@ def _integer(value, name, minimum):
     if isinstance(value, bool) or int(value) != value or value < minimum:
         raise ValueError(f"{name} must be an integer >= {minimum}")
     return int(value)
-
-
-@lru_cache(maxsize=None)
-def uvu_plan(channels, channels_in2, m_max, parity, m_max_in2, parity_in2, normalization,
-             path_normalization):
-    """(entries_in1, entries_in2, paths, coefficients) of a configuration."""
-    _, e1, _ = uvu_representation(channels, m_max, parity)
-    _, e2, _ = uvu_representation(channels_in2, m_max_in2, parity_in2)
-    paths, coef = uvu_paths(e1, e2, normalization, path_normalization, channels_in2)
-    return e1, e2, paths, coef
 
 
 class UvuTensorProduct(torch.nn.Module):
@@ -154,35 +141,48 @@ class UvuTensorProduct(torch.nn.Module):
 
 def _uvu_backward_setup(ctx, inputs, output):
     left, right, weight, grad_output, table, config, shared, needed = inputs
-    ctx.save_for_backward(left, right, weight, grad_output)
+    ctx.save_for_backward(left, right, weight, grad_output, table)
     ctx.config, ctx.shared = config, shared
     ctx.set_materialize_grads(False)
 
 
 def _uvu_double_backward(ctx, dd_left, dd_right, dd_weight):
-    """Second derivatives through the differentiable PyTorch formula (the role of
-    uvu_triton.py:442-457)."""
-    left, right, weight, grad_output = ctx.saved_tensors
-    selected = [(i, c) for i, c in enumerate((dd_left, dd_right, dd_weight))
-                if c is not None and c.numel()]
-    if not selected:
-        return (None,) * 8
-    inv_parity = {v: k for k, v in PARITY_CODE.items()}
-    inv_norm = {v: k for k, v in NORM_CODE.items()}
-    c = ctx.config
-    e1, e2, paths, coef = uvu_plan(c[0], c[1], c[2], inv_parity[c[3]], c[4], inv_parity[c[5]],
-                                   inv_norm[c[6]], "path" if c[7] else "none")
-    coefficients = torch.from_numpy(np.asarray(coef)).to(left)
-    with torch.enable_grad():
-        operands = tuple(v.detach().requires_grad_(True)
-                         for v in (left, right, weight, grad_output))
-        value = ops.torch_uvu_flat(operands[0], operands[1], operands[2], e1, e2, paths,
-                                   coefficients, c[0], c[1], ctx.shared)
-        first = torch.autograd.grad(value, operands[:3], operands[3], create_graph=True)
-        second = torch.autograd.grad(tuple(first[i] for i, _ in selected), operands,
-                                     grad_outputs=tuple(cot for _, cot in selected),
-                                     allow_unused=True)
-    return (*second, None, None, None, None)
+    """Second derivatives through the same kernels, with role-pruned backward calls
+    (the reference recomputes them in PyTorch, uvu_triton.py:442-457).  The map is
+    trilinear in (x, y, w); the cotangents (ddx, ddy, ddw) contract to
+    <B(ddx, y; w) + B(x, ddy; w) + B(x, y; ddw), g>, so
+      d left   = B_x^T(g; ddy, w) + B_x^T(g; y, ddw)
+      d right  = B_y^T(g; ddx, w) + B_y^T(g; x, ddw)
+      d weight = B_w^T(g; ddx, y) + B_w^T(g; x, ddy)
+      d g      = B(ddx, y; w) + B(x, ddy; w) + B(x, y; ddw)."""
+    left, right, weight, grad_output, table = ctx.saved_tensors
+    cfg, shared = ctx.config, ctx.shared
+    ddx, ddy, ddw = (c if c is not None and c.numel() else None
+                     for c in (dd_left, dd_right, dd_weight))
+    need_x, need_y, need_w, need_g = ctx.needs_input_grad[:4]
+    terms = {0: [], 1: [], 2: []}
+
+    def backward(x, y, w, roles):
+        mask = sum(1 << r for r in roles)
+        if mask:
+            outs = ops.uvu_backward(x, y, w, grad_output, table, cfg, shared, mask)
+            for r in roles:
+                terms[r].append(outs[r])
+
+    if ddx is not None:
+        backward(ddx, right, weight, [r for r, n in ((1, need_y), (2, need_w)) if n])
+    if ddy is not None:
+        backward(left, ddy, weight, [r for r, n in ((0, need_x), (2, need_w)) if n])
+    if ddw is not None:
+        backward(left, right, ddw, [r for r, n in ((0, need_x), (1, need_y)) if n])
+    d_g = None
+    if need_g:
+        for x, y, w in ((ddx, right, weight), (left, ddy, weight), (left, right, ddw)):
+            if x is not None and y is not None and w is not None:
+                value = ops.uvu_forward(x, y, w, table, cfg, shared)
+                d_g = value if d_g is None else d_g + value
+    grads = [None if not terms[r] else sum(terms[r][1:], terms[r][0]) for r in range(3)]
+    return (*grads, d_g, None, None, None, None)
 
 
 ops.uvu_backward.register_autograd(_uvu_double_backward, setup_context=_uvu_backward_setup)
