@@ -938,9 +938,12 @@ int radial_validate(const RadialConfig& c) {
 }
 
 // Weight gradients through a materialized gw: edges in blocks of at most
-// kGwBlock (gw block = kGwBlock x Wn floats), dalpha split over kchunks K ranges
-// per block; partials summed in a fixed order at the end.
+// kGwBlock and at most kGwBlockBytes of gw (but never under kGwMinBlock edges, so
+// a block's dx/dy tile launch still fills the GPU), dalpha split over kchunks K
+// ranges per block; partials summed in a fixed order at the end.
 constexpr int64_t kGwBlock = 262144;
+constexpr size_t kGwBlockBytes = size_t(4) << 30;
+constexpr int64_t kGwMinBlock = 32768;
 
 struct GwPlan {
   bool ok;
@@ -951,7 +954,15 @@ struct GwPlan {
 GwPlan radial_gw_plan(int device, int64_t rows, int64_t Wn, int U, int H) {
   GwPlan g{};
   if (rows <= 0 || Wn % 4 != 0 || U % 4 != 0 || H % 4 != 0) return g;
-  g.blk = rows < kGwBlock ? rows : kGwBlock;
+  // Blocks of whole waves of the dx/dy tile (one CTA per SM, RT edges each),
+  // balanced so that about kGwBlockBytes of gw stay live at a time.
+  int64_t cap = static_cast<int64_t>(kGwBlockBytes / (static_cast<size_t>(Wn) * sizeof(float)));
+  cap = cap < kGwMinBlock ? kGwMinBlock : (cap > kGwBlock ? kGwBlock : cap);
+  const int64_t wave = static_cast<int64_t>(sm_count(device)) * (radial_ut(U) == 64 ? 128 : 64);
+  const int64_t waves = (rows + wave - 1) / wave;
+  const int64_t blocks = (rows + cap - 1) / cap;
+  const int64_t blk = ((waves + blocks - 1) / blocks) * wave;
+  g.blk = rows < blk ? rows : blk;
   g.nblocks = (rows + g.blk - 1) / g.blk;
   const int64_t tiles = ((Wn + kGemmBM - 1) / kGemmBM) * ((H + kGemmBN - 1) / kGemmBN);
   int64_t kc = (16 * static_cast<int64_t>(sm_count(device)) + tiles - 1) / tiles;
