@@ -50,6 +50,8 @@ METRICS = {
     "radial": "fwd+VJP edges/s, RadialUvuTensorProduct C64 m3 radial MLP 8-64-64, E=1048576",
     "radial_m6": "fwd+VJP edges/s, RadialUvuTensorProduct C{channels} m6 full / angular "
                  "canonical, radial MLP 16-64-64, E=131072",
+    "radial_m6_force": "force-loss training edges/s (second derivatives), "
+                       "RadialUvuTensorProduct C{channels} m6, radial MLP 16-64-64, E=131072",
 }
 # A100 published fwd+VJP for config 2 (benchmarks/eqx/results/complete_matrix.csv:383)
 A100_TP_ROWS_PER_S = 65536 / 30.087e-3
@@ -85,8 +87,8 @@ def _cpu_worker(task):
         start = time.perf_counter()
         oracle.vjp(x, y, w, g, shared=shared)
     else:
-        uvu = O.UvuOracle(channels if workload == "radial_m6" else 64, 1,
-                          6 if workload == "radial_m6" else 3, "full", "canonical")
+        m6 = workload.startswith("radial_m6")
+        uvu = O.UvuOracle(channels if m6 else 64, 1, 6 if m6 else 3, "full", "canonical")
         radial = O.RadialOracle(uvu)
         x = rng.standard_normal((rows, uvu.width1), dtype=np.float32)
         y = rng.standard_normal((rows, uvu.width2), dtype=np.float32)
@@ -122,6 +124,7 @@ def cpu_units_per_second(workload: str, rows_per_worker: int, steps: int, warmup
                       f"{steps} steps"}
 
 
+# The force-loss workload has no CPU leg: the numpy oracle has no second derivatives.
 CPU_ROWS = {"tp": 1024, "uvu": 16, "uvu_rowwise": 4, "radial": 256, "radial_m6": 64}
 
 
@@ -563,8 +566,47 @@ class RadialM6Workload(Workload):
         return (3 * w1 + 2 * 13 + 2 * 16 + 64 * 2) * 4 * self.edges
 
 
+class RadialM6ForceWorkload(RadialM6Workload):
+    """Force-loss training through the published radial chain (second derivatives,
+    the "force_parameters" metric of docs/RADIAL_PERFORMANCE.md:60-65): energy =
+    sum of the layer output; forces = its gradient with respect to x, angular and the
+    radial features (create_graph=True); loss = sum of the squared forces,
+    differentiated with respect to the three inputs and every network parameter.
+    The reference publishes the metric but not its loss, so vs_baseline stays null."""
+
+    name = "radial_m6_force"
+
+    @staticmethod
+    def published(args):
+        return None
+
+    def step(self, x=None, y=None, f=None, g=None):
+        torch = self.torch
+        x = (self.x if x is None else x).detach().requires_grad_(True)
+        ang = (self.angular if y is None else y).detach().requires_grad_(True)
+        feat = (self.feat if f is None else f).detach().requires_grad_(True)
+        energy = self.model(x, ang, self.trunk(feat)).sum()
+        forces = torch.autograd.grad(energy, (x, ang, feat), create_graph=True)
+        loss = sum(t.square().sum() for t in forces)
+        grads = torch.autograd.grad(loss, [x, ang, feat] + self.params)
+        if self.world > 1:
+            flat = torch.cat([t.reshape(-1) for t in grads[3:]])
+            torch.distributed.all_reduce(flat)
+        return loss, grads
+
+    def config(self):
+        c = super().config()
+        c["workload"] = ("force-loss training through the reference's published radial chain "
+                         "(MLP 16-64-64, fused affine + V=1 uvu C{} m6): energy = sum of "
+                         "outputs, forces = d energy / d (x, angular, features) with "
+                         "create_graph, loss = sum of squared forces, gradients for the "
+                         "inputs and every parameter").format(self.channels)
+        return c
+
+
 WORKLOADS = {"tp": TpWorkload, "uvu": UvuWorkload, "uvu_rowwise": UvuRowWorkload,
-             "radial": RadialWorkload, "radial_m6": RadialM6Workload}
+             "radial": RadialWorkload, "radial_m6": RadialM6Workload,
+             "radial_m6_force": RadialM6ForceWorkload}
 
 
 # ------------------------------------------------------------------ GPU arm
@@ -750,6 +792,9 @@ def _leaves(value):
 def run_reference(args) -> dict | None:
     if int(os.environ.get("RANK", "0")) != 0:
         return None
+    if args.workload not in CPU_ROWS:
+        return {"impl": "reference", "unavailable": "the CPU oracle has no second derivatives "
+                                                     "(force-loss metric)"}
     rows = args.cpu_rows or CPU_ROWS[args.workload]
     base = cpu_units_per_second(args.workload, rows, args.steps, max(1, min(args.warmup, 1)),
                                 args.channels)
@@ -800,7 +845,7 @@ def main(argv=None) -> int:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in CPU_ROWS:
         # The process pool starts before the first CUDA call (spawned workers).
         cpu = cpu_units_per_second(args.workload, args.cpu_rows or CPU_ROWS[args.workload], 3, 1,
                                    args.channels)
