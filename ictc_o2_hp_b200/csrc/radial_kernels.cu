@@ -14,6 +14,7 @@
 //     a path-tiled reduction over edges (fixed row chunks, fixed-order sum).
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -221,11 +222,16 @@ struct RadTileArgs {
   int64_t Wn = 0;
 };
 
-template <int UT>
+// Thread tiles: 4 edges x NH groups of 4 channels (NH = 2: 256 threads, the 4x8
+// "split" tile; NH = 1: 512 threads, the 4x4 "wide" tile with half the registers
+// per thread and twice the warps).  Both cover RT = 128 (UT = 64) or 64 (UT = 128)
+// edges per CTA.
+template <int UT, int NH = 2>
 struct RtShape {
-  static constexpr int TC = UT / 8;           // threads along the channels
-  static constexpr int TR = kRtThreads / TC;  // thread rows
-  static constexpr int RT = TR * 4;           // edges per CTA
+  static constexpr int NT = NH == 2 ? 256 : 512;  // threads per CTA
+  static constexpr int TC = UT / (4 * NH);        // threads along the channels
+  static constexpr int TR = NT / TC;              // thread rows
+  static constexpr int RT = TR * 4;               // edges per CTA
 };
 
 inline size_t radial_tile_smem(int ut, int H, int W2, int np, int n1, int n2, bool dx) {
@@ -276,17 +282,18 @@ __device__ __forceinline__ void store4(float* __restrict__ dst, const float (&v)
   }
 }
 
-template <int MODE, int UT>
-__global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
-  using Sh = RtShape<UT>;
-  constexpr int RT = Sh::RT, TC = Sh::TC;
+template <int MODE, int UT, int NH>
+__global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArgs A) {
+  using Sh = RtShape<UT, NH>;
+  constexpr int RT = Sh::RT, TC = Sh::TC, NT = Sh::NT;
+  constexpr int CW = 4 * NH;  // channels per thread
   extern __shared__ __align__(128) unsigned char rt_raw[];
   // [0, 128): stage barriers (full) and release counters
   uint64_t* full = reinterpret_cast<uint64_t*>(rt_raw);
   unsigned* done = reinterpret_cast<unsigned*>(rt_raw + 64);
   float* sm = reinterpret_cast<float*>(rt_raw + 128);
   const int tid = threadIdx.x, lane = tid & 31;
-  const int nwarps = kRtThreads / 32;
+  const int nwarps = NT / 32;
   const int kc = A.H < kRtKC ? A.H : kRtKC;
   const int nkc = (A.H + kRtKC - 1) / kRtKC;
   const int W2s = odd_stride(A.W2);
@@ -309,25 +316,25 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
     return MODE == kRtDx ? (T / (np * nkc)) * UT : static_cast<int>(blockIdx.y) * UT;
   };
 
-  for (int q = tid; q < np; q += kRtThreads) {
+  for (int q = tid; q < np; q += NT) {
     paths[q] = A.t.paths[q];
     order[q] = MODE == kRtDx ? A.t.by_i[q] : q;
   }
-  for (int q = tid; q < np * 8; q += kRtThreads) coef[q] = __ldg(A.t.coef + q);
-  for (int q = tid; q < A.t.n1; q += kRtThreads) in1[q] = A.t.in1[q];
-  for (int q = tid; q < A.t.n2; q += kRtThreads) in2[q] = A.t.in2[q];
-  for (int idx = tid; idx < RT * A.H; idx += kRtThreads) {
+  for (int q = tid; q < np * 8; q += NT) coef[q] = __ldg(A.t.coef + q);
+  for (int q = tid; q < A.t.n1; q += NT) in1[q] = A.t.in1[q];
+  for (int q = tid; q < A.t.n2; q += NT) in2[q] = A.t.in2[q];
+  for (int idx = tid; idx < RT * A.H; idx += NT) {
     const int r = idx / A.H, h = idx - r * A.H;
     const int64_t row = row0 + r;
     Ht[h * RT + r] = row < A.rows ? __ldg(A.hidden + row * A.H + h) : 0.f;
   }
-  for (int idx = tid; idx < RT * A.W2; idx += kRtThreads) {
+  for (int idx = tid; idx < RT * A.W2; idx += NT) {
     const int r = idx / A.W2, c = idx - r * A.W2;
     const int64_t row = row0 + r;
     angt[r * W2s + c] = row < A.rows ? __ldg(A.ang + row * A.W2 + c) : 0.f;
   }
   if (MODE == kRtDx)
-    for (int idx = tid; idx < RT * W2s; idx += kRtThreads) dyacc[idx] = 0.f;
+    for (int idx = tid; idx < RT * W2s; idx += NT) dyacc[idx] = 0.f;
   if (tid == 0) {
     for (int st = 0; st < kRtStages; ++st) {
       mbar_init(&full[st], 1);
@@ -355,12 +362,12 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
     bulk_g2s(dst, src, bytes, &full[st]);
   };
 
-  float acc[4][8];
-  float res[4][8][2];
+  float acc[4][CW];
+  float res[4][CW][2];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < 8; ++b) res[a][b][0] = res[a][b][1] = 0.f;
+    for (int b = 0; b < CW; ++b) res[a][b][0] = res[a][b][1] = 0.f;
 
   if (tid == 0)
     for (int T = 0; T < kRtStages && T < ntiles; ++T) issue(T, T);
@@ -377,7 +384,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
 #pragma unroll
       for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int b = 0; b < 8; ++b) acc[a][b] = 0.f;
+        for (int b = 0; b < CW; ++b) acc[a][b] = 0.f;
       // Pull the path's epilogue operands (x_i; g_k in dx mode) of this thread's
       // four edges toward L1 while the path's product runs: lane tc takes line tc
       // of each edge's slice, lines that start inside the valid channels only.
@@ -403,14 +410,17 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
     const float* Hb = Ht + static_cast<size_t>(ck) * kRtKC * RT;
     auto kstep = [&](int k) {
       const float4 a4 = *reinterpret_cast<const float4*>(Hb + k * RT + e0);
-      const float4 b0 = *reinterpret_cast<const float4*>(Wb + k * UT + tc * 4);
-      const float4 b1 = *reinterpret_cast<const float4*>(Wb + k * UT + UT / 2 + tc * 4);
       const float av[4] = {a4.x, a4.y, a4.z, a4.w};
-      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      float bv[CW];
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        const float4 b4 = *reinterpret_cast<const float4*>(Wb + k * UT + h * (UT / NH) + tc * 4);
+        bv[4 * h] = b4.x; bv[4 * h + 1] = b4.y; bv[4 * h + 2] = b4.z; bv[4 * h + 3] = b4.w;
+      }
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < CW; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     };
     if (kn == kRtKC) {
 #pragma unroll 8
@@ -448,8 +458,8 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
           const float c10 = fmaf(c[4], y0, c[5] * y1), c11 = fmaf(c[6], y0, c[7] * y1);
           float dyp0 = 0.f, dyp1 = 0.f;
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const int u = ub + (half ? UT / 2 : 0) + tc * 4;
+          for (int half = 0; half < NH; ++half) {
+            const int u = ub + half * (UT / NH) + tc * 4;
             if (MODE == kRtFwd) {
               float xv[4 * D1];
               load4<D1>(xv, A.opnd + row * A.W1 + ei.x + static_cast<int64_t>(u) * D1, row_ok, u,
@@ -541,8 +551,8 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
           const int64_t row = row0 + e0 + ee;
           const bool row_ok = row < A.rows;
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            const int u = ub + (half ? UT / 2 : 0) + tc * 4;
+          for (int half = 0; half < NH; ++half) {
+            const int u = ub + half * (UT / NH) + tc * 4;
             float v[4][2];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -554,7 +564,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
             else store4<1>(dst, v, row_ok, u, A.U, A.vec);
           }
 #pragma unroll
-          for (int b = 0; b < 8; ++b) res[ee][b][0] = res[ee][b][1] = 0.f;
+          for (int b = 0; b < CW; ++b) res[ee][b][0] = res[ee][b][1] = 0.f;
         }
       }
     }
@@ -565,7 +575,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) radial_tile(RadTileArgs A) {
   }
   if (MODE == kRtDx) {
     __syncthreads();
-    for (int idx = tid; idx < RT * A.W2; idx += kRtThreads) {
+    for (int idx = tid; idx < RT * A.W2; idx += NT) {
       const int r = idx / A.W2, col = idx - r * A.W2;
       const int64_t row = row0 + r;
       if (row < A.rows) A.dy[row * A.W2 + col] = dyacc[r * W2s + col];
@@ -579,24 +589,38 @@ inline bool radial_tile_fits(int U, int H, int W2, int np, int n1, int n2, bool 
   return radial_tile_smem(radial_ut(U), H, W2, np, n1, n2, dx) <= 225 * 1024;
 }
 
+template <int MODE, int UT, int NH>
+int launch_radial_tile_shape(const RadTileArgs& ra, size_t smem, cudaStream_t s) {
+  using Sh = RtShape<UT, NH>;
+  const void* fn = reinterpret_cast<const void*>(&radial_tile<MODE, UT, NH>);
+  const int st = allow_smem(fn, smem);
+  if (st != ICTC_OK) return st;
+  const dim3 grid(static_cast<unsigned>(ceil_div(ra.rows, Sh::RT)),
+                  MODE == kRtDx ? 1u : static_cast<unsigned>(ceil_div(ra.U, UT)));
+  radial_tile<MODE, UT, NH><<<grid, Sh::NT, smem, s>>>(ra);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "radial tile launch");
+}
+
+// Thread tile of the edge tile kernel: "wide" (4 x 4 per thread, 512 threads, the
+// default: forward -9 %, dx/dy -6 % at the config-5 shapes) or, with
+// ICTC_RADIAL_TILE=split, the 4 x 8 tile on 256 threads; tests cover both.
+inline bool radial_tile_wide() {
+  const char* v = getenv("ICTC_RADIAL_TILE");
+  return v == nullptr || strcmp(v, "split") != 0;
+}
+
 template <int MODE>
 int launch_radial_tile(const RadTileArgs& ra, cudaStream_t s) {
   const int ut = radial_ut(ra.U);
   const size_t smem = radial_tile_smem(ut, ra.H, ra.W2, ra.t.np, ra.t.n1, ra.t.n2, MODE == kRtDx);
   if (smem > 225 * 1024) return ICTC_ERR_UNSUPPORTED;  // caller falls back to the row tile
-  const void* fn = ut == 64 ? reinterpret_cast<const void*>(&radial_tile<MODE, 64>)
-                            : reinterpret_cast<const void*>(&radial_tile<MODE, 128>);
-  const int st = allow_smem(fn, smem);
-  if (st != ICTC_OK) return st;
-  const int rt = ut == 64 ? RtShape<64>::RT : RtShape<128>::RT;
-  const dim3 grid(static_cast<unsigned>(ceil_div(ra.rows, rt)),
-                  MODE == kRtDx ? 1u : static_cast<unsigned>(ceil_div(ra.U, ut)));
+  const bool wide = radial_tile_wide();
   if (ut == 64)
-    radial_tile<MODE, 64><<<grid, kRtThreads, smem, s>>>(ra);
-  else
-    radial_tile<MODE, 128><<<grid, kRtThreads, smem, s>>>(ra);
-  const cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "radial tile launch");
+    return wide ? launch_radial_tile_shape<MODE, 64, 1>(ra, smem, s)
+                : launch_radial_tile_shape<MODE, 64, 2>(ra, smem, s);
+  return wide ? launch_radial_tile_shape<MODE, 128, 1>(ra, smem, s)
+              : launch_radial_tile_shape<MODE, 128, 2>(ra, smem, s);
 }
 
 // ------------------------------------------------------------ dhidden

@@ -87,6 +87,17 @@ def test_against_oracle(u, m_max, hidden, bias, rows, cuda_device):
         assert err <= TOL, f"{key}: {err:.3e}"
 
 
+@pytest.mark.parametrize("u,m_max,hidden,bias,rows", [
+    (64, 3, 64, True, 300),    # channel tile of 64 (4 x 8 tile: 256 threads)
+    (160, 2, 24, True, 70),    # channel tiles of 128, the last partial
+])
+def test_split_thread_tile(u, m_max, hidden, bias, rows, cuda_device, monkeypatch):
+    """The 4 x 8 per-thread tile (ICTC_RADIAL_TILE=split) against the oracle; the
+    default 4 x 4 tile runs every other case."""
+    monkeypatch.setenv("ICTC_RADIAL_TILE", "split")
+    test_against_oracle(u, m_max, hidden, bias, rows, cuda_device)
+
+
 def test_role_pruning_matches_full(cuda_device):
     """Requesting a subset of gradients returns the same values as the full VJP."""
     torch.manual_seed(0)
