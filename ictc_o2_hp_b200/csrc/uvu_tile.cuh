@@ -31,9 +31,11 @@ struct UvuTileArgs {
   bool vec;  // 16-byte access to 4-channel groups of opnd / out
 };
 
-template <int UT>
+// Thread tiles: 4 rows x NH groups of 4 channels (NH = 2: the 4 x 8 "split" tile;
+// NH = 1: the 4 x 4 "wide" tile, twice the threads at half the registers each).
+template <int UT, int NH = 2>
 struct UtShape {
-  static constexpr int TC = UT / 8;                // threads along the channels
+  static constexpr int TC = UT / (4 * NH);         // threads along the channels
   static constexpr int NT = (kUtRows / 4) * TC;    // threads per CTA
 };
 
@@ -91,9 +93,10 @@ __device__ __forceinline__ void ut_store4(float* __restrict__ dst, const float (
   }
 }
 
-template <int MODE, int UT>
-__global__ void __launch_bounds__(UtShape<UT>::NT, 1) uvu_tile(UvuTileArgs A) {
-  constexpr int TC = UtShape<UT>::TC, NT = UtShape<UT>::NT;
+template <int MODE, int UT, int NH>
+__global__ void __launch_bounds__(UtShape<UT, NH>::NT, 1) uvu_tile(UvuTileArgs A) {
+  constexpr int TC = UtShape<UT, NH>::TC, NT = UtShape<UT, NH>::NT;
+  constexpr int CW = 4 * NH;  // channels per thread
   constexpr int RT = kUtRows;
   extern __shared__ __align__(128) unsigned char ut_raw[];
   uint64_t* full = reinterpret_cast<uint64_t*>(ut_raw);
@@ -156,12 +159,12 @@ __global__ void __launch_bounds__(UtShape<UT>::NT, 1) uvu_tile(UvuTileArgs A) {
     }
   };
 
-  float acc[2][4][8];
-  float res[4][8][2];
+  float acc[2][4][CW];
+  float res[4][CW][2];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < 8; ++b) res[a][b][0] = res[a][b][1] = 0.f;
+    for (int b = 0; b < CW; ++b) res[a][b][0] = res[a][b][1] = 0.f;
 
   if (tid == 0)
     for (int T = 0; T < kUtStages && T < ntiles; ++T) issue(T, T);
@@ -181,16 +184,19 @@ __global__ void __launch_bounds__(UtShape<UT>::NT, 1) uvu_tile(UvuTileArgs A) {
 #pragma unroll
         for (int a = 0; a < 4; ++a)
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[b][a][j] = 0.f;
+          for (int j = 0; j < CW; ++j) acc[b][a][j] = 0.f;
     }
     const int v0 = ck * kUtVC;
     const int kn = A.V - v0 < kUtVC ? A.V - v0 : kUtVC;
     const float* Wb = Wt + st * vc * UT;
     auto gemm = [&]<int D2>() {
       for (int v = 0; v < kn; ++v) {
-        const float4 w0 = *reinterpret_cast<const float4*>(Wb + v * UT + tc * 4);
-        const float4 w1 = *reinterpret_cast<const float4*>(Wb + v * UT + UT / 2 + tc * 4);
-        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float wv[CW];
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          const float4 w4 = *reinterpret_cast<const float4*>(Wb + v * UT + h * (UT / NH) + tc * 4);
+          wv[4 * h] = w4.x; wv[4 * h + 1] = w4.y; wv[4 * h + 2] = w4.z; wv[4 * h + 3] = w4.w;
+        }
 #pragma unroll
         for (int b = 0; b < D2; ++b) {
           const float4 a4 =
@@ -199,7 +205,7 @@ __global__ void __launch_bounds__(UtShape<UT>::NT, 1) uvu_tile(UvuTileArgs A) {
 #pragma unroll
           for (int i = 0; i < 4; ++i)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) acc[b][i][j] = fmaf(av[i], wv[j], acc[b][i][j]);
+            for (int j = 0; j < CW; ++j) acc[b][i][j] = fmaf(av[i], wv[j], acc[b][i][j]);
         }
       }
     };
@@ -227,8 +233,8 @@ __global__ void __launch_bounds__(UtShape<UT>::NT, 1) uvu_tile(UvuTileArgs A) {
         const int64_t row = row0 + r0 + ee;
         const bool row_ok = row < A.rows;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int u = ub + (half ? UT / 2 : 0) + tc * 4;
+        for (int half = 0; half < NH; ++half) {
+          const int u = ub + half * (UT / NH) + tc * 4;
           if (MODE == kUtFwd) {
             float xv[4 * D1];
             ut_load4<D1>(xv, A.opnd + row * A.W1 + ei.x + static_cast<int64_t>(u) * D1, row_ok,
@@ -280,8 +286,8 @@ __global__ void __launch_bounds__(UtShape<UT>::NT, 1) uvu_tile(UvuTileArgs A) {
         const int64_t row = row0 + r0 + ee;
         const bool row_ok = row < A.rows;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int u = ub + (half ? UT / 2 : 0) + tc * 4;
+        for (int half = 0; half < NH; ++half) {
+          const int u = ub + half * (UT / NH) + tc * 4;
           float vv[4][2];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -293,7 +299,7 @@ __global__ void __launch_bounds__(UtShape<UT>::NT, 1) uvu_tile(UvuTileArgs A) {
           else ut_store4<1>(dst, vv, row_ok, u, A.U, A.vec);
         }
 #pragma unroll
-        for (int b = 0; b < 8; ++b) res[ee][b][0] = res[ee][b][1] = 0.f;
+        for (int b = 0; b < CW; ++b) res[ee][b][0] = res[ee][b][1] = 0.f;
       }
     }
   }
@@ -303,6 +309,25 @@ __global__ void __launch_bounds__(UtShape<UT>::NT, 1) uvu_tile(UvuTileArgs A) {
   }
 }
 
+template <int MODE, int UT, int NH>
+int launch_uvu_tile_shape(const UvuTileArgs& ua, size_t smem, cudaStream_t s) {
+  const void* fn = reinterpret_cast<const void*>(&uvu_tile<MODE, UT, NH>);
+  const int st = allow_smem(fn, smem);
+  if (st != ICTC_OK) return st;
+  const dim3 grid(static_cast<unsigned>(ceil_div(ua.rows, kUtRows)),
+                  static_cast<unsigned>(ceil_div(ua.U, UT)));
+  uvu_tile<MODE, UT, NH><<<grid, UtShape<UT, NH>::NT, smem, s>>>(ua);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "uvu tile launch");
+}
+
+// Thread tile of uvu_tile: "wide" (4 x 4 per thread, the default: forward and dx
+// -18 % at config 4) or, with ICTC_UVU_TILE=split, 4 x 8; tests cover both.
+inline bool uvu_tile_wide() {
+  const char* v = getenv("ICTC_UVU_TILE");
+  return v == nullptr || strcmp(v, "split") != 0;
+}
+
 // Launches uvu_tile<MODE> when its shared-memory tiles fit; returns
 // ICTC_ERR_UNSUPPORTED (nothing launched) when they do not.
 template <int MODE>
@@ -310,16 +335,10 @@ int launch_uvu_tile(const UvuTileArgs& ua, cudaStream_t s) {
   const int ut = ua.U <= 64 ? 64 : 128;
   const size_t smem = uvu_tile_smem(ut, ua.V, ua.W2, ua.t.np, ua.t.n1, ua.t.n2);
   if (smem > 225 * 1024) return ICTC_ERR_UNSUPPORTED;
-  const void* fn = ut == 64 ? reinterpret_cast<const void*>(&uvu_tile<MODE, 64>)
-                            : reinterpret_cast<const void*>(&uvu_tile<MODE, 128>);
-  const int st = allow_smem(fn, smem);
-  if (st != ICTC_OK) return st;
-  const dim3 grid(static_cast<unsigned>(ceil_div(ua.rows, kUtRows)),
-                  static_cast<unsigned>(ceil_div(ua.U, ut)));
+  const bool wide = uvu_tile_wide();
   if (ut == 64)
-    uvu_tile<MODE, 64><<<grid, UtShape<64>::NT, smem, s>>>(ua);
-  else
-    uvu_tile<MODE, 128><<<grid, UtShape<128>::NT, smem, s>>>(ua);
-  const cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "uvu tile launch");
+    return wide ? launch_uvu_tile_shape<MODE, 64, 1>(ua, smem, s)
+                : launch_uvu_tile_shape<MODE, 64, 2>(ua, smem, s);
+  return wide ? launch_uvu_tile_shape<MODE, 128, 1>(ua, smem, s)
+              : launch_uvu_tile_shape<MODE, 128, 2>(ua, smem, s);
 }

@@ -77,6 +77,14 @@ def test_against_oracle(case, cuda_device):
     check(run(tp, x, y, w, g, cuda_device, shared), want)
 
 
+@pytest.mark.parametrize("case", [c for c in CASES if c[8]][:3])
+def test_split_thread_tile(case, cuda_device, monkeypatch):
+    """Shared-weight forward / dx with the 4 x 8 per-thread tile (ICTC_UVU_TILE=split);
+    the default 4 x 4 tile runs every other case."""
+    monkeypatch.setenv("ICTC_UVU_TILE", "split")
+    test_against_oracle(case, cuda_device)
+
+
 def test_role_pruning_and_empty(cuda_device):
     from ictc_o2_hp_b200 import UvuTensorProduct
     torch.manual_seed(0)
