@@ -37,6 +37,10 @@ SIGNATURES = {
     "ictc_o2_tp_backward": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _size, _i64, _i32,
                                    _i32, _i32, _i32, _vp]),
     "ictc_o2_tp_backward_noalloc": (_i32, [_vp] * 7 + [_i64, _i32, _i32, _i32, _i32, _vp]),
+    "ictc_o2_tp_forward_layout": (_i32, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i32,
+                                         _vp]),
+    "ictc_o2_tp_backward_layout": (_i32, [_vp] * 8 + [_size, _i64, _i32, _i32, _i32, _i32, _i32,
+                                                      _vp]),
     "ictc_o2_uvu_table": (_i32, [_i32] * 8 + [ctypes.POINTER(_i32), _i64,
                                               ctypes.POINTER(_i64)]),
     "ictc_o2_uvu_workspace": (_i32, [_i32] * 8 + [_i32, _i64, _i32, ctypes.POINTER(_size),
@@ -130,11 +134,12 @@ def tp_path_table(m_max: int, parity: str) -> list[tuple]:
     return rows
 
 
-def tp_forward(left, right, weight, out, channels, m_max, parity, normalization):
+def tp_forward(left, right, weight, out, channels, m_max, parity, normalization, layout=0):
+    """layout: 0 channel-major, 1 component-major frequency blocks."""
     rows = left.shape[0]
-    check(load().ictc_o2_tp_forward(ptr(left), ptr(right), ptr(weight), ptr(out), rows,
-                                    channels, m_max, PARITY[parity], NORMALIZATION[normalization],
-                                    stream_of(left.device)), "tp_forward")
+    check(load().ictc_o2_tp_forward_layout(
+        ptr(left), ptr(right), ptr(weight), ptr(out), rows, channels, m_max, PARITY[parity],
+        NORMALIZATION[normalization], layout, stream_of(left.device)), "tp_forward")
 
 
 def tp_backward_workspace(rows, channels, m_max, parity, device: torch.device) -> int:
@@ -146,12 +151,12 @@ def tp_backward_workspace(rows, channels, m_max, parity, device: torch.device) -
 
 
 def tp_backward(left, right, weight, grad_output, grad_left, grad_right, grad_weight,
-                workspace, channels, m_max, parity, normalization):
+                workspace, channels, m_max, parity, normalization, layout=0):
     rows = left.shape[0]
-    check(load().ictc_o2_tp_backward(
+    check(load().ictc_o2_tp_backward_layout(
         ptr(left), ptr(right), ptr(weight), ptr(grad_output), ptr(grad_left), ptr(grad_right),
         ptr(grad_weight), ptr(workspace), workspace.numel() if workspace is not None else 0,
-        rows, channels, m_max, PARITY[parity], NORMALIZATION[normalization],
+        rows, channels, m_max, PARITY[parity], NORMALIZATION[normalization], layout,
         stream_of(left.device)), "tp_backward")
 
 

@@ -75,4 +75,4 @@ extern "C" int32_t ictc_o2_device_error(int32_t* code) {
   return ICTC_OK;
 }
 
-extern "C" int32_t ictc_o2_abi_version(void) { return 100; }
+extern "C" int32_t ictc_o2_abi_version(void) { return 101; }

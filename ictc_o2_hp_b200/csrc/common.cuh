@@ -42,11 +42,14 @@ struct TpLayout {
   int64_t width;
   int fbase;    // offset of frequency 1
   int fstride;  // offset step between consecutive frequencies
+  int cm;       // frequency blocks stored [copy][component][channel] (1) or
+                // [copy][channel][component] (0)
 };
 
-inline TpLayout tp_layout(int C, int m_max, bool full) {
+inline TpLayout tp_layout(int C, int m_max, bool full, int cm = 0) {
   TpLayout L;
   L.C = C;
+  L.cm = cm;
   L.fbase = full ? 2 * C : C;
   L.fstride = full ? 4 * C : 2 * C;
   L.width = static_cast<int64_t>(L.fbase) + static_cast<int64_t>(m_max) * L.fstride;

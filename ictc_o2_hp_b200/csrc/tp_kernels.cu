@@ -124,7 +124,14 @@ __device__ __forceinline__ void load_slots(const Row& row, const TpLayout& L, in
   v[1] = FULL ? row.ld(L.C + c) : 0.0f;
 #pragma unroll
   for (int m = 1; m <= M; ++m) {
-    const float2 r = row.ld2(L.fbase + (m - 1) * L.fstride + 2 * (q * L.C + c));
+    const int base = L.fbase + (m - 1) * L.fstride;
+    float2 r;
+    if (L.cm) {  // component-major: the two components C apart (triton_o2.py:116-118)
+      const int o = base + 2 * q * L.C + c;
+      r = make_float2(row.ld(o), row.ld(o + L.C));
+    } else {
+      r = row.ld2(base + 2 * (q * L.C + c));
+    }
     v[2 * m] = q ? -r.y : r.x;
     v[2 * m + 1] = q ? r.x : r.y;
   }
@@ -141,8 +148,15 @@ __device__ __forceinline__ void store_slots(float* __restrict__ row, const TpLay
   }
 #pragma unroll
   for (int m = 1; m <= M; ++m) {
-    float* p = row + L.fbase + (m - 1) * L.fstride + 2 * (q * L.C + c);
-    st2(p, q ? v[2 * m + 1] : v[2 * m], q ? -v[2 * m] : v[2 * m + 1], vec2);
+    const float v0 = q ? v[2 * m + 1] : v[2 * m], v1 = q ? -v[2 * m] : v[2 * m + 1];
+    const int base = L.fbase + (m - 1) * L.fstride;
+    if (L.cm) {
+      float* p = row + base + 2 * q * L.C + c;
+      p[0] = v0;
+      p[L.C] = v1;
+    } else {
+      st2(row + base + 2 * (q * L.C + c), v0, v1, vec2);
+    }
   }
 }
 
@@ -1007,19 +1021,22 @@ extern "C" int32_t ictc_o2_tp_path_table(int32_t m_max, int32_t parity, int32_t*
   return ICTC_OK;
 }
 
-extern "C" int32_t ictc_o2_tp_forward(const float* left, const float* right, const float* weight,
-                                      float* output, int64_t rows, int32_t channels,
-                                      int32_t m_max, int32_t parity, int32_t normalization,
-                                      void* stream) {
+namespace {
+
+int32_t tp_forward_impl(const float* left, const float* right, const float* weight,
+                        float* output, int64_t rows, int32_t channels, int32_t m_max,
+                        int32_t parity, int32_t normalization, int32_t layout, void* stream) {
   int st = validate(rows, channels, m_max, parity, normalization);
   if (st != ICTC_OK) return st;
+  if (layout != ICTC_LAYOUT_CHANNEL_MAJOR && layout != ICTC_LAYOUT_COMPONENT_MAJOR)
+    return fail(ICTC_ERR_INVALID, "layout must be ICTC_LAYOUT_CHANNEL_MAJOR or _COMPONENT_MAJOR");
   if (rows == 0) return ICTC_OK;
   if (!left || !right || !weight || !output)
     return fail(ICTC_ERR_INVALID, "null tensor pointer");
   if (!aligned(left, 4) || !aligned(right, 4) || !aligned(weight, 4) || !aligned(output, 4))
     return fail(ICTC_ERR_INVALID, "tensor pointers must be 4-byte aligned");
   const bool full = parity == ICTC_PARITY_FULL;
-  const TpLayout L = tp_layout(channels, m_max, full);
+  const TpLayout L = tp_layout(channels, m_max, full, layout);
   const Kernels& k = kKernels.k[full ? 1 : 0][m_max];
   const Mags mags = tp_mags(normalization);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1089,6 +1106,25 @@ extern "C" int32_t ictc_o2_tp_forward(const float* left, const float* right, con
   return ICTC_OK;
 }
 
+}  // namespace
+
+extern "C" int32_t ictc_o2_tp_forward(const float* left, const float* right, const float* weight,
+                                      float* output, int64_t rows, int32_t channels,
+                                      int32_t m_max, int32_t parity, int32_t normalization,
+                                      void* stream) {
+  return tp_forward_impl(left, right, weight, output, rows, channels, m_max, parity,
+                         normalization, ICTC_LAYOUT_CHANNEL_MAJOR, stream);
+}
+
+extern "C" int32_t ictc_o2_tp_forward_layout(const float* left, const float* right,
+                                             const float* weight, float* output, int64_t rows,
+                                             int32_t channels, int32_t m_max, int32_t parity,
+                                             int32_t normalization, int32_t layout,
+                                             void* stream) {
+  return tp_forward_impl(left, right, weight, output, rows, channels, m_max, parity,
+                         normalization, layout, stream);
+}
+
 extern "C" int32_t ictc_o2_tp_backward_workspace(int64_t rows, int32_t channels, int32_t m_max,
                                                  int32_t parity, int32_t device, size_t* bytes) {
   if (bytes == nullptr) return fail(ICTC_ERR_INVALID, "bytes is null");
@@ -1116,14 +1152,17 @@ extern "C" int32_t ictc_o2_tp_backward_workspace(int64_t rows, int32_t channels,
   return ICTC_OK;
 }
 
-extern "C" int32_t ictc_o2_tp_backward(const float* left, const float* right, const float* weight,
-                                       const float* grad_output, float* grad_left,
-                                       float* grad_right, float* grad_weight, void* workspace,
-                                       size_t workspace_bytes, int64_t rows, int32_t channels,
-                                       int32_t m_max, int32_t parity, int32_t normalization,
-                                       void* stream) {
+namespace {
+
+int32_t tp_backward_impl(const float* left, const float* right, const float* weight,
+                         const float* grad_output, float* grad_left, float* grad_right,
+                         float* grad_weight, void* workspace, size_t workspace_bytes,
+                         int64_t rows, int32_t channels, int32_t m_max, int32_t parity,
+                         int32_t normalization, int32_t layout, void* stream) {
   int st = validate(rows, channels, m_max, parity, normalization);
   if (st != ICTC_OK) return st;
+  if (layout != ICTC_LAYOUT_CHANNEL_MAJOR && layout != ICTC_LAYOUT_COMPONENT_MAJOR)
+    return fail(ICTC_ERR_INVALID, "layout must be ICTC_LAYOUT_CHANNEL_MAJOR or _COMPONENT_MAJOR");
   if (!grad_weight) return fail(ICTC_ERR_INVALID, "grad_weight is null");
   const bool full = parity == ICTC_PARITY_FULL;
   const int64_t numel = weight_numel(channels, m_max, full);
@@ -1140,7 +1179,7 @@ extern "C" int32_t ictc_o2_tp_backward(const float* left, const float* right, co
       !aligned(grad_output, 4) || !aligned(grad_left, 4) || !aligned(grad_right, 4) ||
       !aligned(grad_weight, 4) || !aligned(workspace, 16))
     return fail(ICTC_ERR_INVALID, "tensor pointers must be 4-byte aligned (workspace 16)");
-  const TpLayout L = tp_layout(channels, m_max, full);
+  const TpLayout L = tp_layout(channels, m_max, full, layout);
   const Kernels& k = kKernels.k[full ? 1 : 0][m_max];
   int device = 0;
   if ((st = current_device(&device)) != ICTC_OK) return st;
@@ -1185,6 +1224,29 @@ extern "C" int32_t ictc_o2_tp_backward(const float* left, const float* right, co
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "reduce launch");
   return ICTC_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t ictc_o2_tp_backward(const float* left, const float* right, const float* weight,
+                                       const float* grad_output, float* grad_left,
+                                       float* grad_right, float* grad_weight, void* workspace,
+                                       size_t workspace_bytes, int64_t rows, int32_t channels,
+                                       int32_t m_max, int32_t parity, int32_t normalization,
+                                       void* stream) {
+  return tp_backward_impl(left, right, weight, grad_output, grad_left, grad_right, grad_weight,
+                          workspace, workspace_bytes, rows, channels, m_max, parity,
+                          normalization, ICTC_LAYOUT_CHANNEL_MAJOR, stream);
+}
+
+extern "C" int32_t ictc_o2_tp_backward_layout(
+    const float* left, const float* right, const float* weight, const float* grad_output,
+    float* grad_left, float* grad_right, float* grad_weight, void* workspace,
+    size_t workspace_bytes, int64_t rows, int32_t channels, int32_t m_max, int32_t parity,
+    int32_t normalization, int32_t layout, void* stream) {
+  return tp_backward_impl(left, right, weight, grad_output, grad_left, grad_right, grad_weight,
+                          workspace, workspace_bytes, rows, channels, m_max, parity,
+                          normalization, layout, stream);
 }
 
 // ------------------------------------------------------------ no-alloc backward

@@ -43,24 +43,26 @@ def tp_plan(channels: int, m_max: int, parity: str, normalization: str) -> TpPla
 
 @torch.library.custom_op(f"{NAMESPACE}::tp_forward", mutates_args=())
 def tp_forward(left: Tensor, right: Tensor, weight: Tensor, channels: int, m_max: int,
-               parity: str, normalization: str) -> Tensor:
-    """out[N, W] of TensorProduct on flat rows (triton_o2.py:786-875)."""
+               parity: str, normalization: str, layout: int = 0) -> Tensor:
+    """out[N, W] of TensorProduct on flat rows (triton_o2.py:786-875); layout 1 reads
+    and writes component-major frequency blocks in place."""
     require_cuda_float32("TensorProduct", left, right, weight)
     left, right, weight = left.contiguous(), right.contiguous(), weight.contiguous()
     out = torch.empty_like(left)
     with torch.cuda.device(left.device):
-        _lib.tp_forward(left, right, weight, out, channels, m_max, parity, normalization)
+        _lib.tp_forward(left, right, weight, out, channels, m_max, parity, normalization, layout)
     return out
 
 
 @tp_forward.register_fake
-def _tp_forward_fake(left, right, weight, channels, m_max, parity, normalization):
+def _tp_forward_fake(left, right, weight, channels, m_max, parity, normalization, layout=0):
     return torch.empty_like(left)
 
 
 @torch.library.custom_op(f"{NAMESPACE}::tp_backward", mutates_args=())
 def tp_backward(left: Tensor, right: Tensor, weight: Tensor, grad_output: Tensor, channels: int,
-                m_max: int, parity: str, normalization: str) -> tuple[Tensor, Tensor, Tensor]:
+                m_max: int, parity: str, normalization: str, layout: int = 0
+                ) -> tuple[Tensor, Tensor, Tensor]:
     """(dx, dy, dw) of TensorProduct (triton_o2.py:878-966)."""
     require_cuda_float32("TensorProduct backward", left, right, weight, grad_output)
     left, right = left.contiguous(), right.contiguous()
@@ -71,25 +73,26 @@ def tp_backward(left: Tensor, right: Tensor, weight: Tensor, grad_output: Tensor
         size = _lib.tp_backward_workspace(left.shape[0], channels, m_max, parity, left.device)
         workspace = torch.empty(max(size, 1), dtype=torch.uint8, device=left.device)
         _lib.tp_backward(left, right, weight, grad_output, grad_left, grad_right, grad_weight,
-                         workspace, channels, m_max, parity, normalization)
+                         workspace, channels, m_max, parity, normalization, layout)
     return grad_left, grad_right, grad_weight
 
 
 @tp_backward.register_fake
-def _tp_backward_fake(left, right, weight, grad_output, channels, m_max, parity, normalization):
+def _tp_backward_fake(left, right, weight, grad_output, channels, m_max, parity, normalization,
+                      layout=0):
     return torch.empty_like(left), torch.empty_like(right), torch.empty_like(weight)
 
 
 def _tp_setup(ctx, inputs, output):
-    left, right, weight, channels, m_max, parity, normalization = inputs
+    left, right, weight, channels, m_max, parity, normalization, layout = inputs
     ctx.save_for_backward(left, right, weight)
-    ctx.config = (channels, m_max, parity, normalization)
+    ctx.config = (channels, m_max, parity, normalization, layout)
 
 
 def _tp_autograd(ctx, grad_output):
     left, right, weight = ctx.saved_tensors
     gx, gy, gw = tp_backward(left, right, weight, grad_output.contiguous(), *ctx.config)
-    return gx, gy, gw, None, None, None, None
+    return gx, gy, gw, None, None, None, None, None
 
 
 tp_forward.register_autograd(_tp_autograd, setup_context=_tp_setup)
@@ -140,9 +143,9 @@ def torch_tp_flat(left: Tensor, right: Tensor, weight: Tensor, plan: TpPlan) -> 
 
 
 def _tp_backward_setup(ctx, inputs, output):
-    left, right, weight, grad_output, channels, m_max, parity, normalization = inputs
+    left, right, weight, grad_output, channels, m_max, parity, normalization, layout = inputs
     ctx.save_for_backward(left, right, weight, grad_output)
-    ctx.config = (channels, m_max, parity, normalization)
+    ctx.config = (channels, m_max, parity, normalization, layout)
     ctx.set_materialize_grads(False)
 
 
@@ -187,7 +190,7 @@ def _tp_double_backward(ctx, dd_left, dd_right, dd_weight):
             d_g = _accumulate(d_g, tp_forward(left, dd_right, weight, *cfg))
         if dd_weight is not None:
             d_g = _accumulate(d_g, tp_forward(left, right, dd_weight, *cfg))
-    return d_left, d_right, d_weight, d_g, None, None, None, None
+    return d_left, d_right, d_weight, d_g, None, None, None, None, None
 
 
 tp_backward.register_autograd(_tp_double_backward, setup_context=_tp_backward_setup)

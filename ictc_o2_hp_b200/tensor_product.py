@@ -98,10 +98,11 @@ class _TensorProductBase(torch.nn.Module):
             for parameter, (start, end) in zip(reference.weights, self._weight_offsets):
                 self.weight[start:end].copy_(parameter)
 
-    def _flat(self, left: torch.Tensor, right: torch.Tensor) -> torch.Tensor:
+    def _flat(self, left: torch.Tensor, right: torch.Tensor, layout: int = 0) -> torch.Tensor:
         width = self.representation_dimension
         out = ops.tp_forward(left.reshape(-1, width), right.reshape(-1, width), self.weight,
-                             self.channels, self.max_frequency, self.parity, self.normalization)
+                             self.channels, self.max_frequency, self.parity, self.normalization,
+                             layout)
         return out
 
 
@@ -175,5 +176,6 @@ class ComponentMajorTensorProduct(_TensorProductBase):
         if (left.ndim < 1 or left.shape[-1] != self.representation_dimension
                 or right.shape != left.shape):
             raise ValueError("flat O(2) inputs must have the configured width")
-        out = self._flat(self._to_channel_major(left), self._to_channel_major(right))
-        return self._to_component_major(out.reshape(left.shape))
+        # the kernels address component-major frequency blocks in place (the
+        # reference's layout-1/2 metadata, triton_o2.py:114-118)
+        return self._flat(left, right, layout=1).reshape(left.shape)

@@ -38,6 +38,11 @@ enum {
 
 enum { ICTC_PARITY_CANONICAL = 0, ICTC_PARITY_FULL = 1 };
 enum { ICTC_NORM_COMPONENT = 0, ICTC_NORM_NORM = 1 };
+/* Storage order inside the frequency blocks of a TensorProduct row:
+ * [copy][channel][component] (TensorProduct, layout 0 of triton_o2.py:111-113) or
+ * [copy][component][channel] (ComponentMajorTensorProduct, layouts 1 / 2 of
+ * triton_o2.py:114-118, triton_o2.py:1204-1278). */
+enum { ICTC_LAYOUT_CHANNEL_MAJOR = 0, ICTC_LAYOUT_COMPONENT_MAJOR = 1 };
 
 /* Message describing the last non-OK status returned on this thread. */
 ICTC_API const char* ictc_o2_last_error(void);
@@ -73,6 +78,14 @@ ICTC_API int32_t ictc_o2_tp_forward(const float* left, const float* right, const
                            float* output, int64_t rows, int32_t channels, int32_t m_max,
                            int32_t parity, int32_t normalization, void* stream);
 
+/* ictc_o2_tp_forward with the frequency-block storage order `layout`
+ * (ICTC_LAYOUT_*): component-major rows are read and written in place, the
+ * metadata layout field of the reference's o2_forward (triton_o2.py:786-794). */
+ICTC_API int32_t ictc_o2_tp_forward_layout(const float* left, const float* right,
+                                  const float* weight, float* output, int64_t rows,
+                                  int32_t channels, int32_t m_max, int32_t parity,
+                                  int32_t normalization, int32_t layout, void* stream);
+
 /* Workspace bytes needed by ictc_o2_tp_backward on `device` for these sizes. */
 ICTC_API int32_t ictc_o2_tp_backward_workspace(int64_t rows, int32_t channels, int32_t m_max,
                                       int32_t parity, int32_t device, size_t* bytes);
@@ -86,6 +99,16 @@ ICTC_API int32_t ictc_o2_tp_backward(const float* left, const float* right, cons
                             float* grad_weight, void* workspace, size_t workspace_bytes,
                             int64_t rows, int32_t channels, int32_t m_max, int32_t parity,
                             int32_t normalization, void* stream);
+
+/* ictc_o2_tp_backward with the frequency-block storage order `layout` (reference
+ * o2_backward, triton_o2.py:878-887, on layout-1/2 metadata); the workspace is the
+ * same as for ictc_o2_tp_backward. */
+ICTC_API int32_t ictc_o2_tp_backward_layout(const float* left, const float* right,
+                                   const float* weight, const float* grad_output,
+                                   float* grad_left, float* grad_right, float* grad_weight,
+                                   void* workspace, size_t workspace_bytes, int64_t rows,
+                                   int32_t channels, int32_t m_max, int32_t parity,
+                                   int32_t normalization, int32_t layout, void* stream);
 
 /* ictc_o2_tp_backward for callers that cannot allocate device memory (their
  * allocator belongs to a host runtime or a memory pool they must not bypass, or

@@ -234,6 +234,46 @@ def test_tuple_and_component_major_layouts(cuda_device):
     assert torch.equal(comp._to_channel_major(cm), ref)
 
 
+@pytest.mark.parametrize("channels,m_max,parity,rows,variant", [
+    (16, 3, "full", 300, None),
+    (12, 2, "canonical", 77, None),
+    (128, 6, "full", 2048, None),      # the benchmark configuration's width (staged kernels)
+    (9, 4, "full", 50, "direct"),      # odd channel count, direct kernels
+    (32, 2, "full", 640, "grouped"),
+])
+def test_component_major_in_place(channels, m_max, parity, rows, variant, cuda_device,
+                                  monkeypatch):
+    """ComponentMajorTensorProduct reads and writes component-major rows in place
+    (ICTC_LAYOUT_COMPONENT_MAJOR): forward, dx, dy, dw and the second derivatives
+    equal the channel-major product on the converted rows, bit for bit."""
+    from ictc_o2_hp_b200 import ComponentMajorTensorProduct, TensorProduct
+    if variant:
+        monkeypatch.setenv("ICTC_TP_FORWARD", variant)
+    torch.manual_seed(channels + rows)
+    flat = TensorProduct(channels, m_max, parity=parity).to(cuda_device)
+    comp = ComponentMajorTensorProduct(channels, m_max, parity=parity).to(cuda_device)
+    comp.load_state_dict(flat.state_dict())
+    W = flat.representation_dimension
+    x, y, g = (torch.randn(rows, W, device=cuda_device) for _ in range(3))
+    xc, yc, gc = (comp._to_component_major(t) for t in (x, y, g))
+    xf, yf = x.clone().requires_grad_(True), y.clone().requires_grad_(True)
+    xm, ym = xc.clone().requires_grad_(True), yc.clone().requires_grad_(True)
+    ref = flat(xf, yf)
+    got = comp(xm, ym)
+    assert torch.equal(comp._to_channel_major(got), ref)
+    rf = torch.autograd.grad(ref, (xf, yf, flat.weight), g, create_graph=True)
+    rm = torch.autograd.grad(got, (xm, ym, comp.weight), gc, create_graph=True)
+    assert torch.equal(comp._to_channel_major(rm[0]), rf[0])
+    assert torch.equal(comp._to_channel_major(rm[1]), rf[1])
+    assert torch.equal(rm[2], rf[2])
+    # second derivatives: d/d(x, y) of <dx, cot>
+    cot = torch.randn(rows, W, device=cuda_device)
+    sf = torch.autograd.grad((rf[0] * cot).sum(), (yf, flat.weight))
+    sm = torch.autograd.grad((rm[0] * comp._to_component_major(cot)).sum(), (ym, comp.weight))
+    assert torch.equal(comp._to_channel_major(sm[0]), sf[0])
+    assert torch.equal(sm[1], sf[1])
+
+
 @pytest.mark.parametrize("variant", ["staged", "wide", "direct", "grouped"])
 def test_forward_variants_agree(variant, cuda_device, monkeypatch):
     """Every forward kernel selectable with ICTC_TP_FORWARD (staged ring, wide
