@@ -48,6 +48,9 @@ METRICS = {
     "uvu_rowwise": "fwd+VJP rows/s, UvuTensorProduct C128 V32 m3 full per-row weights, "
                    "16384 rows per GPU",
     "radial": "fwd+VJP edges/s, RadialUvuTensorProduct C64 m3 radial MLP 8-64-64, E=1048576",
+    "radial_mp": "fwd+VJP edges/s, message-passing layer: gather by source, "
+                 "RadialUvuTensorProduct C64 m3, fixed-order sum to destinations, E=1048576 "
+                 "over 65536 nodes",
     "radial_m6": "fwd+VJP edges/s, RadialUvuTensorProduct C{channels} m6 full / angular "
                  "canonical, radial MLP 16-64-64, E=131072",
     "radial_m6_force": "force-loss training edges/s (second derivatives), "
@@ -425,6 +428,7 @@ class RadialWorkload(Workload):
         sl = slice(start, stop)
         # gather of node features by source: outside the reference chain
         self.x = nodes[src[sl]].contiguous()
+        self.nodes, self.src_shard, self.dst_shard = nodes, src[sl], dst[sl]
         self.dst = dst[sl]
         self.r = r[sl].contiguous()
         th = theta[sl]
@@ -485,6 +489,52 @@ class RadialWorkload(Workload):
 
     def step_bytes(self):
         return (3 * 896 + 2 * 7 + 64 * 2) * 4 * self.edges
+
+
+class RadialMpWorkload(RadialWorkload):
+    """Config 5 as a message-passing layer: node features gathered by source
+    (ictc_o2_gather_rows), the radial product, messages summed into the destination
+    nodes (ictc_o2_segment_sum, fixed order); the VJP covers the node features, the
+    angular inputs and every parameter.  Edges are sharded; each rank gathers from
+    the full node set and its node gradients join the one all-reduce."""
+
+    name = "radial_mp"
+
+    def __init__(self, args, device, rank, world):
+        super().__init__(args, device, rank, world)
+        from ictc_o2_hp_b200.graph import EdgeIndex, gather, scatter_sum
+        self.gather, self.scatter_sum = gather, scatter_sum
+        self.edge_index = EdgeIndex(self.src_shard, self.dst_shard, self.NODES)
+        self.g_nodes = self.torch.ones_like(self.nodes)
+        self.launches = 10  # + gather, scatter and their adjoints
+
+    def step(self, x=None, y=None, g=None):
+        torch = self.torch
+        nodes = (self.nodes if x is None else x).detach().requires_grad_(True)
+        ang = (self.angular if y is None else y).detach().requires_grad_(True)
+        hidden = self.trunk(self.basis(self.r))
+        messages = self.model(self.gather(nodes, self.edge_index), ang, hidden)
+        out = self.scatter_sum(messages, self.edge_index)
+        grads = torch.autograd.grad(out, [nodes, ang] + self.params,
+                                    self.g_nodes if g is None else g)
+        if self.world > 1:
+            shared = [grads[0]] + list(grads[2:])
+            flat = torch.cat([t.reshape(-1) for t in shared])
+            torch.distributed.all_reduce(flat)
+        return out, grads
+
+    def host_inputs(self):
+        return (self.nodes, self.angular, self.g_nodes)
+
+    def config(self):
+        c = super().config()
+        c["workload"] = ("message-passing layer (config 5 shapes): node features [65536, 896] "
+                         "gathered by source, Bessel(8) x cosine cutoff, MLP 8-64-64 SiLU, fused "
+                         "affine + V=1 uvu C64 m3, messages summed into destination nodes in a "
+                         "fixed order; VJP to node features, angular and all parameters")
+        c["parallelism"] = (f"edge shards on {self.world} GPU(s), full node set per rank, one "
+                            "NCCL all_reduce of node-feature and parameter gradients")
+        return c
 
 
 class RadialM6Workload(Workload):
@@ -620,7 +670,8 @@ class RadialM6ForceWorkload(RadialM6Workload):
 
 
 WORKLOADS = {"tp": TpWorkload, "uvu": UvuWorkload, "uvu_rowwise": UvuRowWorkload,
-             "radial": RadialWorkload, "radial_m6": RadialM6Workload,
+             "radial": RadialWorkload, "radial_mp": RadialMpWorkload,
+             "radial_m6": RadialM6Workload,
              "radial_m6_force": RadialM6ForceWorkload}
 
 
@@ -840,8 +891,10 @@ def run_reference(args) -> dict | None:
     if int(os.environ.get("RANK", "0")) != 0:
         return None
     if args.workload not in CPU_ROWS:
-        return {"impl": "reference", "unavailable": "the CPU oracle has no second derivatives "
-                                                     "(force-loss metric)"}
+        why = ("the reference has no message-passing layer (gather and scatter are outside its "
+               "chain)" if args.workload == "radial_mp" else
+               "the CPU oracle has no second derivatives (force-loss metric)")
+        return {"impl": "reference", "unavailable": why}
     rows = args.cpu_rows or CPU_ROWS[args.workload]
     base = cpu_units_per_second(args.workload, rows, args.steps, max(1, min(args.warmup, 1)),
                                 args.channels)

@@ -54,6 +54,9 @@ SIGNATURES = {
     "ictc_o2_radial_forward": (_i32, [_vp] * 6 + [_i64] + [_i32] * 8 + [_vp, _vp, _size, _vp]),
     "ictc_o2_radial_backward": (_i32, [_vp] * 11 + [_i64] + [_i32] * 8 +
                                 [_i32, _vp, _vp, _size, _vp]),
+    "ictc_o2_gather_rows": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "ictc_o2_segment_sum": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "ictc_o2_graph_bad_index": (_i32, [ctypes.POINTER(_i32)]),
 }
 
 _lock = threading.Lock()
@@ -224,3 +227,25 @@ def radial_backward(left, angular, hidden, alpha, bias, grad_output, gx, gy, gh,
         ptr(left), ptr(angular), ptr(hidden), ptr(alpha), ptr(bias), ptr(grad_output), ptr(gx),
         ptr(gy), ptr(gh), ptr(ga), ptr(gb), left.shape[0], *rconfig, int(needed), ptr(table),
         ptr(workspace), workspace.numel(), stream_of(left.device)), "radial_backward")
+
+
+# ---------------------------------------------------------------------- graph
+
+
+def gather_rows(source, index, out):
+    check(load().ictc_o2_gather_rows(ptr(source), ptr(index), ptr(out), index.shape[0],
+                                     source.shape[1] if source.dim() > 1 else 1,
+                                     source.shape[0], stream_of(out.device)), "gather_rows")
+
+
+def segment_sum(values, offsets, order, out):
+    check(load().ictc_o2_segment_sum(ptr(values), ptr(offsets), ptr(order), ptr(out),
+                                     out.shape[0], out.shape[1] if out.dim() > 1 else 1,
+                                     values.shape[0], stream_of(out.device)), "segment_sum")
+
+
+def graph_bad_index() -> int:
+    """Reads and clears the out-of-range-index flag of the graph kernels."""
+    flag = _i32()
+    check(load().ictc_o2_graph_bad_index(ctypes.byref(flag)), "graph_bad_index")
+    return int(flag.value)

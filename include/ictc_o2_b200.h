@@ -220,6 +220,32 @@ ICTC_API int32_t ictc_o2_radial_backward(const float* left, const float* angular
                                          int32_t needed, const void* device_table,
                                          void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------------
+ * Message-passing plumbing around the radial product (the node gather and the
+ * message sum the reference leaves outside its chain, docs/RADIAL.md:97-99), with a
+ * fixed summation order so that node outputs and gradients are bit-identical
+ * from run to run.
+ * ------------------------------------------------------------------------------ */
+
+/* out[r, :] = source[index[r], :] for r < rows (rows of `width` floats; index into
+ * [0, source_rows)).  An out-of-range index writes a zero row and raises the flag
+ * read by ictc_o2_graph_bad_index. */
+ICTC_API int32_t ictc_o2_gather_rows(const float* source, const int64_t* index, float* out,
+                            int64_t rows, int64_t width, int64_t source_rows, void* stream);
+
+/* out[s, :] = sum of values[order ? order[e] : e, :] for e in [offsets[s],
+ * offsets[s + 1]), added in increasing e (segments = rows of out; offsets has
+ * segments + 1 entries; order indexes [0, value_rows)).  With order = the edges
+ * sorted by destination and offsets = the destinations' CSR pointers this is the
+ * message sum; grouped by source, the node gradient of a gather. */
+ICTC_API int32_t ictc_o2_segment_sum(const float* values, const int64_t* offsets,
+                            const int64_t* order, float* out, int64_t segments, int64_t width,
+                            int64_t value_rows, void* stream);
+
+/* Synchronizes, then reads and clears the out-of-range-index flag of the two
+ * kernels above on the current device (1 = some index was out of range). */
+ICTC_API int32_t ictc_o2_graph_bad_index(int32_t* flag);
+
 #ifdef __cplusplus
 }
 #endif
