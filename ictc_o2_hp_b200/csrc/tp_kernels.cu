@@ -117,46 +117,48 @@ struct GlobalChunks {
 
 // Slot vector of channel c in world q, in the canonical basis: the odd copy
 // (r0, r1) is read as (-r1, r0) (reference fast_o2.py:61-66).
-template <int M, bool FULL, class Row>
+template <int M, bool FULL, bool CM, class Row>
 __device__ __forceinline__ void load_slots(const Row& row, const TpLayout& L, int c, int q,
                                            float (&v)[2 * M + 2]) {
   v[0] = row.ld(c);
   v[1] = FULL ? row.ld(L.C + c) : 0.0f;
-#pragma unroll
-  for (int m = 1; m <= M; ++m) {
-    const int base = L.fbase + (m - 1) * L.fstride;
-    float2 r;
-    if (L.cm) {  // component-major: the two components C apart (triton_o2.py:116-118)
-      const int o = base + 2 * q * L.C + c;
-      r = make_float2(row.ld(o), row.ld(o + L.C));
-    } else {
-      r = row.ld2(base + 2 * (q * L.C + c));
-    }
+  auto put = [&](int m, float2 r) {
     v[2 * m] = q ? -r.y : r.x;
     v[2 * m + 1] = q ? r.x : r.y;
+  };
+  if constexpr (CM) {  // component-major: the two components C apart (triton_o2.py:116-118)
+#pragma unroll
+    for (int m = 1; m <= M; ++m) {
+      const int o = L.fbase + (m - 1) * L.fstride + 2 * q * L.C + c;
+      put(m, make_float2(row.ld(o), row.ld(o + L.C)));
+    }
+  } else {
+#pragma unroll
+    for (int m = 1; m <= M; ++m) put(m, row.ld2(L.fbase + (m - 1) * L.fstride + 2 * (q * L.C + c)));
   }
 }
 
 // Writes the frequency slots of world q; the odd copy (v0, v1) is stored as
 // (v1, -v0) (reference fast_o2.py:68-73).  Scalars are written by world 0.
-template <int M, bool FULL>
+template <int M, bool FULL, bool CM>
 __device__ __forceinline__ void store_slots(float* __restrict__ row, const TpLayout& L, int c,
                                             int q, bool vec2, const float (&v)[2 * M + 2]) {
   if (q == 0) {
     row[c] = v[0];
     if (FULL) row[L.C + c] = v[1];
   }
+  if constexpr (CM) {
 #pragma unroll
-  for (int m = 1; m <= M; ++m) {
-    const float v0 = q ? v[2 * m + 1] : v[2 * m], v1 = q ? -v[2 * m] : v[2 * m + 1];
-    const int base = L.fbase + (m - 1) * L.fstride;
-    if (L.cm) {
-      float* p = row + base + 2 * q * L.C + c;
-      p[0] = v0;
-      p[L.C] = v1;
-    } else {
-      st2(row + base + 2 * (q * L.C + c), v0, v1, vec2);
+    for (int m = 1; m <= M; ++m) {
+      float* p = row + L.fbase + (m - 1) * L.fstride + 2 * q * L.C + c;
+      p[0] = q ? v[2 * m + 1] : v[2 * m];
+      p[L.C] = q ? -v[2 * m] : v[2 * m + 1];
     }
+  } else {
+#pragma unroll
+    for (int m = 1; m <= M; ++m)
+      st2(row + L.fbase + (m - 1) * L.fstride + 2 * (q * L.C + c), q ? v[2 * m + 1] : v[2 * m],
+          q ? -v[2 * m] : v[2 * m + 1], vec2);
   }
 }
 
@@ -365,7 +367,7 @@ struct LaneMap {
 
 // ------------------------------------------------------------ direct kernels
 
-template <int M, bool FULL>
+template <int M, bool FULL, bool CM = false>
 __global__ void __launch_bounds__(kDirectThreads)
     tp_forward_direct(const float* __restrict__ x, const float* __restrict__ y,
                       const float* __restrict__ w, float* __restrict__ out, int64_t rows,
@@ -380,14 +382,14 @@ __global__ void __launch_bounds__(kDirectThreads)
   load_weights<M, FULL>(w, L, mags, lm.c, lm.q, lm.active, wr);
   for (int64_t row = gw / groups; row < rows; row += slots) {
     float a[S], b[S], o[S];
-    load_slots<M, FULL>(GlobalRow{x + row * L.width, vec2}, L, lm.c, lm.q, a);
-    load_slots<M, FULL>(GlobalRow{y + row * L.width, vec2}, L, lm.c, lm.q, b);
+    load_slots<M, FULL, CM>(GlobalRow{x + row * L.width, vec2}, L, lm.c, lm.q, a);
+    load_slots<M, FULL, CM>(GlobalRow{y + row * L.width, vec2}, L, lm.c, lm.q, b);
     row_forward<M, FULL>(a, b, wr, lm.q, o);
-    if (lm.active) store_slots<M, FULL>(out + row * L.width, L, lm.c, lm.q, vec2, o);
+    if (lm.active) store_slots<M, FULL, CM>(out + row * L.width, L, lm.c, lm.q, vec2, o);
   }
 }
 
-template <int M, bool FULL>
+template <int M, bool FULL, bool CM = false>
 __global__ void __launch_bounds__(kDirectThreads)
     tp_backward_direct(const float* __restrict__ x, const float* __restrict__ y,
                        const float4* __restrict__ ws, const float* __restrict__ go,
@@ -406,16 +408,16 @@ __global__ void __launch_bounds__(kDirectThreads)
   for (int i = 0; i < P::n; ++i) acc[i] = 0.0f;
   for (int64_t row = slot; row < rows; row += slots) {
     float a[S], b[S], g[S], dx[S], dy[S];
-    load_slots<M, FULL>(GlobalRow{x + row * L.width, vec2}, L, lm.c, lm.q, a);
-    load_slots<M, FULL>(GlobalRow{y + row * L.width, vec2}, L, lm.c, lm.q, b);
+    load_slots<M, FULL, CM>(GlobalRow{x + row * L.width, vec2}, L, lm.c, lm.q, a);
+    load_slots<M, FULL, CM>(GlobalRow{y + row * L.width, vec2}, L, lm.c, lm.q, b);
     // The output twist (v0, v1) -> (v1, -v0) has the adjoint g -> (-g1, g0),
     // which is the same map as the input read.
-    load_slots<M, FULL>(GlobalRow{go + row * L.width, vec2}, L, lm.c, lm.q, g);
+    load_slots<M, FULL, CM>(GlobalRow{go + row * L.width, vec2}, L, lm.c, lm.q, g);
     const GlobalChunks chunks{ws + static_cast<int>(gw % groups) * 32 + lane, groups * 32};
     row_vjp<M, FULL>(a, b, g, chunks, lm.q, dx, dy, acc);
     if (lm.active) {
-      store_slots<M, FULL>(gx + row * L.width, L, lm.c, lm.q, vec2, dx);
-      store_slots<M, FULL>(gy + row * L.width, L, lm.c, lm.q, vec2, dy);
+      store_slots<M, FULL, CM>(gx + row * L.width, L, lm.c, lm.q, vec2, dx);
+      store_slots<M, FULL, CM>(gy + row * L.width, L, lm.c, lm.q, vec2, dy);
     }
   }
   if (lm.active) store_partial<M, FULL>(partial + slot * numel, L, mags, lm.c, lm.q, acc);
@@ -518,7 +520,7 @@ __device__ __forceinline__ void staged_loop(unsigned char* smem, unsigned char* 
   }
 }
 
-template <int M, bool FULL>
+template <int M, bool FULL, bool CM = false>
 __global__ void __launch_bounds__(kStagedWarps * 32, 1)
     tp_forward_staged(const float* __restrict__ x, const float* __restrict__ y,
                       const float* __restrict__ w, float* __restrict__ out, int64_t rows,
@@ -533,10 +535,10 @@ __global__ void __launch_bounds__(kStagedWarps * 32, 1)
   const int64_t W = L.width;
   staged_loop<2>(smem, smem, stages, R, rows, W, src, [&](const float* stage, int64_t row) {
     float a[S], b[S], o[S];
-    load_slots<M, FULL>(SharedRow(stage), L, lm.c, lm.q, a);
-    load_slots<M, FULL>(SharedRow(stage + R * W), L, lm.c, lm.q, b);
+    load_slots<M, FULL, CM>(SharedRow(stage), L, lm.c, lm.q, a);
+    load_slots<M, FULL, CM>(SharedRow(stage + R * W), L, lm.c, lm.q, b);
     row_forward<M, FULL>(a, b, wr, lm.q, o);
-    if (lm.active) store_slots<M, FULL>(out + row * W, L, lm.c, lm.q, true, o);
+    if (lm.active) store_slots<M, FULL, CM>(out + row * W, L, lm.c, lm.q, true, o);
   });
 }
 
@@ -557,7 +559,7 @@ constexpr size_t wide_forward_smem() {
 template <int M, bool FULL>
 constexpr bool wide_forward_fits() { return wide_forward_smem<M, FULL>() <= kStagedSmemBudget; }
 
-template <int M, bool FULL>
+template <int M, bool FULL, bool CM = false>
 __global__ void __launch_bounds__(kWideWarps * 32, 1)
     tp_forward_wide(const float* __restrict__ x, const float* __restrict__ y,
                     const float* __restrict__ w, float* __restrict__ out, int64_t rows,
@@ -596,8 +598,8 @@ __global__ void __launch_bounds__(kWideWarps * 32, 1)
   const int64_t W = L.width;
   staged_loop<2>(smem, smem + wbytes, stages, R, rows, W, src, [&](const float* stage, int64_t row) {
     float a[S], b[S], o[S];
-    load_slots<M, FULL>(SharedRow(stage), L, lm.c, lm.q, a);
-    load_slots<M, FULL>(SharedRow(stage + R * W), L, lm.c, lm.q, b);
+    load_slots<M, FULL, CM>(SharedRow(stage), L, lm.c, lm.q, a);
+    load_slots<M, FULL, CM>(SharedRow(stage + R * W), L, lm.c, lm.q, b);
 #pragma unroll
     for (int i = 0; i < S; ++i) o[i] = 0.0f;
     float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -612,7 +614,7 @@ __global__ void __launch_bounds__(kWideWarps * 32, 1)
       static_for<P::n - P::nfreq>(
           [&](auto J) { step(std::integral_constant<int, P::nfreq + J>{}); });
     }
-    if (lm.active) store_slots<M, FULL>(out + row * W, L, lm.c, lm.q, true, o);
+    if (lm.active) store_slots<M, FULL, CM>(out + row * W, L, lm.c, lm.q, true, o);
   });
 }
 
@@ -624,7 +626,7 @@ __global__ void __launch_bounds__(kWideWarps * 32, 1)
 // latency of the coalesced global loads of x and y.
 constexpr int kGroupFwdWarps = 4;
 
-template <int M, bool FULL>
+template <int M, bool FULL, bool CM = false>
 __global__ void __launch_bounds__(kGroupFwdWarps * 32)
     tp_forward_grouped(const float* __restrict__ x, const float* __restrict__ y,
                        const float* __restrict__ w, float* __restrict__ out, int64_t rows,
@@ -658,8 +660,8 @@ __global__ void __launch_bounds__(kGroupFwdWarps * 32)
   const int64_t first = static_cast<int64_t>(blockIdx.x / groups) * kGroupFwdWarps + warp;
   for (int64_t row = first; row < rows; row += row_slots) {
     float a[S], b[S], o[S];
-    load_slots<M, FULL>(GlobalRow{x + row * L.width, vec2}, L, lm.c, lm.q, a);
-    load_slots<M, FULL>(GlobalRow{y + row * L.width, vec2}, L, lm.c, lm.q, b);
+    load_slots<M, FULL, CM>(GlobalRow{x + row * L.width, vec2}, L, lm.c, lm.q, a);
+    load_slots<M, FULL, CM>(GlobalRow{y + row * L.width, vec2}, L, lm.c, lm.q, b);
 #pragma unroll
     for (int i = 0; i < S; ++i) o[i] = 0.0f;
     float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -674,11 +676,11 @@ __global__ void __launch_bounds__(kGroupFwdWarps * 32)
       static_for<P::n - P::nfreq>(
           [&](auto J) { step(std::integral_constant<int, P::nfreq + J>{}); });
     }
-    if (lm.active) store_slots<M, FULL>(out + row * L.width, L, lm.c, lm.q, vec2, o);
+    if (lm.active) store_slots<M, FULL, CM>(out + row * L.width, L, lm.c, lm.q, vec2, o);
   }
 }
 
-template <int M, bool FULL>
+template <int M, bool FULL, bool CM = false>
 __global__ void __launch_bounds__(kStagedWarps * 32, 1)
     tp_backward_staged(const float* __restrict__ x, const float* __restrict__ y,
                        const float4* __restrict__ ws, const float* __restrict__ go,
@@ -703,13 +705,13 @@ __global__ void __launch_bounds__(kStagedWarps * 32, 1)
   auto body = [&](const auto& chunks) {
     return [&](const float* stage, int64_t row) {
       float a[S], b[S], g[S], dx[S], dy[S];
-      load_slots<M, FULL>(SharedRow(stage), L, lm.c, lm.q, a);
-      load_slots<M, FULL>(SharedRow(stage + R * W), L, lm.c, lm.q, b);
-      load_slots<M, FULL>(SharedRow(stage + 2 * R * W), L, lm.c, lm.q, g);
+      load_slots<M, FULL, CM>(SharedRow(stage), L, lm.c, lm.q, a);
+      load_slots<M, FULL, CM>(SharedRow(stage + R * W), L, lm.c, lm.q, b);
+      load_slots<M, FULL, CM>(SharedRow(stage + 2 * R * W), L, lm.c, lm.q, g);
       row_vjp<M, FULL>(a, b, g, chunks, lm.q, dx, dy, acc);
       if (lm.active) {
-        store_slots<M, FULL>(gx + row * W, L, lm.c, lm.q, true, dx);
-        store_slots<M, FULL>(gy + row * W, L, lm.c, lm.q, true, dy);
+        store_slots<M, FULL, CM>(gx + row * W, L, lm.c, lm.q, true, dx);
+        store_slots<M, FULL, CM>(gy + row * W, L, lm.c, lm.q, true, dy);
       }
     };
   };
@@ -743,7 +745,7 @@ __global__ void __launch_bounds__(kStagedWarps * 32, 1)
 // Magnitude-scaled weights in the per-thread order of row_vjp: chunk k of thread
 // t (channel group t / 32, lane t % 32) holds the weights of paths vjp[4k..4k+3]
 // for that lane's (channel, world), at ws[k * T + t]; unused entries are zero.
-template <int M, bool FULL>
+template <int M, bool FULL, bool CM = false>
 __global__ void prescale_kernel(const float* __restrict__ w, float4* __restrict__ ws,
                                 TpLayout L, Mags mags, int groups) {
   using P = Paths<M, FULL>;
@@ -831,15 +833,17 @@ struct Kernels {
   ForwardGroupedFn fwd_grouped;
 };
 
-template <int M, bool FULL>
+// Kernels of one (order, parity, frequency-block layout); the layout is a template
+// parameter so that each layout runs its own straight-line slot accesses.
+template <int M, bool FULL, bool CM>
 constexpr Kernels kernels_for() {
   if constexpr (compiled_order(M)) {
     ForwardStagedFn wide = nullptr;
-    if constexpr (wide_forward_fits<M, FULL>()) wide = &tp_forward_wide<M, FULL>;
-    return Kernels{wide, &tp_forward_direct<M, FULL>, &tp_backward_direct<M, FULL>,
-                   &tp_forward_staged<M, FULL>, &tp_backward_staged<M, FULL>,
+    if constexpr (wide_forward_fits<M, FULL>()) wide = &tp_forward_wide<M, FULL, CM>;
+    return Kernels{wide, &tp_forward_direct<M, FULL, CM>, &tp_backward_direct<M, FULL, CM>,
+                   &tp_forward_staged<M, FULL, CM>, &tp_backward_staged<M, FULL, CM>,
                    &prescale_kernel<M, FULL>, Paths<M, FULL>::chunks,
-                   &tp_forward_grouped<M, FULL>};
+                   &tp_forward_grouped<M, FULL, CM>};
   } else {
     return Kernels{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0, nullptr};
   }
@@ -847,8 +851,9 @@ constexpr Kernels kernels_for() {
 
 template <int... Ms>
 constexpr auto make_table(std::integer_sequence<int, Ms...>) {
-  struct T { Kernels k[2][sizeof...(Ms)]; };
-  return T{{{kernels_for<Ms, false>()...}, {kernels_for<Ms, true>()...}}};
+  struct T { Kernels k[2][2][sizeof...(Ms)]; };  // [layout][full][m_max]
+  return T{{{{kernels_for<Ms, false, false>()...}, {kernels_for<Ms, true, false>()...}},
+            {{kernels_for<Ms, false, true>()...}, {kernels_for<Ms, true, true>()...}}}};
 }
 
 const auto kKernels = make_table(std::make_integer_sequence<int, kMaxOrder + 1>{});
@@ -1037,7 +1042,7 @@ int32_t tp_forward_impl(const float* left, const float* right, const float* weig
     return fail(ICTC_ERR_INVALID, "tensor pointers must be 4-byte aligned");
   const bool full = parity == ICTC_PARITY_FULL;
   const TpLayout L = tp_layout(channels, m_max, full, layout);
-  const Kernels& k = kKernels.k[full ? 1 : 0][m_max];
+  const Kernels& k = kKernels.k[L.cm][full ? 1 : 0][m_max];
   const Mags mags = tp_mags(normalization);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int device = 0;
@@ -1141,14 +1146,21 @@ extern "C" int32_t ictc_o2_tp_backward_workspace(int64_t rows, int32_t channels,
     if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
   }
   const bool full = parity == ICTC_PARITY_FULL;
-  const TpLayout L = tp_layout(channels, m_max, full);
-  const int64_t slots =
-      backward_slots(device, kKernels.k[full ? 1 : 0][m_max], rows, L, full, &st);
+  // the larger of the two layouts' needs (their kernels' launch plans may differ)
+  int64_t slots = 0;
+  size_t chunk_bytes = 0;
+  for (int cm = 0; cm < 2 && st == ICTC_OK; ++cm) {
+    const TpLayout L = tp_layout(channels, m_max, full, cm);
+    const Kernels& k = kKernels.k[cm][full ? 1 : 0][m_max];
+    const int64_t s = backward_slots(device, k, rows, L, full, &st);
+    if (s > slots) slots = s;
+    const size_t c = weight_chunk_bytes(k, channels, full);
+    if (c > chunk_bytes) chunk_bytes = c;
+  }
   if (device != prev) cudaSetDevice(prev);
   if (st != ICTC_OK) return st;
   const int64_t numel = weight_numel(channels, m_max, full);
-  *bytes = weight_chunk_bytes(kKernels.k[full ? 1 : 0][m_max], channels, full) +
-           static_cast<size_t>(slots) * numel * sizeof(float);
+  *bytes = chunk_bytes + static_cast<size_t>(slots) * numel * sizeof(float);
   return ICTC_OK;
 }
 
@@ -1180,7 +1192,7 @@ int32_t tp_backward_impl(const float* left, const float* right, const float* wei
       !aligned(grad_weight, 4) || !aligned(workspace, 16))
     return fail(ICTC_ERR_INVALID, "tensor pointers must be 4-byte aligned (workspace 16)");
   const TpLayout L = tp_layout(channels, m_max, full, layout);
-  const Kernels& k = kKernels.k[full ? 1 : 0][m_max];
+  const Kernels& k = kKernels.k[L.cm][full ? 1 : 0][m_max];
   int device = 0;
   if ((st = current_device(&device)) != ICTC_OK) return st;
   const size_t wbytes = weight_chunk_bytes(k, channels, full);
