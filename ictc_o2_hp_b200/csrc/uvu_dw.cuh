@@ -100,10 +100,9 @@ __global__ void __launch_bounds__(256, 1) uvu_dw_stage(DwArgs A) {
 #pragma unroll 4
     for (int rr = 0; rr < kDwRows / 2; ++rr) {
       const int r = gh * (kDwRows / 2) + rr;
-      const float* xr = &S.xs[buf][r][gu * ei.y];
-      const float* gr = &S.gs[buf][r][gu * ek.y];
-      const float x0 = xr[0], x1 = ei.y == 2 ? xr[1] : 0.f;
-      const float g0 = gr[0], g1 = ek.y == 2 ? gr[1] : 0.f;
+      const float2 xv = dy_slot(&S.xs[buf][r][gu * ei.y], ei.y);
+      const float2 gv = dy_slot(&S.gs[buf][r][gu * ek.y], ek.y);
+      const float x0 = xv.x, x1 = xv.y, g0 = gv.x, g1 = gv.y;
       S.S[2 * r][gu] = g0 * fmaf(c[2], x1, c[0] * x0) + g1 * fmaf(c[6], x1, c[4] * x0);
       S.S[2 * r + 1][gu] = g0 * fmaf(c[3], x1, c[1] * x0) + g1 * fmaf(c[7], x1, c[5] * x0);
     }

@@ -48,6 +48,13 @@ __device__ __forceinline__ void dy_cp16(void* smem, const void* gmem, bool valid
                : "memory");
 }
 
+// Both components of a staged one- or two-component slot (the second is 0 for
+// one-component entries); one 8-byte access for two-component slots keeps the
+// lanes of consecutive channels on distinct banks.
+__device__ __forceinline__ float2 dy_slot(const float* p, int dim) {
+  return dim == 2 ? *reinterpret_cast<const float2*>(p) : make_float2(p[0], 0.f);
+}
+
 __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
   extern __shared__ __align__(16) unsigned char dy_raw[];
   DySmem& S = *reinterpret_cast<DySmem*>(dy_raw);
@@ -120,10 +127,9 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
 #pragma unroll 4
     for (int rr = 0; rr < kDyRows / 2; ++rr) {
       const int r = gh * (kDyRows / 2) + rr;
-      const float* xr = &S.xs[r][gu * ei.y];
-      const float* gr = &S.gs[r][gu * ek.y];
-      const float x0 = xr[0], x1 = ei.y == 2 ? xr[1] : 0.f;
-      const float g0 = gr[0], g1 = ek.y == 2 ? gr[1] : 0.f;
+      const float2 xv = dy_slot(&S.xs[r][gu * ei.y], ei.y);
+      const float2 gv = dy_slot(&S.gs[r][gu * ek.y], ek.y);
+      const float x0 = xv.x, x1 = xv.y, g0 = gv.x, g1 = gv.y;
       const float s0 = g0 * fmaf(c[2], x1, c[0] * x0) + g1 * fmaf(c[6], x1, c[4] * x0);
       const float s1 = g0 * fmaf(c[3], x1, c[1] * x0) + g1 * fmaf(c[7], x1, c[5] * x0);
       *reinterpret_cast<float2*>(&S.S[gu][2 * r]) = make_float2(s0, s1);
@@ -150,12 +156,12 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
     if (last) {
       // sum the channel quarters in order: quarters 1..3 park their sums, 0 adds
       __syncthreads();  // every thread is done reading S
-      float* red = &S.S[0][0];  // [3 quarters][64 threads][16]
+      float* red = &S.S[0][0];  // [3 quarters][64 threads][17]: odd stride, no bank conflicts
       if (ug > 0) {
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int k = 0; k < 4; ++k) red[((ug - 1) * 64 + (tid & 63)) * 16 + i * 4 + k] = acc[i][k];
+          for (int k = 0; k < 4; ++k) red[((ug - 1) * 64 + (tid & 63)) * 17 + i * 4 + k] = acc[i][k];
       }
       __syncthreads();
       if (ug == 0) {
@@ -170,7 +176,7 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
               const int v = vq * 4 + k;
               float sum = acc[i][k];
 #pragma unroll
-              for (int q = 0; q < kDyKs - 1; ++q) sum += red[(q * 64 + tid) * 16 + i * 4 + k];
+              for (int q = 0; q < kDyKs - 1; ++q) sum += red[(q * 64 + tid) * 17 + i * 4 + k];
               if (v < A.V) A.dy[row * A.W2 + ej.x + v * ej.y + b] = sum;
             }
           }
