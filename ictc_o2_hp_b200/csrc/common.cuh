@@ -78,4 +78,20 @@ __device__ __forceinline__ void prefetch_l1(const float* p) {
   asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
+// Paired FP32 multiply-add: c + a * b componentwise as one sm_100 f32x2 FMA.
+// Each component is rounded exactly as fmaf(a, b.x, c.x) / fmaf(a, b.y, c.y), so
+// paired and scalar code give bit-identical results; the pair takes one issue
+// slot instead of two.  The outer-product (GEMM) cores keep their accumulators as
+// float2 pairs along the column index and use this for every k step.
+__device__ __forceinline__ float2 fma2(float a, float2 b, float2 c) {
+  return __ffma2_rn(make_float2(a, a), b, c);
+}
+
+// Element j of a row of paired accumulators (j a compile-time constant after
+// unrolling, so this is a register name, not a select).
+template <int N>
+__device__ __forceinline__ float pair_at(const float2 (&v)[N], int j) {
+  return (j & 1) ? v[j >> 1].y : v[j >> 1].x;
+}
+
 }  // namespace ictc

@@ -168,18 +168,19 @@ __device__ __forceinline__ void load_coef(const UvuDev& t, int p, float (&c)[8])
 // rows m0..m0+3 of A[k][64], columns n0..n0+3 and n0+32..n0+35 of B[k][64].
 template <int KS>
 __device__ __forceinline__ void mma_4x8(const float (*A)[64], const float (*B)[64], int m0,
-                                        int n0, float (&acc)[4][8]) {
+                                        int n0, float2 (&acc)[4][4]) {
 #pragma unroll
   for (int k = 0; k < KS; ++k) {
     const float4 a4 = *reinterpret_cast<const float4*>(&A[k][m0]);
     const float4 b0 = *reinterpret_cast<const float4*>(&B[k][n0]);
     const float4 b1 = *reinterpret_cast<const float4*>(&B[k][n0 + 32]);
     const float av[4] = {a4.x, a4.y, a4.z, a4.w};
-    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    const float2 bv[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w),
+                          make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+      for (int j = 0; j < 4; ++j) acc[i][j] = fma2(av[i], bv[j], acc[i][j]);
   }
 }
 
@@ -362,7 +363,7 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
     bulk_g2s(dst, src, bytes, &full[st]);
   };
 
-  float acc[4][CW];
+  float2 acc[4][CW / 2];  // edge-weight tile, paired along the channels
   float res[4][CW][2];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
@@ -384,7 +385,7 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
 #pragma unroll
       for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int b = 0; b < CW; ++b) acc[a][b] = 0.f;
+        for (int b = 0; b < CW / 2; ++b) acc[a][b] = make_float2(0.f, 0.f);
       // Pull the path's epilogue operands (x_i; g_k in dx mode) of this thread's
       // four edges toward L1 while the path's product runs: lane tc takes line tc
       // of each edge's slice, lines that start inside the valid channels only.
@@ -411,16 +412,17 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
     auto kstep = [&](int k) {
       const float4 a4 = *reinterpret_cast<const float4*>(Hb + k * RT + e0);
       const float av[4] = {a4.x, a4.y, a4.z, a4.w};
-      float bv[CW];
+      float2 bv[CW / 2];
 #pragma unroll
       for (int h = 0; h < NH; ++h) {
         const float4 b4 = *reinterpret_cast<const float4*>(Wb + k * UT + h * (UT / NH) + tc * 4);
-        bv[4 * h] = b4.x; bv[4 * h + 1] = b4.y; bv[4 * h + 2] = b4.z; bv[4 * h + 3] = b4.w;
+        bv[2 * h] = make_float2(b4.x, b4.y);
+        bv[2 * h + 1] = make_float2(b4.z, b4.w);
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < CW; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < CW / 2; ++j) acc[i][j] = fma2(av[i], bv[j], acc[i][j]);
     };
     if (kn == kRtKC) {
 #pragma unroll 8
@@ -466,7 +468,7 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
                         A.U, A.vec);
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                float w = acc[ee][half * 4 + q];
+                float w = pair_at(acc[ee], half * 4 + q);
                 if (A.bias != nullptr && u + q < A.U) w += __ldg(A.bias + p * A.U + u + q);
                 const float x0 = xv[q * D1], x1 = D1 == 2 ? xv[q * D1 + 1] : 0.f;
                 float t0 = c00 * x0;
@@ -487,7 +489,7 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
               float gwv[4];
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                float w = acc[ee][half * 4 + q];
+                float w = pair_at(acc[ee], half * 4 + q);
                 if (A.bias != nullptr && u + q < A.U) w += __ldg(A.bias + p * A.U + u + q);
                 const float g0 = gv[q * D3], g1 = D3 == 2 ? gv[q * D3 + 1] : 0.f;
                 const float x0 = xv[q * D1], x1 = D1 == 2 ? xv[q * D1 + 1] : 0.f;
@@ -654,11 +656,11 @@ __global__ void __launch_bounds__(128, 4) radial_dhidden(DhArgs A) {
   const int m0 = (tid >> 3) * 4, n0 = (tid & 7) * 4;
   const int nuc = (A.U + kDhU - 1) / kDhU;
   const int nsteps = A.t.np * nuc;
-  float acc[4][8];
+  float2 acc[4][4];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < 8; ++b) acc[a][b] = 0.f;
+    for (int b = 0; b < 4; ++b) acc[a][b] = make_float2(0.f, 0.f);
 
   GwRegs r;
   float4 av[2];
@@ -722,7 +724,7 @@ __global__ void __launch_bounds__(128, 4) radial_dhidden(DhArgs A) {
 #pragma unroll
     for (int b = 0; b < 8; ++b) {
       const int h = hb + n0 + (b & 3) + (b >> 2) * 32;
-      if (h < A.H) A.dh[e * A.H + h] = acc[a][b];
+      if (h < A.H) A.dh[e * A.H + h] = pair_at(acc[a], b);
     }
   }
 }
@@ -761,11 +763,12 @@ __device__ __forceinline__ void radial_dalpha_body(const DaArgs& A, float (*gwt)
   const int m0 = (tid >> 3) * 4, n0 = (tid & 7) * 4;
   const int64_t rbeg = static_cast<int64_t>(blockIdx.z) * A.chunk_rows;
   const int64_t rend = rbeg + A.chunk_rows < A.rows ? rbeg + A.chunk_rows : A.rows;
-  float acc[4][8], bsum[8];
+  float2 acc[4][4];
+  float bsum[8];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < 8; ++b) acc[a][b] = 0.f;
+    for (int b = 0; b < 4; ++b) acc[a][b] = make_float2(0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < 8; ++i) bsum[i] = 0.f;
   GwRegs r;
@@ -828,7 +831,7 @@ __device__ __forceinline__ void radial_dalpha_body(const DaArgs& A, float (*gwt)
 #pragma unroll
     for (int b = 0; b < 8; ++b) {
       const int h = hb + n0 + (b & 3) + (b >> 2) * 32;
-      if (h < A.H) dout[(static_cast<int64_t>(p) * A.U + u) * A.H + h] = acc[a][b];
+      if (h < A.H) dout[(static_cast<int64_t>(p) * A.U + u) * A.H + h] = pair_at(acc[a], b);
     }
   }
   if (A.db != nullptr && hb == 0) {

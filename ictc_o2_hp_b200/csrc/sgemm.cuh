@@ -20,6 +20,8 @@
 
 #include <cstdint>
 
+#include "common.cuh"
+
 namespace ictc {
 
 constexpr int kGemmBM = 128, kGemmBN = 64, kGemmBK = 16, kGemmThreads = 128;
@@ -39,8 +41,12 @@ __device__ __forceinline__ void sg_cp16(void* smem, const void* gmem, bool valid
                : "memory");
 }
 
+// The accumulators are float2 pairs along the columns (paired f32x2 FMAs, half the
+// issue slots of scalar FMAs, bit-identical results).  Register pairs cost the
+// [M][K] variant its fit in 128 registers next to the register-staged A rows, so
+// it runs 3 CTAs per SM (166 registers) instead of 4 with spills.
 template <bool A_KMAJOR>
-__global__ void __launch_bounds__(kGemmThreads, 4) sgemm_tile(SgemmArgs G) {
+__global__ void __launch_bounds__(kGemmThreads, A_KMAJOR ? 4 : 3) sgemm_tile(SgemmArgs G) {
   __shared__ __align__(16) float As[2][kGemmBK][kGemmBM];
   __shared__ __align__(16) float Bs[2][kGemmBK][kGemmBN];
   const int tid = threadIdx.x;
@@ -101,11 +107,11 @@ __global__ void __launch_bounds__(kGemmThreads, 4) sgemm_tile(SgemmArgs G) {
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
 
-  float acc[8][8];
+  float2 acc[8][4];  // paired along the columns
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
 
   if (nsteps > 0) {
     if (!A_KMAJOR) {
@@ -130,11 +136,12 @@ __global__ void __launch_bounds__(kGemmThreads, 4) sgemm_tile(SgemmArgs G) {
       const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tn * 4]);
       const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][32 + tn * 4]);
       const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      const float2 bv[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w),
+                            make_float2(b1.x, b1.y), make_float2(b1.z, b1.w)};
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < 4; ++j) acc[i][j] = fma2(av[i], bv[j], acc[i][j]);
     }
     if (more && !A_KMAJOR) store_a_rows(buf ^ 1);
   }
@@ -146,7 +153,7 @@ __global__ void __launch_bounds__(kGemmThreads, 4) sgemm_tile(SgemmArgs G) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int64_t n = n0 + (j < 4 ? tn * 4 + j : 32 + tn * 4 + j - 4);
-      if (n < G.N) C[m * G.ldc + n] = acc[i][j];
+      if (n < G.N) C[m * G.ldc + n] = pair_at(acc[i], j);
     }
   }
 }

@@ -87,11 +87,11 @@ __global__ void __launch_bounds__(256, 1) uvu_dw_stage(DwArgs A) {
   const int gu = tid & 127, gh = tid >> 7;
   // GEMM: u quad uq (0..31), v quad vq (0..7)
   const int uq = tid >> 3, vq = tid & 7;
-  float acc[4][4];
+  float2 acc[4][2];  // paired along v
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+    for (int b = 0; b < 2; ++b) acc[a][b] = make_float2(0.f, 0.f);
   for (int64_t step = 0; step < nsteps; ++step) {
     const int buf = static_cast<int>(step & 1);
     asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -118,11 +118,11 @@ __global__ void __launch_bounds__(256, 1) uvu_dw_stage(DwArgs A) {
       const float4 a4 = *reinterpret_cast<const float4*>(&S.S[k][uq * 4]);
       const float4 b4 = *reinterpret_cast<const float4*>(&S.Y[k][vq * 4]);
       const float av[4] = {a4.x, a4.y, a4.z, a4.w};
-      const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+      const float2 bv[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        for (int j = 0; j < 2; ++j) acc[i][j] = fma2(av[i], bv[j], acc[i][j]);
     }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(256, 1) uvu_dw_stage(DwArgs A) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int v = vq * 4 + j;
-      if (v < A.V) out[static_cast<int64_t>(u) * A.V + v] = acc[i][j];
+      if (v < A.V) out[static_cast<int64_t>(u) * A.V + v] = pair_at(acc[i], j);
     }
   }
 }

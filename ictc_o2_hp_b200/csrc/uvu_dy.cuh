@@ -108,11 +108,11 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
   // GEMM: (row, b) quad rq (0..7), v quad vq (0..7), u quarter ug (0..3)
   const int ug = tid >> 6, rq = (tid & 63) >> 3, vq = tid & 7;
   constexpr int kUq = kDyU / kDyKs;
-  float acc[4][4];
+  float2 acc[4][2];  // paired along v
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+    for (int b = 0; b < 2; ++b) acc[a][b] = make_float2(0.f, 0.f);
   for (int pos = 0; pos < np; ++pos) {
     const int buf = pos & 1;
     asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -146,11 +146,11 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
       const float4 a4 = *reinterpret_cast<const float4*>(&S.S[u][rq * 4]);
       const float4 b4 = *reinterpret_cast<const float4*>(&S.wp[buf][u][vq * 4]);
       const float av[4] = {a4.x, a4.y, a4.z, a4.w};
-      const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+      const float2 bv[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) acc[i][k] = fmaf(av[i], bv[k], acc[i][k]);
+        for (int k = 0; k < 2; ++k) acc[i][k] = fma2(av[i], bv[k], acc[i][k]);
     }
     const bool last = pos + 1 == np || A.t.paths[A.t.by_j[pos + 1]].y != pt.y;
     if (last) {
@@ -161,7 +161,8 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int k = 0; k < 4; ++k) red[((ug - 1) * 64 + (tid & 63)) * 17 + i * 4 + k] = acc[i][k];
+          for (int k = 0; k < 4; ++k)
+            red[((ug - 1) * 64 + (tid & 63)) * 17 + i * 4 + k] = pair_at(acc[i], k);
       }
       __syncthreads();
       if (ug == 0) {
@@ -174,7 +175,7 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const int v = vq * 4 + k;
-              float sum = acc[i][k];
+              float sum = pair_at(acc[i], k);
 #pragma unroll
               for (int q = 0; q < kDyKs - 1; ++q) sum += red[(q * 64 + tid) * 17 + i * 4 + k];
               if (v < A.V) A.dy[row * A.W2 + ej.x + v * ej.y + b] = sum;
@@ -185,7 +186,7 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) acc[i][k] = 0.f;
+        for (int k = 0; k < 2; ++k) acc[i][k] = make_float2(0.f, 0.f);
     }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");

@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(UtShape<UT, NH>::NT, 1) uvu_tile(UvuTileArgs A
     }
   };
 
-  float acc[2][4][CW];
+  float2 acc[2][4][CW / 2];  // projections, paired along the channels
   float res[4][CW][2];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
@@ -184,18 +184,19 @@ __global__ void __launch_bounds__(UtShape<UT, NH>::NT, 1) uvu_tile(UvuTileArgs A
 #pragma unroll
         for (int a = 0; a < 4; ++a)
 #pragma unroll
-          for (int j = 0; j < CW; ++j) acc[b][a][j] = 0.f;
+          for (int j = 0; j < CW / 2; ++j) acc[b][a][j] = make_float2(0.f, 0.f);
     }
     const int v0 = ck * kUtVC;
     const int kn = A.V - v0 < kUtVC ? A.V - v0 : kUtVC;
     const float* Wb = Wt + st * vc * UT;
     auto gemm = [&]<int D2>() {
       for (int v = 0; v < kn; ++v) {
-        float wv[CW];
+        float2 wv[CW / 2];
 #pragma unroll
         for (int h = 0; h < NH; ++h) {
           const float4 w4 = *reinterpret_cast<const float4*>(Wb + v * UT + h * (UT / NH) + tc * 4);
-          wv[4 * h] = w4.x; wv[4 * h + 1] = w4.y; wv[4 * h + 2] = w4.z; wv[4 * h + 3] = w4.w;
+          wv[2 * h] = make_float2(w4.x, w4.y);
+          wv[2 * h + 1] = make_float2(w4.z, w4.w);
         }
 #pragma unroll
         for (int b = 0; b < D2; ++b) {
@@ -205,7 +206,7 @@ __global__ void __launch_bounds__(UtShape<UT, NH>::NT, 1) uvu_tile(UvuTileArgs A
 #pragma unroll
           for (int i = 0; i < 4; ++i)
 #pragma unroll
-            for (int j = 0; j < CW; ++j) acc[b][i][j] = fmaf(av[i], wv[j], acc[b][i][j]);
+            for (int j = 0; j < CW / 2; ++j) acc[b][i][j] = fma2(av[i], wv[j], acc[b][i][j]);
         }
       }
     };
@@ -241,7 +242,7 @@ __global__ void __launch_bounds__(UtShape<UT, NH>::NT, 1) uvu_tile(UvuTileArgs A
                          u, A.U, A.vec);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              const float p0 = acc[0][ee][half * 4 + q], p1 = acc[1][ee][half * 4 + q];
+              const float p0 = pair_at(acc[0][ee], half * 4 + q), p1 = pair_at(acc[1][ee], half * 4 + q);
               const float x0 = xv[q * D1], x1 = D1 == 2 ? xv[q * D1 + 1] : 0.f;
               // out[kc] += sum_{a,b} c[4 kc + 2 a + b] x[a] proj[b]
               float t0 = fmaf(c[1], p1, c[0] * p0);
@@ -261,7 +262,7 @@ __global__ void __launch_bounds__(UtShape<UT, NH>::NT, 1) uvu_tile(UvuTileArgs A
                          u, A.U, A.vec);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              const float p0 = acc[0][ee][half * 4 + q], p1 = acc[1][ee][half * 4 + q];
+              const float p0 = pair_at(acc[0][ee], half * 4 + q), p1 = pair_at(acc[1][ee], half * 4 + q);
               const float g0 = gv[q * D3], g1 = D3 == 2 ? gv[q * D3 + 1] : 0.f;
               // dx[a] += sum_{kc,b} c[4 kc + 2 a + b] g[kc] proj[b]
               float s0 = g0 * fmaf(c[1], p1, c[0] * p0);
