@@ -364,11 +364,11 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
   };
 
   float2 acc[4][CW / 2];  // edge-weight tile, paired along the channels
-  float res[4][CW][2];
+  float2 res[4][CW];  // output (forward) or dx (dx mode) components of each channel
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < CW; ++b) res[a][b][0] = res[a][b][1] = 0.f;
+    for (int b = 0; b < CW; ++b) res[a][b] = make_float2(0.f, 0.f);
 
   if (tid == 0)
     for (int T = 0; T < kRtStages && T < ntiles; ++T) issue(T, T);
@@ -448,6 +448,11 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
       const int2 ei = in1[pt.x], ej = in2[pt.y], ek = in1[pt.z];
       const float* c = coef + 8 * p;
       const int key = MODE == kRtFwd ? pt.z : pt.x;
+      // The coefficient pairs below feed paired f32x2 operations (`fma2`, `__fmul2_rn`):
+      // each component is computed in the same operation order as the scalar form,
+      // so the results are bit-identical to it with half the issue slots.
+      const float2 k01 = make_float2(c[0], c[1]), k23 = make_float2(c[2], c[3]);
+      const float2 k45 = make_float2(c[4], c[5]), k67 = make_float2(c[6], c[7]);
       with_dims(ei.y, ek.y, [&]<int D1, int D3>() {
 #pragma unroll
         for (int ee = 0; ee < 4; ++ee) {
@@ -456,9 +461,10 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
           const bool row_ok = row < A.rows;
           const float y0 = angt[r * W2s + ej.x];
           const float y1 = ej.y == 2 ? angt[r * W2s + ej.x + 1] : 0.f;
+          // C[kc][a] = sum_b c[4 kc + 2 a + b] y_b
           const float c00 = fmaf(c[0], y0, c[1] * y1), c01 = fmaf(c[2], y0, c[3] * y1);
           const float c10 = fmaf(c[4], y0, c[5] * y1), c11 = fmaf(c[6], y0, c[7] * y1);
-          float dyp0 = 0.f, dyp1 = 0.f;
+          float2 dyp = make_float2(0.f, 0.f);
 #pragma unroll
           for (int half = 0; half < NH; ++half) {
             const int u = ub + half * (UT / NH) + tc * 4;
@@ -466,18 +472,22 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
               float xv[4 * D1];
               load4<D1>(xv, A.opnd + row * A.W1 + ei.x + static_cast<int64_t>(u) * D1, row_ok, u,
                         A.U, A.vec);
+              // out[kc] += w sum_a C[kc][a] x[a], both kc at once: (C00, C10) x0 + (C01, C11) x1
+              const float2 ca0 = make_float2(c00, c10), ca1 = make_float2(c01, c11);
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 float w = pair_at(acc[ee], half * 4 + q);
                 if (A.bias != nullptr && u + q < A.U) w += __ldg(A.bias + p * A.U + u + q);
                 const float x0 = xv[q * D1], x1 = D1 == 2 ? xv[q * D1 + 1] : 0.f;
-                float t0 = c00 * x0;
-                if (D1 == 2) t0 = fmaf(c01, x1, t0);
-                res[ee][half * 4 + q][0] = fmaf(w, t0, res[ee][half * 4 + q][0]);
+                float2& o = res[ee][half * 4 + q];
                 if (D3 == 2) {
-                  float t1 = c10 * x0;
-                  if (D1 == 2) t1 = fmaf(c11, x1, t1);
-                  res[ee][half * 4 + q][1] = fmaf(w, t1, res[ee][half * 4 + q][1]);
+                  float2 t = __fmul2_rn(make_float2(x0, x0), ca0);
+                  if (D1 == 2) t = fma2(x1, ca1, t);
+                  o = fma2(w, t, o);
+                } else {
+                  float t0 = c00 * x0;
+                  if (D1 == 2) t0 = fmaf(c01, x1, t0);
+                  o.x = fmaf(w, t0, o.x);
                 }
               }
             } else {
@@ -486,6 +496,8 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
                         A.U, A.vec);
               load4<D1>(xv, A.x + row * A.W1 + ei.x + static_cast<int64_t>(u) * D1, row_ok, u,
                         A.U, A.vec);
+              // dx[a] += w sum_kc C[kc][a] g[kc], both a at once: (C00, C01) g0 + (C10, C11) g1
+              const float2 ck0 = make_float2(c00, c01), ck1 = make_float2(c10, c11);
               float gwv[4];
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
@@ -493,27 +505,24 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
                 if (A.bias != nullptr && u + q < A.U) w += __ldg(A.bias + p * A.U + u + q);
                 const float g0 = gv[q * D3], g1 = D3 == 2 ? gv[q * D3 + 1] : 0.f;
                 const float x0 = xv[q * D1], x1 = D1 == 2 ? xv[q * D1 + 1] : 0.f;
-                // dx[a] += w sum_kc C[kc][a] g[kc]
-                float s0 = c00 * g0;
-                if (D3 == 2) s0 = fmaf(c10, g1, s0);
-                res[ee][half * 4 + q][0] = fmaf(w, s0, res[ee][half * 4 + q][0]);
+                float2& o = res[ee][half * 4 + q];
                 if (D1 == 2) {
-                  float s1 = c01 * g0;
-                  if (D3 == 2) s1 = fmaf(c11, g1, s1);
-                  res[ee][half * 4 + q][1] = fmaf(w, s1, res[ee][half * 4 + q][1]);
+                  float2 sv = __fmul2_rn(ck0, make_float2(g0, g0));
+                  if (D3 == 2) sv = fma2(g1, ck1, sv);
+                  o = fma2(w, sv, o);
+                } else {
+                  float s0 = c00 * g0;
+                  if (D3 == 2) s0 = fmaf(c10, g1, s0);
+                  o.x = fmaf(w, s0, o.x);
                 }
-                // dy[b] += w sum_{kc,a} c[kc][a][b] g[kc] x[a]  (index 4 kc + 2 a + b)
-                float d0 = c[0] * g0 * x0, d1 = c[1] * g0 * x0;
-                if (D1 == 2) { d0 = fmaf(c[2] * g0, x1, d0); d1 = fmaf(c[3] * g0, x1, d1); }
-                if (D3 == 2) { d0 = fmaf(c[4] * g1, x0, d0); d1 = fmaf(c[5] * g1, x0, d1); }
-                if (D1 == 2 && D3 == 2) {
-                  d0 = fmaf(c[6] * g1, x1, d0);
-                  d1 = fmaf(c[7] * g1, x1, d1);
-                }
-                dyp0 = fmaf(w, d0, dyp0);
-                dyp1 = fmaf(w, d1, dyp1);
+                // (dy0, dy1) += w sum_{kc,a} (c[4 kc + 2 a], c[4 kc + 2 a + 1]) g[kc] x[a]
+                float2 d = __fmul2_rn(__fmul2_rn(k01, make_float2(g0, g0)), make_float2(x0, x0));
+                if (D1 == 2) d = fma2(x1, __fmul2_rn(k23, make_float2(g0, g0)), d);
+                if (D3 == 2) d = fma2(x0, __fmul2_rn(k45, make_float2(g1, g1)), d);
+                if (D1 == 2 && D3 == 2) d = fma2(x1, __fmul2_rn(k67, make_float2(g1, g1)), d);
+                dyp = fma2(w, d, dyp);
                 // gw = sum_b y_b sum_{kc,a} c[kc][a][b] g[kc] x[a]
-                gwv[q] = fmaf(y0, d0, y1 * d1);
+                gwv[q] = fmaf(y0, d.x, y1 * d.y);
               }
               if (A.gw != nullptr && row_ok) {
                 // streaming stores (evict first): the gw block is far larger than L2
@@ -531,6 +540,7 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
           }
           if (MODE == kRtDx) {
             // sum over the TC threads that share these edges (consecutive lanes)
+            float dyp0 = dyp.x, dyp1 = dyp.y;
 #pragma unroll
             for (int m = 1; m < TC; m <<= 1) {
               dyp0 += __shfl_xor_sync(0xffffffffu, dyp0, m);
@@ -558,15 +568,15 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
             float v[4][2];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              v[q][0] = res[ee][half * 4 + q][0];
-              v[q][1] = res[ee][half * 4 + q][1];
+              v[q][0] = res[ee][half * 4 + q].x;
+              v[q][1] = res[ee][half * 4 + q].y;
             }
             float* dst = A.out + row * A.W1 + eo.x + static_cast<int64_t>(u) * dd;
             if (dd == 2) store4<2>(dst, v, row_ok, u, A.U, A.vec);
             else store4<1>(dst, v, row_ok, u, A.U, A.vec);
           }
 #pragma unroll
-          for (int b = 0; b < CW; ++b) res[ee][b][0] = res[ee][b][1] = 0.f;
+          for (int b = 0; b < CW; ++b) res[ee][b] = make_float2(0.f, 0.f);
         }
       }
     }
