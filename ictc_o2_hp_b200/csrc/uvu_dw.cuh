@@ -58,20 +58,22 @@ __global__ void __launch_bounds__(256, 1) uvu_dw_stage(DwArgs A) {
     if (step < nsteps) {
       const int64_t r0 = rbeg + step * kDwRows;
       const int nv = rend - r0 < kDwRows ? static_cast<int>(rend - r0) : kDwRows;
-      for (int q = tid; q < kDwRows * nx; q += 256) {
-        const int r = q / nx, cc = q - r * nx;
+      // thread -> float4 column tid % 64 of rows tid / 64 + 4 k (x, g: <= 64 columns)
+      // and column tid % 16 of row tid / 16 (y: <= 16 columns): no index division
+      const int cc = tid & 63, rb = tid >> 6;
+#pragma unroll
+      for (int k = 0; k < kDwRows / 4; ++k) {
+        const int r = rb + 4 * k;
         const bool ok = r < nv;
-        dy_cp16(&S.xs[buf][r][cc * 4], ok ? A.x + (r0 + r) * A.W1 + ei.x + cc * 4 : A.x, ok);
+        if (cc < nx)
+          dy_cp16(&S.xs[buf][r][cc * 4], ok ? A.x + (r0 + r) * A.W1 + ei.x + cc * 4 : A.x, ok);
+        if (cc < ng)
+          dy_cp16(&S.gs[buf][r][cc * 4], ok ? A.g + (r0 + r) * A.W1 + ek.x + cc * 4 : A.g, ok);
       }
-      for (int q = tid; q < kDwRows * ng; q += 256) {
-        const int r = q / ng, cc = q - r * ng;
-        const bool ok = r < nv;
-        dy_cp16(&S.gs[buf][r][cc * 4], ok ? A.g + (r0 + r) * A.W1 + ek.x + cc * 4 : A.g, ok);
-      }
-      for (int q = tid; q < kDwRows * ny; q += 256) {
-        const int r = q / ny, cc = q - r * ny;
-        const bool ok = r < nv;
-        dy_cp16(&S.ys[buf][r][cc * 4], ok ? A.y + (r0 + r) * A.W2 + ej.x + cc * 4 : A.y, ok);
+      const int yc = tid & 15, yr = tid >> 4;
+      if (yc < ny) {
+        const bool ok = yr < nv;
+        dy_cp16(&S.ys[buf][yr][yc * 4], ok ? A.y + (r0 + yr) * A.W2 + ej.x + yc * 4 : A.y, ok);
       }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");

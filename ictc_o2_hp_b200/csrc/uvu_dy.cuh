@@ -68,16 +68,17 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
       const int p = A.t.by_j[pos];
       const int4 pt = A.t.paths[p];
       const int2 ei = A.t.in1[pt.x], ek = A.t.in1[pt.z];
-      const int nx = A.U * ei.y / 4, ng = A.U * ek.y / 4;  // float4 per row
-      for (int q = tid; q < kDyRows * nx; q += 256) {
-        const int r = q / nx, c = q - r * nx;
+      const int nx = A.U * ei.y / 4, ng = A.U * ek.y / 4;  // float4 per row (<= 64)
+      // thread -> float4 column tid % 64 of rows tid / 64 + 4 k: no index division
+      const int c = tid & 63, rb = tid >> 6;
+#pragma unroll
+      for (int k = 0; k < kDyRows / 4; ++k) {
+        const int r = rb + 4 * k;
         const bool ok = r < nvalid;
-        dy_cp16(&S.xs[r][c * 4], ok ? A.x + (row0 + r) * A.W1 + ei.x + c * 4 : A.x, ok);
-      }
-      for (int q = tid; q < kDyRows * ng; q += 256) {
-        const int r = q / ng, c = q - r * ng;
-        const bool ok = r < nvalid;
-        dy_cp16(&S.gs[r][c * 4], ok ? A.g + (row0 + r) * A.W1 + ek.x + c * 4 : A.g, ok);
+        if (c < nx)
+          dy_cp16(&S.xs[r][c * 4], ok ? A.x + (row0 + r) * A.W1 + ei.x + c * 4 : A.x, ok);
+        if (c < ng)
+          dy_cp16(&S.gs[r][c * 4], ok ? A.g + (row0 + r) * A.W1 + ek.x + c * 4 : A.g, ok);
       }
     }
   };
@@ -85,11 +86,15 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
   auto issue_w = [&](int pos, int buf) {
     if (pos < np) {
       const int p = A.t.by_j[pos];
-      const int nw = A.U * A.V / 4;
       const float* wsrc = A.w + static_cast<int64_t>(p) * A.U * A.V;
-      for (int q = tid; q < nw; q += 256) {
-        const int u = (q * 4) / A.V, v = q * 4 - u * A.V;
-        dy_cp16(&S.wp[buf][u][v], wsrc + q * 4, true);
+      // thread -> float4 column tid % 8 of channels tid / 8 + 32 k (V <= 32, U <= 128)
+      const int c = tid & 7, ub = tid >> 3;
+      if (4 * c < A.V) {
+#pragma unroll
+        for (int k = 0; k < kDyU / 32; ++k) {
+          const int u = ub + 32 * k;
+          if (u < A.U) dy_cp16(&S.wp[buf][u][4 * c], wsrc + u * A.V + 4 * c, true);
+        }
       }
     }
   };
