@@ -373,13 +373,23 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
   if (tid == 0)
     for (int T = 0; T < kRtStages && T < ntiles; ++T) issue(T, T);
   bool ok = true;
-  for (int T = 0; T < ntiles && ok; ++T) {
+  // (channel tile, path position, hidden chunk) of tile T, advanced per tile: T runs
+  // over ck fastest, then pos, then the channel tile (no division per tile)
+  int ck = 0, pos = 0, ub = tile_ub(0);
+  auto advance = [&]() {
+    if (++ck == nkc) {
+      ck = 0;
+      if (++pos == np) {
+        pos = 0;
+        ub += UT;
+      }
+    }
+  };
+  for (int T = 0; T < ntiles && ok; ++T, advance()) {
     const int st = T % kRtStages;
     const uint32_t round = static_cast<uint32_t>(T / kRtStages);
     ok = mbar_wait(&full[st], round & 1, 5);
     if (!ok) break;
-    const int pos = (T / nkc) % np, ck = T % nkc;
-    const int ub = tile_ub(T);
     const int p = order[pos];
     if (ck == 0) {
 #pragma unroll

@@ -169,12 +169,19 @@ __global__ void __launch_bounds__(UtShape<UT, NH>::NT, 1) uvu_tile(UvuTileArgs A
   if (tid == 0)
     for (int T = 0; T < kUtStages && T < ntiles; ++T) issue(T, T);
   bool ok = true;
-  for (int T = 0; T < ntiles && ok; ++T) {
+  // (path position, weight chunk) of tile T, advanced per tile (no division per tile)
+  int pos = 0, ck = 0;
+  auto advance = [&]() {
+    if (++ck == nkc) {
+      ck = 0;
+      ++pos;
+    }
+  };
+  for (int T = 0; T < ntiles && ok; ++T, advance()) {
     const int st = T % kUtStages;
     const uint32_t round = static_cast<uint32_t>(T / kUtStages);
     ok = mbar_wait(&full[st], round & 1, 7);
     if (!ok) break;
-    const int pos = T / nkc, ck = T - pos * nkc;
     const int p = order[pos];
     const int4 pt = paths[p];
     const int2 ej = in2[pt.y];
