@@ -203,6 +203,10 @@ class Workload:
         """Results read back to the host in the end-to-end figure (all of them)."""
         return _leaves(results)
 
+    def collective_numel(self) -> int:
+        """float32 elements of the one all-reduce a step makes with N > 1 ranks."""
+        return 0
+
 
 class TpWorkload(Workload):
     """Config 2: TensorProduct(128, 6, 'full') fwd + VJP, 65,536 rows per GPU."""
@@ -273,6 +277,9 @@ class TpWorkload(Workload):
     def step_bytes(self):
         return 32 * self.W * self.rows
 
+    def collective_numel(self):
+        return self.tp.weight.numel()
+
 
 class UvuWorkload(Workload):
     """Config 4 (shared weights): UvuTensorProduct(128, 32, 3) fwd + VJP."""
@@ -331,6 +338,9 @@ class UvuWorkload(Workload):
     def step_bytes(self):
         return (3 * self.tp.input1_dimension + self.tp.input2_dimension) * 4 * self.rows * 2
 
+    def collective_numel(self):
+        return self.tp.weight_numel
+
 
 class UvuRowWorkload(UvuWorkload):
     """Config 4 (per-row weights): UvuTensorProduct(128, 32, 3), an (N, weight_numel)
@@ -383,6 +393,9 @@ class UvuRowWorkload(UvuWorkload):
     def e2e_outputs(self, results):
         # out, dx and dy; dw (2.4 MB per row, like the weights) stays on the device
         return results[:3]
+
+    def collective_numel(self):
+        return 0
 
     def config(self):
         return {"workload": f"UvuTensorProduct(128, 32, 3, parity='full') per-row weights, "
@@ -490,6 +503,9 @@ class RadialWorkload(Workload):
     def step_bytes(self):
         return (3 * 896 + 2 * 7 + 64 * 2) * 4 * self.edges
 
+    def collective_numel(self):
+        return sum(p.numel() for p in self.params)
+
 
 class RadialMpWorkload(RadialWorkload):
     """Config 5 as a message-passing layer: node features gathered by source
@@ -525,6 +541,9 @@ class RadialMpWorkload(RadialWorkload):
 
     def host_inputs(self):
         return (self.nodes, self.angular, self.g_nodes)
+
+    def collective_numel(self):
+        return self.nodes.numel() + sum(p.numel() for p in self.params)
 
     def config(self):
         c = super().config()
@@ -630,6 +649,9 @@ class RadialM6Workload(Workload):
         w1 = self.x.shape[1]
         return (3 * w1 + 2 * 13 + 2 * 16 + 64 * 2) * 4 * self.edges
 
+    def collective_numel(self):
+        return sum(p.numel() for p in self.params)
+
 
 class RadialM6ForceWorkload(RadialM6Workload):
     """Force-loss training through the published radial chain (second derivatives,
@@ -706,38 +728,58 @@ def run_gpu(args) -> dict | None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
-        wl.step()
-    barrier()
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
-        time.sleep(0.3)
+    def timed_steps(w, steps, warmup, clocks=None):
+        """Device time of `steps` steps after `warmup`, barrier and synchronize on
+        both sides, max over ranks (ms per step)."""
+        for _ in range(warmup):
+            w.step()
+        barrier()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if clocks is not None:
+            time.sleep(0.3)
         start.record()
-        for _ in range(args.steps):
-            wl.step()
+        for _ in range(steps):
+            w.step()
         end.record()
         torch.cuda.synchronize()
-        time.sleep(0.2)
-    barrier()
-    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+        if clocks is not None:
+            time.sleep(0.2)
+        barrier()
+        return max_over_ranks(start.elapsed_time(end) / steps)
+
+    with ClockSampler(local_rank) as clocks:
+        ms = timed_steps(wl, args.steps, args.warmup, clocks)
 
     # Per-kernel timing for the roofline, on the launching (current) stream.
-    def time_op(fn):
+    def time_op(fn, steps=None):
+        steps = steps or args.steps
         for _ in range(2):
             fn()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             fn()
         b.record()
         torch.cuda.synchronize()
-        return a.elapsed_time(b) / args.steps
+        return a.elapsed_time(b) / steps
+
+    def time_allreduce(numel):
+        """The step's one all-reduce timed by itself on a buffer of its size (ms,
+        max over ranks); None with one rank (no collective)."""
+        if world == 1 or numel == 0:
+            return None
+        buf = torch.ones(numel, device=device)
+        barrier()
+        t = time_op(lambda: dist.all_reduce(buf), steps=20)
+        return max_over_ranks(t)
 
     with torch.no_grad():
         kernels, bound = wl.kernels(time_op)
     kernels = {k: (max_over_ranks(t), work) for k, (t, work) in kernels.items()}
+    collective = {"allreduce_bytes": 4 * wl.collective_numel(),
+                  "allreduce_ms": time_allreduce(wl.collective_numel())}
 
     # End to end through the public API with host buffers: H2D of this step's
     # inputs from pinned memory, forward + VJP, D2H of every result.
@@ -810,6 +852,27 @@ def run_gpu(args) -> dict | None:
                "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in host_out),
                "steps": e2e_steps}
 
+    # The north-star multi-GPU target: config 5 (1,048,576 edges in total, strong
+    # scaling) measured in the same run as the default workload.
+    radial = None
+    if args.workload == "tp" and not args.no_radial_scaling:
+        del wl.x, wl.y, wl.g
+        torch.cuda.empty_cache()
+        rargs = argparse.Namespace(**{**vars(args), "rows": 0})
+        rw = RadialWorkload(rargs, device, rank, world)
+        rsteps = max(3, min(args.steps, 10))
+        rms = timed_steps(rw, rsteps, 3)
+        with torch.no_grad():
+            rk, _ = rw.kernels(lambda fn: time_op(fn, steps=rsteps))
+        rk = {k: max_over_ranks(t) for k, (t, _) in rk.items()}
+        radial = {"metric": METRICS["radial"], "value": rw.total / (rms * 1e-3),
+                  "unit": "edges/s", "scaling": "strong", "ms_per_step": rms, "steps": rsteps,
+                  "edges_total": rw.total, "edges_per_gpu": rw.edges,
+                  "kernel_ms_max_over_ranks": rk,
+                  "allreduce_bytes": 4 * rw.collective_numel(),
+                  "allreduce_ms": time_allreduce(rw.collective_numel())}
+        del rw
+
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
@@ -853,8 +916,11 @@ def run_gpu(args) -> dict | None:
         "gpu_launches": wl.launches * args.steps,
         "clocks": clocks.summary(),
     }
+    result["collective"] = collective
     if e2e is not None:
         result["e2e"] = e2e
+    if radial is not None:
+        result["radial_strong_scaling"] = radial
     return result
 
 
@@ -885,15 +951,105 @@ def _leaves(value):
             yield from _leaves(v)
 
 
+# ------------------------------------------------------------------ config-3 sweep
+
+SWEEP_CHANNELS = (32, 64, 96, 128, 256)
+SWEEP_M_MAX = (1, 2, 3, 4, 5, 6)
+SWEEP_PARITY = ("canonical", "full")
+SWEEP_ROWS = (16384, 32768, 65536, 131072)
+
+
+def run_sweep(args) -> dict:
+    """Config 3: TensorProduct over m_max 1-6 x C {32, 64, 96, 128, 256} x parity x
+    N {16,384, 32,768, 65,536, 131,072}, iid N(0, 1) inputs (seed per shape), ones
+    cotangent; forward and forward + VJP timed separately, each launch alone with
+    CUDA events and an L2 flush (a 256 MB write) before it, median of the steps."""
+    import torch
+    from ictc_o2_hp_b200 import TensorProduct, ops
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    hbm = float(peaks()[0]["hbm_gbs"])
+    steps = max(3, min(args.steps, 10))
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
+
+    def median_ms(fn):
+        for _ in range(2):
+            fn()
+        times = []
+        for _ in range(steps):
+            flush.fill_(1.0)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        return statistics.median(times)
+
+    shapes = []
+    launches = 0
+    with ClockSampler(0) as clocks:
+        for channels in SWEEP_CHANNELS:
+            for m_max in SWEEP_M_MAX:
+                for parity in SWEEP_PARITY:
+                    torch.manual_seed(channels * 100 + m_max * 10 + (parity == "full"))
+                    tp = TensorProduct(channels, m_max, parity=parity).to(device)
+                    W = tp.representation_dimension
+                    top = max(SWEEP_ROWS)
+                    x = torch.randn(top, W, device=device)
+                    y = torch.randn(top, W, device=device)
+                    g = torch.ones(top, W, device=device)
+                    for rows in SWEEP_ROWS:
+                        xs, ys, gs = x[:rows], y[:rows], g[:rows]
+                        w = tp.weight.detach()
+
+                        def forward():
+                            ops.tp_forward(xs, ys, w, channels, m_max, parity, "component")
+
+                        def forward_vjp():
+                            xx = xs.detach().requires_grad_(True)
+                            yy = ys.detach().requires_grad_(True)
+                            out = tp(xx, yy)
+                            torch.autograd.grad(out, (xx, yy, tp.weight), gs)
+
+                        fwd = median_ms(forward)
+                        both = median_ms(forward_vjp)
+                        launches += 5 * (steps + 2)
+                        shapes.append({
+                            "channels": channels, "m_max": m_max, "parity": parity,
+                            "rows": rows, "width": W, "fwd_ms": fwd, "fwd_vjp_ms": both,
+                            "fwd_hbm_frac": 12 * W * rows / (fwd * 1e-3) / 1e9 / hbm,
+                            "fwd_vjp_hbm_frac": 32 * W * rows / (both * 1e-3) / 1e9 / hbm})
+                    del x, y, g, tp
+                    torch.cuda.empty_cache()
+    fracs = [s["fwd_vjp_hbm_frac"] for s in shapes]
+    geo = math.exp(sum(math.log(f) for f in fracs) / len(fracs))
+    total_ms = sum(s["fwd_vjp_ms"] for s in shapes)
+    return {
+        "metric": "TensorProduct shape sweep (config 3): geometric mean over 240 shapes of the "
+                  "fwd+VJP fraction of measured HBM (32 W B per row)",
+        "value": geo, "unit": "fraction of measured HBM", "n_gpus": 1, "steps": steps,
+        "warmup": 2, "ms_per_step": total_ms, "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded iid N(0,1) inputs, seeded init, ones cotangent)",
+        "config": {"workload": "m_max 1-6 x C {32,64,96,128,256} x parity {canonical, full} x "
+                               "N {16384, 32768, 65536, 131072}; forward and forward + VJP "
+                               "timed separately per launch",
+                   "l2": "L2 flushed (256 MB write) before every timed launch"},
+        "gpu_launches": launches, "clocks": clocks.summary(), "shapes": shapes}
+
+
 # ------------------------------------------------------------------ reference arm
 
 def run_reference(args) -> dict | None:
     if int(os.environ.get("RANK", "0")) != 0:
         return None
     if args.workload not in CPU_ROWS:
-        why = ("the reference has no message-passing layer (gather and scatter are outside its "
-               "chain)" if args.workload == "radial_mp" else
-               "the CPU oracle has no second derivatives (force-loss metric)")
+        why = {"radial_mp": "the reference has no message-passing layer (gather and scatter "
+                            "are outside its chain)",
+               "sweep": "the shape sweep is timed on the GPU only; the CPU reference arm "
+                        "runs on the single-config workloads"}.get(
+            args.workload, "the CPU oracle has no second derivatives (force-loss metric)")
         return {"impl": "reference", "unavailable": why}
     rows = args.cpu_rows or CPU_ROWS[args.workload]
     base = cpu_units_per_second(args.workload, rows, args.steps, max(1, min(args.warmup, 1)),
@@ -923,7 +1079,7 @@ def main(argv=None) -> int:
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    parser.add_argument("--workload", choices=tuple(WORKLOADS), default="tp")
+    parser.add_argument("--workload", choices=tuple(WORKLOADS) + ("sweep",), default="tp")
     parser.add_argument("--rows", type=int, default=0,
                         help="rows per GPU (tp, uvu) or total edges (radial); 0 = config")
     parser.add_argument("--channels", type=int, default=64,
@@ -932,6 +1088,8 @@ def main(argv=None) -> int:
                         help="rows per host core per CPU-baseline step; 0 = default")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-radial-scaling", action="store_true",
+                        help="tp workload: skip the config-5 strong-scaling companion line")
     args = parser.parse_args(argv)
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
@@ -944,6 +1102,10 @@ def main(argv=None) -> int:
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.workload == "sweep":
+        if rank == 0:
+            print(json.dumps(run_sweep(args)), flush=True)
+        return 0
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in CPU_ROWS:
         # The process pool starts before the first CUDA call (spawned workers).

@@ -28,6 +28,7 @@ SIGNATURES = {
     "ictc_o2_last_error": (ctypes.c_char_p, []),
     "ictc_o2_abi_version": (_i32, []),
     "ictc_o2_device_error": (_i32, [ctypes.POINTER(_i32)]),
+    "ictc_o2_test_wait_timeout": (_i32, [_i32, _vp, _vp]),
     "ictc_o2_tp_weight_numel": (_i32, [_i32, _i32, _i32, ctypes.POINTER(_i64)]),
     "ictc_o2_tp_path_table": (_i32, [_i32, _i32, ctypes.POINTER(_i32), _i32,
                                      ctypes.POINTER(_i32)]),
@@ -112,6 +113,13 @@ def device_error() -> int:
     code = _i32()
     check(load().ictc_o2_device_error(ctypes.byref(code)), "device_error")
     return int(code.value)
+
+
+def test_wait_timeout(limit_us: int, waited_ok) -> None:
+    """Launches the bounded-wait probe (a wait that can never complete, limit
+    `limit_us`); `waited_ok` is a one-element int32 CUDA tensor that receives 0."""
+    check(load().ictc_o2_test_wait_timeout(int(limit_us), ptr(waited_ok),
+                                           stream_of(waited_ok.device)), "test_wait_timeout")
 
 
 def tp_weight_numel(channels: int, m_max: int, parity: str) -> int:

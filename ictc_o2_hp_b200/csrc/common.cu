@@ -68,11 +68,20 @@ extern "C" const char* ictc_o2_last_error(void) { return ictc::g_message; }
 
 extern "C" int32_t ictc_o2_device_error(int32_t* code) {
   if (code == nullptr) return ictc::fail(ICTC_ERR_INVALID, "code is null");
-  int value = 0;
-  const int st = ictc::tp_take_device_error(&value);
-  if (st != ICTC_OK) return st;
-  *code = value;
+  const cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return ictc::cuda_fail(e, "cudaDeviceSynchronize");
+  // every unit's flag is read and cleared; the first nonzero code is reported
+  int (*const units[])(int*) = {ictc::tp_take_device_error, ictc::uvu_take_device_error,
+                                ictc::radial_take_device_error, ictc::probe_take_device_error};
+  int first = 0;
+  for (auto take : units) {
+    int value = 0;
+    const int st = take(&value);
+    if (st != ICTC_OK) return st;
+    if (first == 0) first = value;
+  }
+  *code = first;
   return ICTC_OK;
 }
 
-extern "C" int32_t ictc_o2_abi_version(void) { return 101; }
+extern "C" int32_t ictc_o2_abi_version(void) { return 102; }

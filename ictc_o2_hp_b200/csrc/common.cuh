@@ -21,9 +21,13 @@ int cuda_fail(cudaError_t err, const char* what);
 // SM count and the current device; cached per device.
 int sm_count(int device);
 
-// Reads and clears the device error flag of the TensorProduct kernels on the
-// current device (nonzero: a bounded wait ran out).
+// Each translation unit whose kernels hold bounded waits reads and clears its own
+// copy of the device error flag on the current device (nonzero: a bounded wait ran
+// out); the caller synchronizes the device first.
 int tp_take_device_error(int* code);
+int uvu_take_device_error(int* code);
+int radial_take_device_error(int* code);
+int probe_take_device_error(int* code);
 
 // Opts a kernel into `bytes` of dynamic shared memory (cached per kernel).
 int allow_smem(const void* kernel, size_t bytes);

@@ -60,8 +60,13 @@ __global__ void __launch_bounds__(kGraphThreads) segment_sum_kernel(
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (kGraphThreads / 32);
   for (int64_t s = static_cast<int64_t>(blockIdx.x) * (kGraphThreads / 32) + (threadIdx.x >> 5);
        s < segments; s += warps) {
-    const int64_t e0 = __ldg(offsets + s), e1 = __ldg(offsets + s + 1);
+    int64_t e0 = __ldg(offsets + s), e1 = __ldg(offsets + s + 1);
     float* dst = out + s * width;
+    if (e0 < 0 || e1 < e0 || e1 > value_rows) {
+      // not a CSR range of the value / order rows: flag it, sum nothing
+      if (lane == 0) atomicExch(bad, 1);
+      e0 = e1 = 0;
+    }
     if (vec) {
       float4* d4 = reinterpret_cast<float4*>(dst);
       for (int64_t c = lane; c < width / 4; c += 32) {

@@ -593,7 +593,7 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
   }
   if (!ok && tid == 0) {
     // a wait ran out: let copies already issued land before the CTA exits
-    for (int st = 0; st < kRtStages; ++st) mbar_wait(&full[st], 0, 6);
+    for (int st = 0; st < kRtStages; ++st) mbar_wait(&full[st], 0, 6, kDrainLimitNs);
   }
   if (MODE == kRtDx) {
     __syncthreads();
@@ -1034,6 +1034,12 @@ int64_t radial_chunks(int device, int64_t rows, int P, int U, int H) {
 }
 
 }  // namespace
+
+int radial_take_device_error(int* code) {
+  cudaError_t e;
+  if (take_unit_device_error(code, &e) != 0) return cuda_fail(e, "radial device error flag");
+  return ICTC_OK;
+}
 
 }  // namespace ictc
 

@@ -529,7 +529,7 @@ __device__ __forceinline__ void staged_loop(unsigned char* smem, unsigned char* 
   }
   if (!ok && threadIdx.x == 0) {
     // a wait ran out: let copies already issued land before the CTA exits
-    for (int st = 0; st < stages; ++st) mbar_wait(&ring.full[st], 0, 3);
+    for (int st = 0; st < stages; ++st) mbar_wait(&ring.full[st], 0, 3, kDrainLimitNs);
   }
 }
 
@@ -990,15 +990,8 @@ int64_t backward_slots(int device, const Kernels& k, int64_t rows, const TpLayou
 }  // namespace
 
 int tp_take_device_error(int* code) {
-  int value = 0;
-  cudaError_t e = cudaDeviceSynchronize();
-  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
-  e = cudaMemcpyFromSymbol(&value, g_ictc_device_error, sizeof(int));
-  if (e != cudaSuccess) return cuda_fail(e, "read device error flag");
-  const int zero = 0;
-  e = cudaMemcpyToSymbol(g_ictc_device_error, &zero, sizeof(int));
-  if (e != cudaSuccess) return cuda_fail(e, "clear device error flag");
-  *code = value;
+  cudaError_t e;
+  if (take_unit_device_error(code, &e) != 0) return cuda_fail(e, "TensorProduct device error flag");
   return ICTC_OK;
 }
 

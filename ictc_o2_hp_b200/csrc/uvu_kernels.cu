@@ -489,6 +489,12 @@ int64_t dw_chunks(int device, int64_t rows, int P, int U, int V) {
 
 }  // namespace
 
+int uvu_take_device_error(int* code) {
+  cudaError_t e;
+  if (take_unit_device_error(code, &e) != 0) return cuda_fail(e, "uvu device error flag");
+  return ICTC_OK;
+}
+
 }  // namespace ictc
 
 using namespace ictc;

@@ -372,7 +372,7 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowquad(RowStreamArgs A) {
   }
   if (!ok && tid == 0) {
     // a wait ran out: let copies already issued land before the CTA exits
-    for (int st = 0; st < NS; ++st) mbar_wait(&full[st], 0, 12);
+    for (int st = 0; st < NS; ++st) mbar_wait(&full[st], 0, 12, kDrainLimitNs);
   }
 }
 

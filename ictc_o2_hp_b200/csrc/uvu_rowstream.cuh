@@ -287,6 +287,6 @@ __global__ void __launch_bounds__(kRsThreads, 2) uvu_rowstream(RowStreamArgs A) 
   }
   if (!ok && tid == 0) {
     // a wait ran out: let copies already issued land before the CTA exits
-    for (int st = 0; st < kRsStages; ++st) mbar_wait(&full[st], 0, 10);
+    for (int st = 0; st < kRsStages; ++st) mbar_wait(&full[st], 0, 10, kDrainLimitNs);
   }
 }

@@ -313,7 +313,7 @@ __global__ void __launch_bounds__(UtShape<UT, NH>::NT, 1) uvu_tile(UvuTileArgs A
   }
   if (!ok && tid == 0) {
     // a wait ran out: let copies already issued land before the CTA exits
-    for (int st = 0; st < kUtStages; ++st) mbar_wait(&full[st], 0, 8);
+    for (int st = 0; st < kUtStages; ++st) mbar_wait(&full[st], 0, 8, kDrainLimitNs);
   }
 }
 

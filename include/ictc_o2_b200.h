@@ -51,10 +51,23 @@ ICTC_API const char* ictc_o2_last_error(void);
 ICTC_API int32_t ictc_o2_abi_version(void);
 
 /* Synchronizes with the current device, then reads and clears the kernels'
- * device-side error flag: 0 = none; nonzero = a bounded wait inside a kernel ran
- * out and that kernel stopped early (its outputs are invalid).  No counterpart in
- * the reference, whose Triton kernels have no waits. */
+ * device-side error flags (one per compiled unit: TensorProduct, uvu, radial and
+ * the wait probe below) and returns the first nonzero code in that order: 0 = none;
+ * nonzero = a bounded wait inside a kernel ran out (2 s of the GPU's global timer)
+ * and that kernel stopped early, so its outputs are invalid.  Codes: 1-4
+ * TensorProduct staged kernels (stage ring, drain, weight copy), 5-6 radial edge
+ * tile, 7-8 shared-weight uvu tile, 9-10 per-row uvu streamed kernel, 11-12
+ * per-row uvu quad kernel, 13 the wait probe.  No counterpart in the reference,
+ * whose Triton kernels have no waits. */
 ICTC_API int32_t ictc_o2_device_error(int32_t* code);
+
+/* Test hook, no counterpart in the reference: launches one CTA that waits, with the
+ * kernels' bounded-wait helper and a limit of `limit_us` microseconds (1 to
+ * 1,000,000), on an mbarrier that nothing arrives at.  The wait runs out, the CTA
+ * records code 13 in the device error flag and exits; *waited_ok (a device int)
+ * receives 0.  Read the code with ictc_o2_device_error. */
+ICTC_API int32_t ictc_o2_test_wait_timeout(int32_t limit_us, int32_t* waited_ok,
+                                           void* stream);
 
 /* ---------------------------------------------------------------- TensorProduct
  * Flat channel-major operands of width W = C * (2 * m_max + 1) * (full ? 2 : 1),
@@ -235,7 +248,10 @@ ICTC_API int32_t ictc_o2_gather_rows(const float* source, const int64_t* index, 
 
 /* out[s, :] = sum of values[order ? order[e] : e, :] for e in [offsets[s],
  * offsets[s + 1]), added in increasing e (segments = rows of out; offsets has
- * segments + 1 entries; order indexes [0, value_rows)).  With order = the edges
+ * segments + 1 entries; order, when given, has value_rows entries, each in
+ * [0, value_rows)).  A segment whose offsets fall outside [0, value_rows] or
+ * decrease, and any out-of-range order entry, raise the flag read by
+ * ictc_o2_graph_bad_index; such a segment is written as zeros.  With order = the edges
  * sorted by destination and offsets = the destinations' CSR pointers this is the
  * message sum; grouped by source, the node gradient of a gather. */
 ICTC_API int32_t ictc_o2_segment_sum(const float* values, const int64_t* offsets,

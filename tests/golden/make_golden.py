@@ -149,6 +149,259 @@ def _radial_case(name, u, m_max, hidden, bias, rows, seed):
     print("wrote", name)
 
 
+def _chunks(rows, size):
+    for start in range(0, rows, size):
+        yield start, min(rows, start + size)
+
+
+def _uvu_cfg4_shared(chunk=4096):
+    """Config 4 with shared weights at its full 131,072 rows: the reference's float64
+    CPU path over row chunks, the weight gradient summed across chunks (the
+    validator's pattern, benchmarks/eqx/scripts/validate_math.py:54-74).  Kept:
+    sampled rows, per-column sums of out / dx / dy and the whole dw."""
+    torch = _torch()
+    import recipes as R
+    from ictc_o2_hp import ReferenceUvuTensorProduct
+    c = R.CFG4
+    tp = ReferenceUvuTensorProduct(c["u"], c["v"], c["m_max"], shared_weights=True).double()
+    x, y, w, g = R.cfg4_shared_inputs()
+    n = x.shape[0]
+    keep = np.asarray(R.CFG4_SHARED_KEEP)
+    wd = torch.from_numpy(w).double().requires_grad_(True)
+    sums = {k: np.zeros(c["width2"] if k == "dy" else c["width1"]) for k in ("out", "dx", "dy")}
+    rows = {k: np.zeros((len(keep), c["width2"] if k == "dy" else c["width1"]))
+            for k in ("out", "dx", "dy")}
+    dw = np.zeros(c["weight_numel"])
+    for s, e in _chunks(n, chunk):
+        xx = torch.from_numpy(x[s:e]).double().requires_grad_(True)
+        yy = torch.from_numpy(y[s:e]).double().requires_grad_(True)
+        out = tp(xx, yy, wd)
+        gx, gy, gw = torch.autograd.grad(out, (xx, yy, wd), torch.from_numpy(g[s:e]).double())
+        dw += gw.numpy()
+        for key, value in (("out", out.detach()), ("dx", gx), ("dy", gy)):
+            v = value.numpy()
+            sums[key] += v.sum(axis=0)
+            sel = (keep >= s) & (keep < e)
+            rows[key][sel] = v[keep[sel] - s]
+        print(f"  cfg4 shared rows {e}/{n}", flush=True)
+    record = {f"{k}_f64_rows": rows[k] for k in rows}
+    record.update({f"{k}_f64_sum": sums[k] for k in sums})
+    record.update(dw_f64=dw, keep_rows=keep, rows=n, seed=R.CFG4_SHARED_SEED)
+    np.savez_compressed(HERE / "full_uvu_cfg4_shared.npz", **record)
+    print("wrote full_uvu_cfg4_shared")
+
+
+def _uvu_cfg4_perrow():
+    """Config 4 with per-row weights: the reference's float64 values of the sampled
+    rows (each row's inputs from its own seeded stream, recipes.cfg4_perrow_row)."""
+    torch = _torch()
+    import recipes as R
+    from ictc_o2_hp import ReferenceUvuTensorProduct
+    c = R.CFG4
+    tp = ReferenceUvuTensorProduct(c["u"], c["v"], c["m_max"], shared_weights=False).double()
+    parts = [R.cfg4_perrow_row(r) for r in R.CFG4_PERROW_KEEP]
+    x, y, w, g = (torch.from_numpy(np.stack([p[i] for p in parts])).double() for i in range(4))
+    x.requires_grad_(True), y.requires_grad_(True), w.requires_grad_(True)
+    out = tp(x, y, w)
+    dx, dy, dw = torch.autograd.grad(out, (x, y, w), g)
+    # a row of dw is as large as a row of weights (606,208 values): keep a fixed
+    # strided subset of its entries (every row is also checked in full on the GPU
+    # against the float64 formula)
+    cols = np.asarray(R.CFG4_PERROW_DW_COLUMNS)
+    np.savez_compressed(
+        HERE / "full_uvu_cfg4_perrow_rows.npz", keep_rows=np.asarray(R.CFG4_PERROW_KEEP),
+        rows=R.CFG4_PERROW_ROWS, seed=R.CFG4_PERROW_SEED, out_f64=out.detach().numpy(),
+        dx_f64=dx.numpy(), dy_f64=dy.numpy(), dw_columns=cols, dw_f64=dw.numpy()[:, cols])
+    print("wrote full_uvu_cfg4_perrow_rows")
+
+
+def _radial_cfg5(chunk=8192):
+    """Config 5 at its full 1,048,576 edges through the reference's composition
+    ``tp(left, angular, radial_out(hidden))`` (radial_uvu.py:50-52) in float64 on the
+    CPU, over edge chunks with the affine-layer gradients summed across chunks
+    (the accumulation of radial_streamed.py:126-138).  Kept: sampled edges,
+    per-column sums of out / dx / dangular / dhidden, the whole dalpha and dbias."""
+    torch = _torch()
+    import recipes as R
+    from ictc_o2_hp import RadialUvuTensorProduct, ReferenceUvuTensorProduct
+    c = R.CFG5
+    d = R.cfg5_inputs()
+    tp = ReferenceUvuTensorProduct(c["u"], 1, c["m_max"], parity="full",
+                                   parity_in2="canonical", shared_weights=False)
+    lin = torch.nn.Linear(c["hidden"], c["weight_numel"], bias=True)
+    with torch.no_grad():
+        lin.weight.copy_(torch.from_numpy(d["alpha"]))
+        lin.bias.copy_(torch.from_numpy(d["bias"]))
+    module = RadialUvuTensorProduct(tp, lin).double()
+    params = (module.radial_out.weight, module.radial_out.bias)
+    n = d["src"].shape[0]
+    keep = np.asarray(R.CFG5_KEEP)
+    widths = {"out": c["width1"], "dx": c["width1"], "dy": c["width2"], "dh": c["hidden"]}
+    sums = {k: np.zeros(v) for k, v in widths.items()}
+    rows = {k: np.zeros((len(keep), v)) for k, v in widths.items()}
+    da = np.zeros((c["weight_numel"], c["hidden"]))
+    db = np.zeros(c["weight_numel"])
+    for s, e in _chunks(n, chunk):
+        xx = torch.from_numpy(d["nodes"][d["src"][s:e]]).double().requires_grad_(True)
+        yy = torch.from_numpy(d["angular"][s:e]).double().requires_grad_(True)
+        hh = torch.from_numpy(d["hidden"][s:e]).double().requires_grad_(True)
+        out = module(xx, yy, hh)
+        gx, gy, gh, ga, gb = torch.autograd.grad(
+            out, (xx, yy, hh, *params), torch.from_numpy(d["g"][s:e]).double())
+        da += ga.numpy()
+        db += gb.numpy()
+        for key, value in (("out", out.detach()), ("dx", gx), ("dy", gy), ("dh", gh)):
+            v = value.numpy()
+            sums[key] += v.sum(axis=0)
+            sel = (keep >= s) & (keep < e)
+            rows[key][sel] = v[keep[sel] - s]
+        if (e // chunk) % 16 == 0 or e == n:
+            print(f"  cfg5 edges {e}/{n}", flush=True)
+    record = {f"{k}_f64_rows": rows[k] for k in rows}
+    record.update({f"{k}_f64_sum": sums[k] for k in sums})
+    record.update(da_f64=da, db_f64=db, keep_rows=keep, edges=n, seed=R.CFG5_SEED)
+    np.savez_compressed(HERE / "full_radial_cfg5.npz", **record)
+    print("wrote full_radial_cfg5")
+
+
+def _second_order(create, inputs, first_roles, extra=()):
+    """Second derivatives of S = sum_r <d(out . g)/d role_r, h_r> with respect to every
+    operand and the cotangent g, by the reference's own autograd (create_graph)."""
+    torch = _torch()
+    out = create(*inputs)
+    g, hs = extra[0], extra[1:]
+    firsts = torch.autograd.grad(out, first_roles, g, create_graph=True)
+    total = sum((f * h).sum() for f, h in zip(firsts, hs))
+    return torch.autograd.grad(total, (*first_roles, g))
+
+
+def _tp_second_case(name, channels, m_max, parity, normalization, rows, seed):
+    """TensorProduct second derivatives (reference CPU autograd over fast_o2.py:80-149,
+    the map whose double backward triton_o2.py:1041-1069 recomputes)."""
+    torch = _torch()
+    from ictc_o2_hp import TensorProduct
+    tp = TensorProduct(channels, m_max, parity=parity, normalization=normalization)
+    tp = tp.to(torch.float64)
+    tp.internal_compute_dtype = torch.float64
+    width = tp.representation_dimension
+    rng = np.random.default_rng(seed)
+    arrays = {k: rng.standard_normal((rows, width)).astype(np.float32)
+              for k in ("x", "y", "g", "hx", "hy")}
+    arrays["w"] = rng.standard_normal(tp.weight.numel()).astype(np.float32)
+    arrays["hw"] = rng.standard_normal(tp.weight.numel()).astype(np.float32)
+    t = {k: torch.from_numpy(v).double() for k, v in arrays.items()}
+    with torch.no_grad():
+        tp.weight.copy_(t["w"])
+    x, y, g = (t[k].requires_grad_(True) for k in ("x", "y", "g"))
+    sx, sy, sw, sg = _second_order(lambda a, b: tp(a, b), (x, y), (x, y, tp.weight),
+                                   (g, t["hx"], t["hy"], t["hw"]))
+    np.savez_compressed(HERE / f"{name}.npz", channels=channels, m_max=m_max, parity=parity,
+                        normalization=normalization, **arrays, sx_f64=sx.numpy(),
+                        sy_f64=sy.numpy(), sw_f64=sw.numpy(), sg_f64=sg.numpy())
+    print("wrote", name)
+
+
+def _uvu_second_case(name, u, v, m_max, shared, rows, seed):
+    torch = _torch()
+    from ictc_o2_hp import ReferenceUvuTensorProduct
+    tp = ReferenceUvuTensorProduct(u, v, m_max, shared_weights=shared,
+                                   internal_weights=False).double()
+    rng = np.random.default_rng(seed)
+    wshape = (tp.weight_numel,) if shared else (rows, tp.weight_numel)
+    arrays = {"x": rng.standard_normal((rows, tp.input1_dimension)),
+              "y": rng.standard_normal((rows, tp.input2_dimension)),
+              "w": rng.standard_normal(wshape) / np.sqrt(v),
+              "g": rng.standard_normal((rows, tp.representation_dimension)),
+              "hx": rng.standard_normal((rows, tp.input1_dimension)),
+              "hy": rng.standard_normal((rows, tp.input2_dimension)),
+              "hw": rng.standard_normal(wshape)}
+    arrays = {k: a.astype(np.float32) for k, a in arrays.items()}
+    t = {k: torch.from_numpy(a).double() for k, a in arrays.items()}
+    x, y, w, g = (t[k].requires_grad_(True) for k in ("x", "y", "w", "g"))
+    sx, sy, sw, sg = _second_order(lambda a, b, c: tp(a, b, c), (x, y, w), (x, y, w),
+                                   (g, t["hx"], t["hy"], t["hw"]))
+    np.savez_compressed(HERE / f"{name}.npz", u=u, v=v, m_max=m_max, shared=shared, **arrays,
+                        sx_f64=sx.numpy(), sy_f64=sy.numpy(), sw_f64=sw.numpy(),
+                        sg_f64=sg.numpy())
+    print("wrote", name)
+
+
+def _radial_second_case(name, u, m_max, hidden, bias, rows, seed):
+    """Radial second derivatives through the reference composition (the map whose
+    double backward radial_streamed.py:173-207 recomputes)."""
+    torch = _torch()
+    from ictc_o2_hp import RadialUvuTensorProduct, ReferenceUvuTensorProduct
+    tp = ReferenceUvuTensorProduct(u, 1, m_max, parity="full", parity_in2="canonical",
+                                   shared_weights=False)
+    lin = torch.nn.Linear(hidden, tp.weight_numel, bias=bias)
+    rng = np.random.default_rng(seed)
+    arrays = {"x": rng.standard_normal((rows, tp.input1_dimension)),
+              "y": rng.standard_normal((rows, tp.input2_dimension)),
+              "h": rng.standard_normal((rows, hidden)),
+              "alpha": rng.standard_normal((tp.weight_numel, hidden)) / np.sqrt(hidden),
+              "g": rng.standard_normal((rows, tp.representation_dimension)),
+              "hx": rng.standard_normal((rows, tp.input1_dimension)),
+              "hy": rng.standard_normal((rows, tp.input2_dimension)),
+              "hh": rng.standard_normal((rows, hidden)),
+              "ha": rng.standard_normal((tp.weight_numel, hidden))}
+    if bias:
+        arrays["b"] = rng.standard_normal(tp.weight_numel)
+        arrays["hb"] = rng.standard_normal(tp.weight_numel)
+    arrays = {k: a.astype(np.float32) for k, a in arrays.items()}
+    t = {k: torch.from_numpy(a).double() for k, a in arrays.items()}
+    with torch.no_grad():
+        lin.weight.copy_(t["alpha"].float())
+        if bias:
+            lin.bias.copy_(t["b"].float())
+    module = RadialUvuTensorProduct(tp, lin).double()
+    x, y, h, g = (t[k].requires_grad_(True) for k in ("x", "y", "h", "g"))
+    params = (module.radial_out.weight,) + ((module.radial_out.bias,) if bias else ())
+    hs = (t["hx"], t["hy"], t["hh"], t["ha"]) + ((t["hb"],) if bias else ())
+    result = _second_order(lambda a, b, c: module(a, b, c), (x, y, h), (x, y, h, *params),
+                           (g, *hs))
+    keys = ["sx", "sy", "sh", "sa"] + (["sb"] if bias else []) + ["sg"]
+    np.savez_compressed(HERE / f"{name}.npz", u=u, m_max=m_max, hidden=hidden, bias=bias,
+                        **arrays, **{f"{k}_f64": r.numpy() for k, r in zip(keys, result)})
+    print("wrote", name)
+
+
+def _layout_case(name, cls_name, channels, m_max, parity, normalization, rows, seed):
+    """ComponentMajorTensorProduct / TupleTensorProduct forward and VJP by the
+    reference's own classes (api.py:32-49) in float64 on the CPU.  Tuple inputs and
+    outputs are stored as the flat concatenation of their blocks in block order."""
+    torch = _torch()
+    import ictc_o2_hp
+    cls = getattr(ictc_o2_hp, cls_name)
+    tp = cls(channels, m_max, parity=parity, normalization=normalization).to(torch.float64)
+    tp.internal_compute_dtype = torch.float64
+    width = tp.representation_dimension
+    rng = np.random.default_rng(seed)
+    arrays = {k: rng.standard_normal((rows, width)).astype(np.float32) for k in ("x", "y", "g")}
+    arrays["w"] = (0.5 * rng.standard_normal(tp.weight.numel())).astype(np.float32)
+    with torch.no_grad():
+        tp.weight.copy_(torch.from_numpy(arrays["w"]).double())
+    x, y, g = (torch.from_numpy(arrays[k]).double() for k in ("x", "y", "g"))
+    x.requires_grad_(True), y.requires_grad_(True)
+    if cls_name == "TupleTensorProduct":
+        def split(value):
+            parts, cursor = [], 0
+            for block in tp.blocks:
+                width_b = block.multiplicity * block.irrep_dimension
+                parts.append(value[:, cursor:cursor + width_b].reshape(
+                    rows, block.multiplicity, block.irrep_dimension))
+                cursor += width_b
+            return tuple(parts)
+        out = torch.cat([v.reshape(rows, -1) for v in tp(split(x), split(y))], dim=-1)
+    else:
+        out = tp(x, y)
+    dx, dy, dw = torch.autograd.grad(out, (x, y, tp.weight), g)
+    np.savez_compressed(HERE / f"{name}.npz", cls=cls_name, channels=channels, m_max=m_max,
+                        parity=parity, normalization=normalization, **arrays,
+                        out_f64=out.detach().numpy(), dx_f64=dx.numpy(), dy_f64=dy.numpy(),
+                        dw_f64=dw.numpy())
+    print("wrote", name)
+
+
 def _cg_tables(max_order=8):
     torch = _torch()
     from ictc_o2_hp import o2_math
@@ -173,9 +426,36 @@ def main(argv=None):
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference-src", default=os.environ.get("ICTC_REFERENCE_SRC"))
     parser.add_argument("--skip-large", action="store_true")
+    parser.add_argument("--only", nargs="*", default=None,
+                        help="groups to write: base, full, second, layout (default: all)")
     args = parser.parse_args(argv)
     if args.reference_src:
         sys.path.insert(0, args.reference_src)
+    sys.path.insert(0, str(HERE))
+    groups = set(args.only or ("base", "full", "second", "layout"))
+    if "second" in groups:
+        _tp_second_case("second_tp_c6_m3_full", 6, 3, "full", "component", 5, 41)
+        _tp_second_case("second_tp_c5_m2_canonical_norm", 5, 2, "canonical", "norm", 4, 42)
+        _tp_second_case("second_tp_c3_m6_full", 3, 6, "full", "component", 3, 43)
+        _uvu_second_case("second_uvu_u6_v3_m2_shared", 6, 3, 2, True, 5, 44)
+        _uvu_second_case("second_uvu_u5_v2_m3_perrow", 5, 2, 3, False, 4, 45)
+        _radial_second_case("second_radial_u4_m2_h5_bias", 4, 2, 5, True, 5, 46)
+        _radial_second_case("second_radial_u6_m3_h4_nobias", 6, 3, 4, False, 4, 47)
+    if "layout" in groups:
+        _layout_case("layout_cm_c7_m3_full", "ComponentMajorTensorProduct", 7, 3, "full",
+                     "component", 6, 51)
+        _layout_case("layout_cm_c5_m4_canonical_norm", "ComponentMajorTensorProduct", 5, 4,
+                     "canonical", "norm", 5, 52)
+        _layout_case("layout_tuple_c6_m2_full", "TupleTensorProduct", 6, 2, "full",
+                     "component", 4, 53)
+        _layout_case("layout_tuple_c4_m5_canonical", "TupleTensorProduct", 4, 5, "canonical",
+                     "component", 3, 54)
+    if "full" in groups:
+        _uvu_cfg4_perrow()
+        _uvu_cfg4_shared()
+        _radial_cfg5()
+    if "base" not in groups:
+        return 0
     f64 = [("f64", "float64")]
     both = [("f32", "float32"), ("f64", "float64")]
 

@@ -58,6 +58,10 @@ def test_invalid_arguments_return_status():
         _lib.ERR_INVALID
     assert lib.ictc_o2_tp_forward(None, None, None, None, 5, 4, 2, 1, 3, None) == \
         _lib.ERR_INVALID
+    # the wait probe validates its limit and pointer before touching a device
+    assert lib.ictc_o2_test_wait_timeout(0, None, None) == _lib.ERR_INVALID
+    assert lib.ictc_o2_test_wait_timeout(2000000, None, None) == _lib.ERR_INVALID
+    assert lib.ictc_o2_test_wait_timeout(100, None, None) == _lib.ERR_INVALID
 
 
 def test_check_maps_status_to_exceptions():

@@ -111,3 +111,19 @@ def test_message_passing_layer(cuda_device):
     assert _err(out, od) <= TOL
     for name, a, b in zip(("nodes", "angular", "hidden", "alpha"), grads, want):
         assert _err(a, b) <= TOL, name
+
+
+def test_segment_sum_rejects_non_csr_offsets(cuda_device):
+    """Offsets outside [0, value_rows] or decreasing raise the flag and zero the
+    segment; valid segments of the same call are summed as usual."""
+    from ictc_o2_hp_b200 import _lib
+    values = torch.randn(4, 8, device=cuda_device)
+    order = torch.arange(4, device=cuda_device)
+    out = torch.empty(3, 8, device=cuda_device)
+    offsets = torch.tensor([0, 2, 9, 1], device=cuda_device)   # [2, 9) past the end; 9 > 1
+    assert _lib.graph_bad_index() == 0
+    _lib.segment_sum(values, offsets, order, out)
+    torch.cuda.synchronize()
+    assert _lib.graph_bad_index() == 1
+    assert torch.equal(out[0], values[0] + values[1])
+    assert torch.count_nonzero(out[1]) == 0 and torch.count_nonzero(out[2]) == 0

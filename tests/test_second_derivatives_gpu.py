@@ -2,14 +2,17 @@
 UvuTensorProduct through the CUDA kernels, every role at once: the gradients of
 <cx, dx> + <cy, dy> + <cw, dw> with respect to x, y, w and the cotangent g,
 against the float64 PyTorch formulas on the CPU (the arbiter's role in the
-reference, triton_o2.py:1041-1069, uvu_triton.py:442-457); gate 1e-5 normalised
-max error."""
+reference, triton_o2.py:1041-1069, uvu_triton.py:442-457), which
+tests/test_formula_pins.py pins to the reference's own second derivatives, and
+directly against those reference values (tests/golden/second_*.npz); gate 1e-5
+normalised max error."""
 
 from __future__ import annotations
 
 import pytest
 import torch
 
+from conftest import golden_names, load_golden
 from oracle import o2_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -137,3 +140,71 @@ def test_radial_all_roles(U, m, H, bias, rows, cuda_device):
     want = _second_n(composed, ref_inputs, gc, [c.double() for c in cot], (*ref_inputs, gc))
     names = ["d x", "d angular", "d hidden", "d alpha"] + (["d bias"] if bias else []) + ["d g"]
     _check(got, want, names)
+
+
+# ------------------------------------------------ against the reference's own values
+# The second derivatives the reference's CPU autograd produced (create_graph) on
+# seeded inputs (tests/golden/second_*.npz, written by make_golden.py): the kernels'
+# double backward must match them, not only this package's formulas.
+
+
+def _dev(a, device, grad=True):
+    return torch.as_tensor(a, dtype=torch.float32, device=device).requires_grad_(grad)
+
+
+def _check_fixture(got, case, keys):
+    for key, value in zip(keys, got):
+        err = O.max_error(value.detach().cpu().double().numpy(), case[f"{key}_f64"])
+        assert err <= TOL, f"{key}: {err:.3e}"
+
+
+@pytest.mark.parametrize("name", golden_names("second_tp_"))
+def test_tensor_product_reference_second_order(name, cuda_device):
+    from ictc_o2_hp_b200 import TensorProduct
+    c = load_golden(name)
+    tp = TensorProduct(int(c["channels"]), int(c["m_max"]), parity=str(c["parity"]),
+                       normalization=str(c["normalization"])).to(cuda_device)
+    with torch.no_grad():
+        tp.weight.copy_(torch.as_tensor(c["w"]))
+    x, y, g = (_dev(c[k], cuda_device) for k in ("x", "y", "g"))
+    got = _second_n(lambda a, b, w: tp(a, b), (x, y, tp.weight), g,
+                    [_dev(c[k], cuda_device, False) for k in ("hx", "hy", "hw")],
+                    (x, y, tp.weight, g))
+    _check_fixture(got, c, ("sx", "sy", "sw", "sg"))
+
+
+@pytest.mark.parametrize("name", golden_names("second_uvu_"))
+def test_uvu_reference_second_order(name, cuda_device):
+    from ictc_o2_hp_b200 import UvuTensorProduct
+    c = load_golden(name)
+    tp = UvuTensorProduct(int(c["u"]), int(c["v"]), int(c["m_max"]),
+                          shared_weights=bool(c["shared"]), internal_weights=False)
+    tp = tp.to(cuda_device)
+    x, y, w, g = (_dev(c[k], cuda_device) for k in ("x", "y", "w", "g"))
+    got = _second_n(tp, (x, y, w), g,
+                    [_dev(c[k], cuda_device, False) for k in ("hx", "hy", "hw")], (x, y, w, g))
+    _check_fixture(got, c, ("sx", "sy", "sw", "sg"))
+
+
+@pytest.mark.parametrize("name", golden_names("second_radial_"))
+def test_radial_reference_second_order(name, cuda_device):
+    from ictc_o2_hp_b200 import RadialUvuTensorProduct, UvuTensorProduct
+    c = load_golden(name)
+    bias = bool(c["bias"])
+    tp = UvuTensorProduct(int(c["u"]), 1, int(c["m_max"]), parity="full",
+                          parity_in2="canonical", shared_weights=False)
+    lin = torch.nn.Linear(int(c["hidden"]), tp.weight_numel, bias=bias)
+    with torch.no_grad():
+        lin.weight.copy_(torch.as_tensor(c["alpha"]))
+        if bias:
+            lin.bias.copy_(torch.as_tensor(c["b"]))
+    model = RadialUvuTensorProduct(tp, lin).to(cuda_device)
+    x, y, h, g = (_dev(c[k], cuda_device) for k in ("x", "y", "h", "g"))
+    params = (model.radial_out.weight,) + ((model.radial_out.bias,) if bias else ())
+    hs = [_dev(c[k], cuda_device, False) for k in ("hx", "hy", "hh", "ha")]
+    if bias:
+        hs.append(_dev(c["hb"], cuda_device, False))
+    operands = (x, y, h, *params)
+    got = _second_n(lambda a, b, hh, *p: model(a, b, hh), operands, g, hs, (*operands, g))
+    keys = ["sx", "sy", "sh", "sa"] + (["sb"] if bias else []) + ["sg"]
+    _check_fixture(got, c, keys)

@@ -297,3 +297,35 @@ def test_no_device_error_flag(cuda_device):
     from ictc_o2_hp_b200 import _lib
     assert _lib.device_error() == 0
 
+
+
+@pytest.mark.parametrize("name", golden_names("layout_"))
+def test_layout_classes_against_reference(name, cuda_device):
+    """ComponentMajorTensorProduct and TupleTensorProduct against the values of the
+    reference's own classes of the same name (api.py:32-49), forward and VJP."""
+    import ictc_o2_hp_b200 as P
+    c = load_golden(name)
+    cls = getattr(P, str(c["cls"]))
+    tp = cls(int(c["channels"]), int(c["m_max"]), parity=str(c["parity"]),
+             normalization=str(c["normalization"])).to(cuda_device)
+    with torch.no_grad():
+        tp.weight.copy_(torch.as_tensor(c["w"]))
+    x, y = (torch.as_tensor(c[k], device=cuda_device).requires_grad_(True) for k in ("x", "y"))
+    g = torch.as_tensor(c["g"], device=cuda_device)
+    if str(c["cls"]) == "TupleTensorProduct":
+        rows = x.shape[0]
+
+        def split(v):
+            parts, cursor = [], 0
+            for b in tp.blocks:
+                width = b.multiplicity * b.irrep_dimension
+                parts.append(v[:, cursor:cursor + width].reshape(rows, b.multiplicity,
+                                                                 b.irrep_dimension))
+                cursor += width
+            return tuple(parts)
+        out = torch.cat([t.reshape(rows, -1) for t in tp(split(x), split(y))], dim=-1)
+    else:
+        out = tp(x, y)
+    grads = torch.autograd.grad(out, (x, y, tp.weight), g)
+    got = tuple(t.detach().cpu().numpy() for t in (out, *grads))
+    assert_close(got, tuple(c[f"{k}_f64"] for k in ("out", "dx", "dy", "dw")))
