@@ -32,6 +32,7 @@
 #include "common.cuh"
 #include "o2_paths.cuh"
 #include "tma.cuh"
+#include "tmap.cuh"
 
 namespace ictc {
 
@@ -754,6 +755,155 @@ __global__ void __launch_bounds__(kStagedWarps * 32, 1)
   }
 }
 
+// ------------------------------------------------------------ channel-tiled backward
+//
+// For channel counts whose warps do not fill a staged CTA (full parity: C = 96
+// gives 6 warps, C = 256 needs 16 channel groups), the CTA works on a tile of Ct
+// channels of every row instead: the tile's slice of a row arrives by two tiled
+// TMA boxes per operand (tmap.cuh) and lands as a row of a Ct-channel product,
+// so the per-row arithmetic is that of the untiled kernel.  CTA b serves tile
+// b % ntiles and the blocks of R rows (b / ntiles) + k * (grid / ntiles); slot
+// (b / ntiles) * R + r of the weight-gradient partials holds the tile's channels,
+// the other tiles' CTAs of the same slot index the rest, so every partial row is
+// written in full.
+
+template <int M, bool FULL, bool CM = false>
+__global__ void __launch_bounds__(kStagedWarps * 32, 1)
+    tp_backward_tiled(const __grid_constant__ RowTileMaps maps, const float4* __restrict__ ws,
+                      float* __restrict__ gx, float* __restrict__ gy,
+                      float* __restrict__ partial, int64_t numel, int64_t rows, TpLayout L,
+                      TpLayout Lt, Mags mags, int gt, int R, int stages, int ntiles,
+                      int weights_in_smem) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  using P = Paths<M, FULL>;
+  constexpr int S = 2 * M + 2;
+  constexpr int S0 = FULL ? 2 : 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = static_cast<int>(blockIdx.x % ntiles);
+  const int64_t cta = blockIdx.x / ntiles, ctas = gridDim.x / ntiles;
+  const int r = warp / gt;
+  const int Ct = Lt.C, c0 = tile * Ct;
+  const int Tt = gt * 32;                       // threads of one row slot of the tile
+  const int T = ntiles * Tt;                    // threads of all channel groups
+  const int tl = (warp % gt) * 32 + lane;       // thread within the tile's row slot
+  const LaneMap<FULL> lm(tile * gt + warp % gt, lane, L.C);
+  const int cl = lm.active ? lm.c - c0 : 0;     // channel within the tile
+  const int64_t Wt = Lt.width;
+  const size_t wbytes = weights_in_smem ? static_cast<size_t>(P::chunks) * Tt * sizeof(float4)
+                                        : 0;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  unsigned* done = reinterpret_cast<unsigned*>(full + kMaxStages);
+  uint64_t* wbar = full + 2 * kMaxStages;
+  float4* wsm = reinterpret_cast<float4*>(smem + kBarrierBytes);
+  float* buf = reinterpret_cast<float*>(smem + kBarrierBytes + wbytes);
+  const int64_t nblocks = (rows + R - 1) / R;
+  const uint32_t scalar_bytes = static_cast<uint32_t>(S0 * Ct * 4);
+
+  // stage s <- rows of block b of this tile: two boxes per operand row
+  auto issue = [&](int s, int64_t b) {
+    const int64_t row0 = b * R;
+    const int nr = rows - row0 < R ? static_cast<int>(rows - row0) : R;
+    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(3 * nr * Wt * 4));
+    float* st = buf + static_cast<int64_t>(s) * 3 * R * Wt;
+    for (int t = 0; t < 3; ++t) {
+      for (int rr = 0; rr < nr; ++rr) {
+        float* dst = st + (t * R + rr) * Wt;
+        const int z = static_cast<int>(row0 + rr);
+        tma_load_3d(dst, &maps.m[2 * t], c0, 0, z, &full[s]);
+        if constexpr (M > 0) {
+          tma_load_3d(reinterpret_cast<unsigned char*>(dst) + scalar_bytes, &maps.m[2 * t + 1],
+                      CM ? c0 : 2 * c0, 0, z, &full[s]);
+        }
+      }
+    }
+  };
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < stages; ++st) {
+      mbar_init(&full[st], 1);
+      done[st] = 0;
+    }
+    if (weights_in_smem) mbar_init(wbar, 1);
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (weights_in_smem) {
+      // chunk k of the tile's threads: ws[k * T + tile * Tt .. + Tt)
+      mbar_arrive_expect_tx(wbar, static_cast<uint32_t>(wbytes));
+      for (int k = 0; k < P::chunks; ++k)
+        bulk_g2s(wsm + k * Tt, ws + static_cast<int64_t>(k) * T + tile * Tt,
+                 static_cast<uint32_t>(Tt * sizeof(float4)), wbar);
+    }
+    for (int st = 0; st < stages; ++st) {
+      const int64_t b = cta + st * ctas;
+      if (b < nblocks) issue(st, b);
+    }
+  }
+  float acc[P::n];
+#pragma unroll
+  for (int i = 0; i < P::n; ++i) acc[i] = 0.0f;
+  bool ok = true;
+  auto run = [&](const auto& chunks) {
+    int s = 0;
+    uint32_t round = 0;
+    const int nwarps = blockDim.x >> 5;
+    for (int64_t b = cta; b < nblocks && ok; b += ctas) {
+      ok = mbar_wait(&full[s], round & 1, 1);
+      if (!ok) break;
+      const int64_t row = b * R + r;
+      if (row < rows) {
+        const float* st = buf + static_cast<int64_t>(s) * 3 * R * Wt + r * Wt;
+        float a[S], bb[S], g[S], dx[S], dy[S];
+        load_slots<M, FULL, CM>(SharedRow(st), Lt, cl, lm.q, a);
+        load_slots<M, FULL, CM>(SharedRow(st + R * Wt), Lt, cl, lm.q, bb);
+        load_slots<M, FULL, CM>(SharedRow(st + 2 * R * Wt), Lt, cl, lm.q, g);
+        row_vjp<M, FULL>(a, bb, g, chunks, lm.q, dx, dy, acc);
+        if (lm.active) {
+          store_slots<M, FULL, CM>(gx + row * L.width, L, lm.c, lm.q, true, dx);
+          store_slots<M, FULL, CM>(gy + row * L.width, L, lm.c, lm.q, true, dy);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        unsigned prev;
+        asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+                     : "=r"(prev)
+                     : "r"(smem_addr(&done[s]))
+                     : "memory");
+        if (prev + 1 == static_cast<unsigned>(nwarps) * (round + 1)) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          const int64_t next = b + static_cast<int64_t>(stages) * ctas;
+          if (next < nblocks) issue(s, next);
+        }
+      }
+      if (++s == stages) {
+        s = 0;
+        ++round;
+      }
+    }
+  };
+  if (weights_in_smem) {
+    ok = mbar_wait(wbar, 0, 4);
+    if (ok)
+      run(SharedChunks{static_cast<uint32_t>(__cvta_generic_to_shared(wsm + tl)),
+                       Tt * static_cast<int>(sizeof(float4))});
+  } else {
+    run(GlobalChunks{ws + tile * Tt + tl, T});
+  }
+  if (!ok) {
+    if (threadIdx.x == 0) {
+      // a wait ran out: let copies already issued land before the CTA exits
+      for (int st = 0; st < stages; ++st) mbar_wait(&full[st], 0, 3, kDrainLimitNs);
+    }
+    return;
+  }
+  if (lm.active) {
+    const int64_t slot = cta * R + r;
+    store_partial<M, FULL>(partial + slot * numel, L, mags, lm.c, lm.q, acc);
+  }
+}
+
 // ------------------------------------------------------------ small kernels
 
 // Magnitude-scaled weights in the per-thread order of row_vjp: chunk k of thread
@@ -828,6 +978,8 @@ using BackwardStagedFn = void (*)(const float*, const float*, const float4*, con
 using PrescaleFn = void (*)(const float*, float4*, TpLayout, Mags, int);
 using ForwardGroupedFn = void (*)(const float*, const float*, const float*, float*, int64_t,
                                   TpLayout, Mags, int, int64_t, bool);
+using BackwardTiledFn = void (*)(RowTileMaps, const float4*, float*, float*, float*, int64_t,
+                                 int64_t, TpLayout, TpLayout, Mags, int, int, int, int, int);
 
 // ICTC_ONLY_ORDER=m builds one order only (quick register/spill checks).
 #ifdef ICTC_ONLY_ORDER
@@ -845,6 +997,7 @@ struct Kernels {
   PrescaleFn prescale;
   int chunks;  // float4 weight chunks per thread (Paths::chunks)
   ForwardGroupedFn fwd_grouped;
+  BackwardTiledFn bwd_tiled;
 };
 
 // Kernels of one (order, parity, frequency-block layout); the layout is a template
@@ -857,9 +1010,9 @@ constexpr Kernels kernels_for() {
     return Kernels{wide, &tp_forward_direct<M, FULL, CM>, &tp_backward_direct<M, FULL, CM>,
                    &tp_forward_staged<M, FULL, CM>, &tp_backward_staged<M, FULL, CM>,
                    &prescale_kernel<M, FULL>, Paths<M, FULL>::chunks,
-                   &tp_forward_grouped<M, FULL, CM>};
+                   &tp_forward_grouped<M, FULL, CM>, &tp_backward_tiled<M, FULL, CM>};
   } else {
-    return Kernels{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0, nullptr};
+    return Kernels{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0, nullptr, nullptr};
   }
 }
 
@@ -966,6 +1119,63 @@ StagedPlan plan_staged(int device, int64_t rows, const TpLayout& L, bool full, i
   return p;
 }
 
+// Channel-tiled backward (tp_backward_tiled): used where the untiled staged CTA
+// would hold fewer than kStagedWarps warps (full parity, e.g. C = 96: 6 warps) or
+// cannot be formed (more than kStagedWarps channel groups, e.g. C = 256 full).
+// Tiles of Ct channels (Ct in 128, 64, 32, 16, a multiple of the channels per
+// warp, dividing C) with gt = Ct / channels-per-warp groups and R = 8 / gt rows per
+// stage; floor(SMs / ntiles) CTAs per tile, so every tile has as many CTAs.
+struct TiledPlan {
+  bool ok, weights_in_smem;
+  int Ct, gt, R, ntiles, stages;
+  int64_t ctas, grid;
+  size_t smem;
+};
+
+TiledPlan plan_tiled(int device, int64_t rows, const TpLayout& L, bool full, int chunks) {
+  TiledPlan p{};
+  const int cpw = full ? 16 : 32;
+  const int groups = static_cast<int>(ceil_div(L.C, cpw));
+  const bool untiled_short =
+      groups > kStagedWarps || (full && (kStagedWarps / groups) * groups < kStagedWarps);
+  if (!untiled_short || rows == 0 || rows > INT32_MAX || L.C % 16 != 0) return p;
+  for (int ct : {128, 64, 32, 16}) {
+    if (ct % cpw == 0 && ct < L.C && L.C % ct == 0) {
+      p.Ct = ct;
+      break;
+    }
+  }
+  if (p.Ct == 0) return p;
+  p.gt = p.Ct / cpw;
+  p.R = kStagedWarps / p.gt;
+  p.ntiles = L.C / p.Ct;
+  const int m_max = static_cast<int>((L.width / L.C / (full ? 2 : 1) - 1) / 2);
+  const TpLayout Lt = tp_layout(p.Ct, m_max, full, L.cm);
+  const size_t stage_bytes = static_cast<size_t>(3) * p.R * Lt.width * sizeof(float);
+  const size_t wbytes = static_cast<size_t>(chunks) * p.gt * 32 * sizeof(float4);
+  if (kStagedSmemBudget > kBarrierBytes + wbytes) {
+    const int fit = static_cast<int>((kStagedSmemBudget - kBarrierBytes - wbytes) / stage_bytes);
+    if (fit >= 3) {
+      p.weights_in_smem = true;
+      p.stages = fit < kMaxStages ? fit : kMaxStages;
+      p.smem = kBarrierBytes + wbytes + static_cast<size_t>(p.stages) * stage_bytes;
+    }
+  }
+  if (!p.weights_in_smem) {
+    const int fit = static_cast<int>((kStagedSmemBudget - kBarrierBytes) / stage_bytes);
+    p.stages = fit < kMaxStages ? fit : kMaxStages;
+    if (p.stages < 2) return p;
+    p.smem = kBarrierBytes + static_cast<size_t>(p.stages) * stage_bytes;
+  }
+  const int64_t nblocks = ceil_div(rows, p.R);
+  p.ctas = sm_count(device) / p.ntiles;
+  if (p.ctas < 1) p.ctas = 1;
+  if (p.ctas > nblocks) p.ctas = nblocks;
+  p.grid = p.ctas * p.ntiles;
+  p.ok = true;
+  return p;
+}
+
 bool aligned16(std::initializer_list<const void*> ptrs) {
   for (const void* p : ptrs)
     if (!aligned(p, 16)) return false;
@@ -983,8 +1193,11 @@ int64_t backward_slots(int device, const Kernels& k, int64_t rows, const TpLayou
   DirectPlan d{};
   *status = plan_direct(reinterpret_cast<const void*>(k.bwd_direct), device, rows, L.C, full, &d);
   const StagedPlan s = plan_staged(device, rows, L, full, 3, weight_chunk_bytes(k, L.C, full));
-  const int64_t staged = s.ok ? s.grid * s.R : 0;
-  return d.slots > staged ? d.slots : staged;
+  int64_t slots = d.slots;
+  if (s.ok && s.grid * s.R > slots) slots = s.grid * s.R;
+  const TiledPlan t = plan_tiled(device, rows, L, full, k.chunks);
+  if (t.ok && t.ctas * t.R > slots) slots = t.ctas * t.R;
+  return slots;
 }
 
 }  // namespace
@@ -1203,15 +1416,28 @@ int32_t tp_backward_impl(const float* left, const float* right, const float* wei
   int device = 0;
   if ((st = current_device(&device)) != ICTC_OK) return st;
   const size_t wbytes = weight_chunk_bytes(k, channels, full);
-  const StagedPlan sp = plan_staged(device, rows, L, full, 3, wbytes);
-  const bool staged = sp.ok && aligned16({left, right, grad_output, grad_left, grad_right});
+  const bool al16 = aligned16({left, right, grad_output, grad_left, grad_right});
+  const char* bwd_variant = getenv("ICTC_TP_BACKWARD");
+  const bool allow_tiled = bwd_variant == nullptr || strcmp(bwd_variant, "tiled") == 0;
+  const TiledPlan tp = (al16 && allow_tiled) ? plan_tiled(device, rows, L, full, k.chunks)
+                                             : TiledPlan{};
+  RowTileMaps maps{};
+  bool tiled = tp.ok;
+  if (tiled) {
+    const float* ops[3] = {left, right, grad_output};
+    for (int t = 0; t < 3 && tiled; ++t)
+      tiled = encode_row_tile_maps(ops[t], rows, channels, m_max, full, L.cm != 0, L.width,
+                                   tp.Ct, &maps.m[2 * t]) == 0;
+  }
+  const StagedPlan sp = tiled ? StagedPlan{} : plan_staged(device, rows, L, full, 3, wbytes);
+  const bool staged = !tiled && sp.ok && al16;
   DirectPlan dp{};
-  if (!staged) {
+  if (!staged && !tiled) {
     st = plan_direct(reinterpret_cast<const void*>(k.bwd_direct), device, rows, channels, full,
                      &dp);
     if (st != ICTC_OK) return st;
   }
-  const int64_t slots = staged ? sp.grid * sp.R : dp.slots;
+  const int64_t slots = tiled ? tp.ctas * tp.R : (staged ? sp.grid * sp.R : dp.slots);
   const size_t need = wbytes + static_cast<size_t>(slots) * numel * sizeof(float);
   if (workspace_bytes < need)
     return fail(ICTC_ERR_WORKSPACE, "workspace has %zu bytes, needs %zu", workspace_bytes, need);
@@ -1223,7 +1449,14 @@ int32_t tp_backward_impl(const float* left, const float* right, const float* wei
                                                                                mags, groups);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "prescale launch");
-  if (staged) {
+  if (tiled) {
+    if ((st = allow_smem(reinterpret_cast<const void*>(k.bwd_tiled), tp.smem)) != ICTC_OK)
+      return st;
+    const TpLayout Lt = tp_layout(tp.Ct, m_max, full, layout);
+    k.bwd_tiled<<<static_cast<unsigned>(tp.grid), kStagedWarps * 32, tp.smem, s>>>(
+        maps, chunks, grad_left, grad_right, partial, numel, rows, L, Lt, mags, tp.gt, tp.R,
+        tp.stages, tp.ntiles, tp.weights_in_smem ? 1 : 0);
+  } else if (staged) {
     if ((st = allow_smem(reinterpret_cast<const void*>(k.bwd_staged), sp.smem)) != ICTC_OK)
       return st;
     k.bwd_staged<<<static_cast<unsigned>(sp.grid), sp.warps * 32, sp.smem, s>>>(

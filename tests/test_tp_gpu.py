@@ -93,6 +93,12 @@ SHAPES = [
     (5, 7, "full", "component", 11),
     (3, 8, "canonical", "norm", 6),
     (48, 1, "full", "component", 1000),
+    # channel-tiled backward (tiles of 32 / 16 / 64 / 128 channels)
+    (96, 3, "full", "component", 300),
+    (48, 2, "full", "norm", 77),
+    (192, 4, "full", "component", 21),
+    (256, 2, "full", "component", 13),
+    (320, 1, "canonical", "component", 40),
 ]
 
 
@@ -240,6 +246,7 @@ def test_tuple_and_component_major_layouts(cuda_device):
     (128, 6, "full", 2048, None),      # the benchmark configuration's width (staged kernels)
     (9, 4, "full", 50, "direct"),      # odd channel count, direct kernels
     (32, 2, "full", 640, "grouped"),
+    (96, 3, "full", 200, None),        # channel-tiled backward
 ])
 def test_component_major_in_place(channels, m_max, parity, rows, variant, cuda_device,
                                   monkeypatch):
@@ -329,3 +336,26 @@ def test_layout_classes_against_reference(name, cuda_device):
     grads = torch.autograd.grad(out, (x, y, tp.weight), g)
     got = tuple(t.detach().cpu().numpy() for t in (out, *grads))
     assert_close(got, tuple(c[f"{k}_f64"] for k in ("out", "dx", "dy", "dw")))
+
+
+@pytest.mark.parametrize("channels,m_max,parity,rows", [
+    (96, 6, "full", 333),
+    (256, 3, "full", 70),
+    (160, 2, "full", 129),
+])
+def test_tiled_backward_matches_untiled(channels, m_max, parity, rows, cuda_device, monkeypatch):
+    """The channel-tiled backward (ICTC_TP_BACKWARD unset or "tiled") against the
+    untiled kernels on the same rows: dx and dy bit for bit (the same per-row
+    arithmetic), dw to float32 summation-order differences."""
+    from ictc_o2_hp_b200 import TensorProduct
+    torch.manual_seed(channels + rows)
+    tp = TensorProduct(channels, m_max, parity=parity).to(cuda_device)
+    W = tp.representation_dimension
+    x, y, g = (torch.randn(rows, W, device=cuda_device) for _ in range(3))
+    w = tp.weight.detach()
+    args = (channels, m_max, parity, "component")
+    tiled = torch.ops.ictc_o2_b200.tp_backward(x, y, w, g, *args)
+    monkeypatch.setenv("ICTC_TP_BACKWARD", "untiled")
+    plain = torch.ops.ictc_o2_b200.tp_backward(x, y, w, g, *args)
+    assert torch.equal(tiled[0], plain[0]) and torch.equal(tiled[1], plain[1])
+    assert O.max_error(tiled[2].cpu().numpy(), plain[2].cpu().numpy()) < 1e-6
