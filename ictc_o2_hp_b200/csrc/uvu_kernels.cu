@@ -479,9 +479,18 @@ UvuTableH table_of(const UvuConfig& c) {
   return build_uvu_table(c.U, c.V, c.m1, c.full1, c.m2, c.full2, c.component, c.path_norm);
 }
 
+// Row chunks of the shared-weight dw: enough CTAs to fill the GPU, and no chunk
+// longer than kDwChunkRows rows.  Each chunk's partial is a sequential FP32 sum of
+// 2 x chunk rows terms per weight; at 65,536 rows per chunk the float64-normalised
+// error of dw reached 1.4e-5 at 131,072 rows (the gate is 1e-5), at 1,024 rows it
+// stays near 2e-6, and the chunk partials are summed in a fixed order after.
+constexpr int64_t kDwChunkRows = 1024;
+
 int64_t dw_chunks(int device, int64_t rows, int P, int U, int V) {
   const int64_t tiles = static_cast<int64_t>(P) * ((U + 127) / 128) * ((V + 31) / 32);
   int64_t chunks = (2 * sm_count(device) + tiles - 1) / tiles;
+  const int64_t short_chunks = (rows + kDwChunkRows - 1) / kDwChunkRows;
+  if (chunks < short_chunks) chunks = short_chunks;
   const int64_t max_chunks = (rows + 255) / 256;
   if (chunks > max_chunks) chunks = max_chunks;
   return chunks < 1 ? 1 : chunks;
