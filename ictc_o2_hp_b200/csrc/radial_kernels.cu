@@ -222,14 +222,11 @@ struct RadTileArgs {
   bool vec;  // 16-byte access to 4-channel groups of opnd / x / out
   float* gw = nullptr;  // dx mode, optional: edge-weight gradient [rows][Wn]
   int64_t Wn = 0;
-  // dx mode, optional: the epilogue operands staged in shared memory by tiled TMA
-  // boxes of (2 UT floats, RT edges) of the 2-D views of x and g: x once per
-  // first-input group (paths run grouped by it), g once per path, each load issued
-  // by the last warp done with the previous slice so that it lands during the next
-  // path's weight product.  Without it every path loads its slices from L2 / HBM
-  // in the epilogue.
+  // dx mode, optional: x staged in shared memory once per first-input entry (paths
+  // run grouped by it), by a tiled TMA box of (2 UT floats, RT edges) of the 2-D
+  // view of x; without it every path re-reads its x slice from L2 / HBM.
   int xstage = 0;
-  CUtensorMap xmap, gmap;
+  CUtensorMap xmap;
 };
 
 // Thread tiles: 4 edges x NH groups of 4 channels (NH = 2: 256 threads, the 4x8
@@ -247,11 +244,10 @@ struct RtShape {
 inline size_t radial_tile_smem(int ut, int H, int W2, int np, int n1, int n2, bool dx,
                                bool xstage = false) {
   const size_t rt = static_cast<size_t>(kRtThreads / (ut / 8)) * 4;
-  const size_t xs = xstage ? 2 * rt * 2 * ut : 0;  // staged x and g slices [RT][2 UT] each
-  const size_t stages = dx ? kRtStages - 1 : kRtStages;
+  const size_t xs = xstage ? rt * 2 * ut : 0;  // staged x slice [RT][2 UT]
   const size_t kc = static_cast<size_t>(H < kRtKC ? H : kRtKC);
   const size_t w2s = static_cast<size_t>(odd_stride(W2));
-  const size_t floats = xs + static_cast<size_t>(H) * rt + stages * kc * ut + rt * w2s +
+  const size_t floats = xs + static_cast<size_t>(H) * rt + kRtStages * kc * ut + rt * w2s +
                         static_cast<size_t>(np) * 8 + (dx ? rt * w2s : 0);
   const size_t aligned_floats = (floats + 3) & ~size_t(3);
   const size_t ints = static_cast<size_t>(np) * 4 + static_cast<size_t>(n1 + n2) * 2 + np;
@@ -302,20 +298,15 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
   constexpr int RT = Sh::RT, TC = Sh::TC, NT = Sh::NT;
   constexpr int CW = 4 * NH;  // channels per thread
   extern __shared__ __align__(128) unsigned char rt_raw[];
-  // [0, 128): stage barriers (full), the staged-slice barriers and release counters
+  // [0, 128): stage barriers (full), the staged-x barriers and release counters
   uint64_t* full = reinterpret_cast<uint64_t*>(rt_raw);
   uint64_t* xfull = full + kRtStages;       // x slice landed (TMA transaction count)
-  uint64_t* gfull = full + kRtStages + 1;   // g slice landed
+  uint64_t* xfree = full + kRtStages + 1;   // every warp done with the x slice
   unsigned* done = reinterpret_cast<unsigned*>(rt_raw + 64);
-  unsigned* xdone = done + kRtStages;       // warps done with the x slice (cumulative)
-  unsigned* gdone = done + kRtStages + 1;   // warps done with the g slice (cumulative)
   const bool xst = MODE == kRtDx && A.xstage;
-  // weight-chunk ring stages (one fewer in the dx mode, whose staged slices need room)
-  constexpr int nst = MODE == kRtDx ? kRtStages - 1 : kRtStages;
-  constexpr int XB = 2 * UT;                // staged row: 2 UT floats
+  constexpr int XB = 2 * UT;                // staged x row: 2 UT floats
   float* xs = reinterpret_cast<float*>(rt_raw + 128);     // [RT][XB] when staged
-  float* gs = xs + (xst ? RT * XB : 0);                    // [RT][XB] when staged
-  float* sm = gs + (xst ? RT * XB : 0);
+  float* sm = xs + (xst ? RT * XB : 0);
   const int tid = threadIdx.x, lane = tid & 31;
   const int nwarps = NT / 32;
   const int kc = A.H < kRtKC ? A.H : kRtKC;
@@ -323,8 +314,8 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
   const int W2s = odd_stride(A.W2);
   const int np = A.t.np;
   float* Ht = sm;                                          // [H][RT]
-  float* Wt = Ht + static_cast<size_t>(A.H) * RT;          // [nst][kc][UT]
-  float* angt = Wt + nst * kc * UT;                        // [RT][W2s]
+  float* Wt = Ht + static_cast<size_t>(A.H) * RT;          // [kRtStages][kc][UT]
+  float* angt = Wt + kRtStages * kc * UT;                  // [RT][W2s]
   float* coef = angt + RT * W2s;                           // [np][8]
   float* dyacc = coef + np * 8;                            // [RT][W2s] (dx mode)
   float* fend = dyacc + (MODE == kRtDx ? RT * W2s : 0);
@@ -366,9 +357,7 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
     }
     if (xst) {
       mbar_init(xfull, 1);
-      mbar_init(gfull, 1);
-      *xdone = 0;
-      *gdone = 0;
+      mbar_init(xfree, nwarps);
     }
     fence_mbarrier_init();
   }
@@ -399,24 +388,8 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
 #pragma unroll
     for (int b = 0; b < CW; ++b) res[a][b] = make_float2(0.f, 0.f);
 
-  // staged slices of path q (q-th (channel tile, path position) pair)
-  auto issue_slice = [&](int q, bool gslice) {
-    const int qp = q % np;
-    const int4 pt = paths[order[qp]];
-    const int2 e = in1[gslice ? pt.z : pt.x];
-    uint64_t* bar = gslice ? gfull : xfull;
-    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(RT * XB * 4));
-    tma_load_2d(gslice ? gs : xs, gslice ? &A.gmap : &A.xmap, e.x + (q / np) * UT * e.y,
-                static_cast<int>(row0), bar);
-  };
-  const int nq = nub * np;  // paths to run, over all channel tiles
-  if (tid == 0) {
-    for (int T = 0; T < nst && T < ntiles; ++T) issue(T, T);
-    if (xst) {
-      issue_slice(0, false);
-      issue_slice(0, true);
-    }
-  }
+  if (tid == 0)
+    for (int T = 0; T < kRtStages && T < ntiles; ++T) issue(T, T);
   bool ok = true;
   // (channel tile, path position, hidden chunk) of tile T, advanced per tile: T runs
   // over ck fastest, then pos, then the channel tile (no division per tile)
@@ -430,13 +403,25 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
       }
     }
   };
-  int xgroup = -1;  // first-input groups reached (staged x), minus one
-  int q = 0;        // paths completed
+  int xgroup = -1;  // staged-x groups started so far, minus one
   for (int T = 0; T < ntiles && ok; ++T, advance()) {
-    const int st = T % nst;  // nst is a compile-time constant: no division issued
-    const uint32_t round = static_cast<uint32_t>(T / nst);
+    const int st = T % kRtStages;
+    const uint32_t round = static_cast<uint32_t>(T / kRtStages);
     const int p = order[pos];
-    ok = mbar_wait(&full[st], round & 1, 5);
+    if (xst && ck == 0 && (pos == 0 || paths[order[pos - 1]].x != paths[p].x)) {
+      // first path of a first-input group: once every warp is done with the last
+      // group's slice, bring this group's x slice of the tile's edges in
+      ++xgroup;
+      if (tid == 0) {
+        if (xgroup > 0) ok = mbar_wait(xfree, (xgroup - 1) & 1, 14);
+        if (ok) {
+          const int2 ea = in1[paths[p].x];
+          mbar_arrive_expect_tx(xfull, static_cast<uint32_t>(RT * XB * 4));
+          tma_load_2d(xs, &A.xmap, ea.x + ub * ea.y, static_cast<int>(row0), xfull);
+        }
+      }
+    }
+    ok = ok && mbar_wait(&full[st], round & 1, 5);
     if (!ok) break;
     if (ck == 0) {
 #pragma unroll
@@ -497,7 +482,7 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
                    : "memory");
       if (prev + 1 == static_cast<unsigned>(nwarps) * (round + 1)) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        if (T + nst < ntiles) issue(T + nst, st);
+        if (T + kRtStages < ntiles) issue(T + kRtStages, st);
       }
     }
     if (ck == nkc - 1) {
@@ -506,8 +491,7 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
       const float* c = coef + 8 * p;
       const int key = MODE == kRtFwd ? pt.z : pt.x;
       if (xst) {
-        if (pos == 0 || paths[order[pos - 1]].x != key) ++xgroup;
-        ok = mbar_wait(xfull, xgroup & 1, 15) && mbar_wait(gfull, q & 1, 16);
+        ok = mbar_wait(xfull, xgroup & 1, 15);
         if (!ok) break;
       }
       // The coefficient pairs below feed paired f32x2 operations (`fma2`, `__fmul2_rn`):
@@ -554,36 +538,17 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
               }
             } else {
               float gv[4 * D3], xv[4 * D1];
+              load4<D3>(gv, A.opnd + row * A.W1 + ek.x + static_cast<int64_t>(u) * D3, row_ok, u,
+                        A.U, A.vec);
               if (xst) {
-                // staged slices: zero past the rows (TMA fill); past U within the tile
-                // they hold the next entry's values, zeroed here as the loads do
-                const float* gsrc = gs + r * XB + (u - ub) * D3;
-#pragma unroll
-                for (int k4 = 0; k4 < D3; ++k4) {
-                  const float4 t = *reinterpret_cast<const float4*>(gsrc + 4 * k4);
-                  gv[4 * k4] = t.x; gv[4 * k4 + 1] = t.y; gv[4 * k4 + 2] = t.z;
-                  gv[4 * k4 + 3] = t.w;
-                }
-                if (u + 3 >= A.U) {
-#pragma unroll
-                  for (int k4 = 0; k4 < 4 * D3; ++k4)
-                    if (u + k4 / D3 >= A.U) gv[k4] = 0.f;
-                }
+                // zero past the rows (TMA fill) and past U within a tile of UT channels
                 const float* xsrc = xs + r * XB + (u - ub) * D1;
 #pragma unroll
-                for (int k4 = 0; k4 < D1; ++k4) {
-                  const float4 t = *reinterpret_cast<const float4*>(xsrc + 4 * k4);
-                  xv[4 * k4] = t.x; xv[4 * k4 + 1] = t.y; xv[4 * k4 + 2] = t.z;
-                  xv[4 * k4 + 3] = t.w;
-                }
-                if (u + 3 >= A.U) {
-#pragma unroll
-                  for (int k4 = 0; k4 < 4 * D1; ++k4)
-                    if (u + k4 / D1 >= A.U) xv[k4] = 0.f;
+                for (int q = 0; q < D1; ++q) {
+                  const float4 t = *reinterpret_cast<const float4*>(xsrc + 4 * q);
+                  xv[4 * q] = t.x; xv[4 * q + 1] = t.y; xv[4 * q + 2] = t.z; xv[4 * q + 3] = t.w;
                 }
               } else {
-                load4<D3>(gv, A.opnd + row * A.W1 + ek.x + static_cast<int64_t>(u) * D3, row_ok,
-                          u, A.U, A.vec);
                 load4<D1>(xv, A.x + row * A.W1 + ei.x + static_cast<int64_t>(u) * D1, row_ok,
                           u, A.U, A.vec);
               }
@@ -646,29 +611,11 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
       });
       const bool last = pos + 1 == np ||
                         (MODE == kRtFwd ? paths[order[pos + 1]].z : paths[order[pos + 1]].x) != key;
-      if (xst) {
-        // this warp is done with path q's g slice (and, at the group's end, with the
-        // x slice): the last warp out loads the next ones
+      if (xst && last) {
+        // this warp is done with the group's x slice
         __syncwarp();
-        if (lane == 0) {
-          unsigned prev;
-          asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
-                       : "=r"(prev) : "r"(smem_addr(gdone)) : "memory");
-          if (prev + 1 == static_cast<unsigned>(nwarps) * (q + 1) && q + 1 < nq) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue_slice(q + 1, true);
-          }
-          if (last) {
-            asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
-                         : "=r"(prev) : "r"(smem_addr(xdone)) : "memory");
-            if (prev + 1 == static_cast<unsigned>(nwarps) * (xgroup + 1) && q + 1 < nq) {
-              asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-              issue_slice(q + 1, false);
-            }
-          }
-        }
+        if (lane == 0) mbar_arrive(xfree);
       }
-      ++q;
       if (last) {
         const int2 eo = in1[key];
         const int dd = eo.y;
@@ -697,11 +644,8 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
   }
   if (!ok && tid == 0) {
     // a wait ran out: let copies already issued land before the CTA exits
-    for (int s2 = 0; s2 < nst; ++s2) mbar_wait(&full[s2], 0, 6, kDrainLimitNs);
-    if (xst) {
-      mbar_wait(xfull, 0, 15, kDrainLimitNs);
-      mbar_wait(gfull, 0, 16, kDrainLimitNs);
-    }
+    for (int st = 0; st < kRtStages; ++st) mbar_wait(&full[st], 0, 6, kDrainLimitNs);
+    if (xst && xgroup >= 0) mbar_wait(xfull, xgroup & 1, 15, kDrainLimitNs);
   }
   if (MODE == kRtDx) {
     __syncthreads();
@@ -754,12 +698,10 @@ int launch_radial_tile(const RadTileArgs& ra_in, cudaStream_t s) {
   RadTileArgs ra = ra_in;
   ra.xstage = 0;
   if (MODE == kRtDx && radial_xstage_enabled() && ra.x != nullptr && ra.vec &&
-      aligned(ra.x, 16) && aligned(ra.opnd, 16) && ra.rows <= INT32_MAX &&
+      aligned(ra.x, 16) && ra.rows <= INT32_MAX &&
       radial_tile_smem(ut, ra.H, ra.W2, ra.t.np, ra.t.n1, ra.t.n2, true, true) <= 225 * 1024) {
     const int rt = (kRtThreads / (ut / 8)) * 4;
-    ra.xstage = (encode_rows_2d(ra.x, ra.rows, ra.W1, 2 * ut, rt, &ra.xmap) == 0 &&
-                 encode_rows_2d(ra.opnd, ra.rows, ra.W1, 2 * ut, rt, &ra.gmap) == 0)
-                    ? 1 : 0;
+    ra.xstage = encode_rows_2d(ra.x, ra.rows, ra.W1, 2 * ut, rt, &ra.xmap) == 0 ? 1 : 0;
   }
   const size_t smem = radial_tile_smem(ut, ra.H, ra.W2, ra.t.np, ra.t.n1, ra.t.n2, MODE == kRtDx,
                                        ra.xstage != 0);
