@@ -96,21 +96,6 @@ int encode3(PFN_cuTensorMapEncodeTiled_v12000 fn, CUtensorMap* map, const float*
 
 }  // namespace
 
-int encode_rows_2d(const float* base, int64_t rows, int64_t width, int box_cols, int box_rows,
-                   CUtensorMap* map) {
-  PFN_cuTensorMapEncodeTiled_v12000 fn = tensor_map_encoder();
-  if (fn == nullptr) return -1;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(width) * 4};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? 0 : -1;
-}
-
 int encode_row_tile_maps(const float* base, int64_t rows, int C, int M, bool full, bool cm,
                          int64_t width, int Ct, CUtensorMap* maps) {
   PFN_cuTensorMapEncodeTiled_v12000 fn = tensor_map_encoder();

@@ -21,7 +21,6 @@
 #include "rowtile.cuh"
 #include "sgemm.cuh"
 #include "tma.cuh"
-#include "tmap.cuh"
 #include "uvu_table.cuh"
 
 namespace ictc {
@@ -222,11 +221,6 @@ struct RadTileArgs {
   bool vec;  // 16-byte access to 4-channel groups of opnd / x / out
   float* gw = nullptr;  // dx mode, optional: edge-weight gradient [rows][Wn]
   int64_t Wn = 0;
-  // dx mode, optional: x staged in shared memory once per first-input entry (paths
-  // run grouped by it), by a tiled TMA box of (2 UT floats, RT edges) of the 2-D
-  // view of x; without it every path re-reads its x slice from L2 / HBM.
-  int xstage = 0;
-  CUtensorMap xmap;
 };
 
 // Thread tiles: 4 edges x NH groups of 4 channels (NH = 2: 256 threads, the 4x8
@@ -241,13 +235,11 @@ struct RtShape {
   static constexpr int RT = TR * 4;               // edges per CTA
 };
 
-inline size_t radial_tile_smem(int ut, int H, int W2, int np, int n1, int n2, bool dx,
-                               bool xstage = false) {
+inline size_t radial_tile_smem(int ut, int H, int W2, int np, int n1, int n2, bool dx) {
   const size_t rt = static_cast<size_t>(kRtThreads / (ut / 8)) * 4;
-  const size_t xs = xstage ? rt * 2 * ut : 0;  // staged x slice [RT][2 UT]
   const size_t kc = static_cast<size_t>(H < kRtKC ? H : kRtKC);
   const size_t w2s = static_cast<size_t>(odd_stride(W2));
-  const size_t floats = xs + static_cast<size_t>(H) * rt + kRtStages * kc * ut + rt * w2s +
+  const size_t floats = static_cast<size_t>(H) * rt + kRtStages * kc * ut + rt * w2s +
                         static_cast<size_t>(np) * 8 + (dx ? rt * w2s : 0);
   const size_t aligned_floats = (floats + 3) & ~size_t(3);
   const size_t ints = static_cast<size_t>(np) * 4 + static_cast<size_t>(n1 + n2) * 2 + np;
@@ -292,21 +284,15 @@ __device__ __forceinline__ void store4(float* __restrict__ dst, const float (&v)
 }
 
 template <int MODE, int UT, int NH>
-__global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
-    radial_tile(const __grid_constant__ RadTileArgs A) {
+__global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArgs A) {
   using Sh = RtShape<UT, NH>;
   constexpr int RT = Sh::RT, TC = Sh::TC, NT = Sh::NT;
   constexpr int CW = 4 * NH;  // channels per thread
   extern __shared__ __align__(128) unsigned char rt_raw[];
-  // [0, 128): stage barriers (full), the staged-x barriers and release counters
+  // [0, 128): stage barriers (full) and release counters
   uint64_t* full = reinterpret_cast<uint64_t*>(rt_raw);
-  uint64_t* xfull = full + kRtStages;       // x slice landed (TMA transaction count)
-  uint64_t* xfree = full + kRtStages + 1;   // every warp done with the x slice
   unsigned* done = reinterpret_cast<unsigned*>(rt_raw + 64);
-  const bool xst = MODE == kRtDx && A.xstage;
-  constexpr int XB = 2 * UT;                // staged x row: 2 UT floats
-  float* xs = reinterpret_cast<float*>(rt_raw + 128);     // [RT][XB] when staged
-  float* sm = xs + (xst ? RT * XB : 0);
+  float* sm = reinterpret_cast<float*>(rt_raw + 128);
   const int tid = threadIdx.x, lane = tid & 31;
   const int nwarps = NT / 32;
   const int kc = A.H < kRtKC ? A.H : kRtKC;
@@ -355,10 +341,6 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
       mbar_init(&full[st], 1);
       done[st] = 0;
     }
-    if (xst) {
-      mbar_init(xfull, 1);
-      mbar_init(xfree, nwarps);
-    }
     fence_mbarrier_init();
   }
   __syncthreads();
@@ -403,26 +385,12 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
       }
     }
   };
-  int xgroup = -1;  // staged-x groups started so far, minus one
   for (int T = 0; T < ntiles && ok; ++T, advance()) {
     const int st = T % kRtStages;
     const uint32_t round = static_cast<uint32_t>(T / kRtStages);
-    const int p = order[pos];
-    if (xst && ck == 0 && (pos == 0 || paths[order[pos - 1]].x != paths[p].x)) {
-      // first path of a first-input group: once every warp is done with the last
-      // group's slice, bring this group's x slice of the tile's edges in
-      ++xgroup;
-      if (tid == 0) {
-        if (xgroup > 0) ok = mbar_wait(xfree, (xgroup - 1) & 1, 14);
-        if (ok) {
-          const int2 ea = in1[paths[p].x];
-          mbar_arrive_expect_tx(xfull, static_cast<uint32_t>(RT * XB * 4));
-          tma_load_2d(xs, &A.xmap, ea.x + ub * ea.y, static_cast<int>(row0), xfull);
-        }
-      }
-    }
-    ok = ok && mbar_wait(&full[st], round & 1, 5);
+    ok = mbar_wait(&full[st], round & 1, 5);
     if (!ok) break;
+    const int p = order[pos];
     if (ck == 0) {
 #pragma unroll
       for (int a = 0; a < 4; ++a)
@@ -440,7 +408,7 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
         if (row < A.rows) {
           const float* xr = (MODE == kRtFwd ? A.opnd : A.x) + row * A.W1 + ea.x +
                             static_cast<int64_t>(ub) * ea.y;
-          if (!xst && tc * 32 < uspan * ea.y) prefetch_l1(xr + tc * 32);
+          if (tc * 32 < uspan * ea.y) prefetch_l1(xr + tc * 32);
           if (MODE == kRtDx) {
             const float* gr = A.opnd + row * A.W1 + eb.x + static_cast<int64_t>(ub) * eb.y;
             if (tc * 32 < uspan * eb.y) prefetch_l1(gr + tc * 32);
@@ -490,10 +458,6 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
       const int2 ei = in1[pt.x], ej = in2[pt.y], ek = in1[pt.z];
       const float* c = coef + 8 * p;
       const int key = MODE == kRtFwd ? pt.z : pt.x;
-      if (xst) {
-        ok = mbar_wait(xfull, xgroup & 1, 15);
-        if (!ok) break;
-      }
       // The coefficient pairs below feed paired f32x2 operations (`fma2`, `__fmul2_rn`):
       // each component is computed in the same operation order as the scalar form,
       // so the results are bit-identical to it with half the issue slots.
@@ -540,18 +504,8 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
               float gv[4 * D3], xv[4 * D1];
               load4<D3>(gv, A.opnd + row * A.W1 + ek.x + static_cast<int64_t>(u) * D3, row_ok, u,
                         A.U, A.vec);
-              if (xst) {
-                // zero past the rows (TMA fill) and past U within a tile of UT channels
-                const float* xsrc = xs + r * XB + (u - ub) * D1;
-#pragma unroll
-                for (int q = 0; q < D1; ++q) {
-                  const float4 t = *reinterpret_cast<const float4*>(xsrc + 4 * q);
-                  xv[4 * q] = t.x; xv[4 * q + 1] = t.y; xv[4 * q + 2] = t.z; xv[4 * q + 3] = t.w;
-                }
-              } else {
-                load4<D1>(xv, A.x + row * A.W1 + ei.x + static_cast<int64_t>(u) * D1, row_ok,
-                          u, A.U, A.vec);
-              }
+              load4<D1>(xv, A.x + row * A.W1 + ei.x + static_cast<int64_t>(u) * D1, row_ok, u,
+                        A.U, A.vec);
               // dx[a] += w sum_kc C[kc][a] g[kc], both a at once: (C00, C01) g0 + (C10, C11) g1
               const float2 ck0 = make_float2(c00, c01), ck1 = make_float2(c10, c11);
               float gwv[4];
@@ -611,11 +565,6 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
       });
       const bool last = pos + 1 == np ||
                         (MODE == kRtFwd ? paths[order[pos + 1]].z : paths[order[pos + 1]].x) != key;
-      if (xst && last) {
-        // this warp is done with the group's x slice
-        __syncwarp();
-        if (lane == 0) mbar_arrive(xfree);
-      }
       if (last) {
         const int2 eo = in1[key];
         const int dd = eo.y;
@@ -645,7 +594,6 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1)
   if (!ok && tid == 0) {
     // a wait ran out: let copies already issued land before the CTA exits
     for (int st = 0; st < kRtStages; ++st) mbar_wait(&full[st], 0, 6, kDrainLimitNs);
-    if (xst && xgroup >= 0) mbar_wait(xfull, xgroup & 1, 15, kDrainLimitNs);
   }
   if (MODE == kRtDx) {
     __syncthreads();
@@ -684,27 +632,10 @@ inline bool radial_tile_wide() {
   return v == nullptr || strcmp(v, "split") != 0;
 }
 
-// Staged x for the dx mode (ICTC_RADIAL_XSTAGE=0 turns it off, for tests): needs
-// 16-byte channel groups, a row count that TMA coordinates hold, room in shared
-// memory and the 2-D tensor map of x.
-inline bool radial_xstage_enabled() {
-  const char* v = getenv("ICTC_RADIAL_XSTAGE");
-  return v == nullptr || strcmp(v, "0") != 0;
-}
-
 template <int MODE>
-int launch_radial_tile(const RadTileArgs& ra_in, cudaStream_t s) {
-  const int ut = radial_ut(ra_in.U);
-  RadTileArgs ra = ra_in;
-  ra.xstage = 0;
-  if (MODE == kRtDx && radial_xstage_enabled() && ra.x != nullptr && ra.vec &&
-      aligned(ra.x, 16) && ra.rows <= INT32_MAX &&
-      radial_tile_smem(ut, ra.H, ra.W2, ra.t.np, ra.t.n1, ra.t.n2, true, true) <= 225 * 1024) {
-    const int rt = (kRtThreads / (ut / 8)) * 4;
-    ra.xstage = encode_rows_2d(ra.x, ra.rows, ra.W1, 2 * ut, rt, &ra.xmap) == 0 ? 1 : 0;
-  }
-  const size_t smem = radial_tile_smem(ut, ra.H, ra.W2, ra.t.np, ra.t.n1, ra.t.n2, MODE == kRtDx,
-                                       ra.xstage != 0);
+int launch_radial_tile(const RadTileArgs& ra, cudaStream_t s) {
+  const int ut = radial_ut(ra.U);
+  const size_t smem = radial_tile_smem(ut, ra.H, ra.W2, ra.t.np, ra.t.n1, ra.t.n2, MODE == kRtDx);
   if (smem > 225 * 1024) return ICTC_ERR_UNSUPPORTED;  // caller falls back to the row tile
   const bool wide = radial_tile_wide();
   if (ut == 64)

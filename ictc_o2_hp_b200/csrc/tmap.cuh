@@ -32,23 +32,6 @@ struct alignas(64) RowTileMaps {
 int encode_row_tile_maps(const float* base, int64_t rows, int C, int M, bool full, bool cm,
                          int64_t width, int Ct, CUtensorMap* maps);
 
-// Host: encodes a 2-D view (column, row) of a row-major [rows, width] float tensor
-// with box (box_cols, box_rows).  Returns 0, or -1 when unavailable or rejected.
-int encode_rows_2d(const float* base, int64_t rows, int64_t width, int box_cols, int box_rows,
-                   CUtensorMap* map);
-
-// 2-D tile load of box coordinates (x, y) into shared memory, completing on `bar`.
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y),
-        "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
-      : "memory");
-}
-
 // 3-D tile load of box coordinates (x, y, z) into shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
                                             uint64_t* bar) {

@@ -128,27 +128,3 @@ def test_compile_and_validation(cuda_device):
                                torch.nn.Linear(3, 10))
     with pytest.raises(ValueError):
         module(x, y[:, :-1], h)
-
-
-@pytest.mark.parametrize("u,m_max,hidden,bias,rows", [
-    (64, 3, 64, True, 1000),   # config-5 shape, one channel tile, a partial last edge tile
-    (160, 2, 24, True, 150),   # two channel tiles, the last partial
-    (48, 1, 16, False, 129),   # channels short of the tile
-])
-def test_staged_x_is_bit_identical(u, m_max, hidden, bias, rows, cuda_device, monkeypatch):
-    """The dx tile stages each first-input group's x slice in shared memory by TMA
-    (default); ICTC_RADIAL_XSTAGE=0 reads x from global memory per path.  The
-    arithmetic is the same, so every gradient is bit-identical."""
-    torch.manual_seed(u + rows)
-    module = build(u, m_max, hidden, bias, cuda_device)
-    tp = module.tp
-    x = torch.randn(rows, tp.input1_dimension, device=cuda_device, requires_grad=True)
-    y = torch.randn(rows, tp.input2_dimension, device=cuda_device, requires_grad=True)
-    h = torch.randn(rows, hidden, device=cuda_device, requires_grad=True)
-    g = torch.randn(rows, tp.representation_dimension, device=cuda_device)
-    params = [module.radial_out.weight] + ([module.radial_out.bias] if bias else [])
-    staged = torch.autograd.grad(module(x, y, h), (x, y, h, *params), g)
-    monkeypatch.setenv("ICTC_RADIAL_XSTAGE", "0")
-    plain = torch.autograd.grad(module(x, y, h), (x, y, h, *params), g)
-    for a, b in zip(staged, plain):
-        assert torch.equal(a, b)
