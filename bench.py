@@ -962,8 +962,10 @@ SWEEP_ROWS = (16384, 32768, 65536, 131072)
 def run_sweep(args) -> dict:
     """Config 3: TensorProduct over m_max 1-6 x C {32, 64, 96, 128, 256} x parity x
     N {16,384, 32,768, 65,536, 131,072}, iid N(0, 1) inputs (seed per shape), ones
-    cotangent; forward and forward + VJP timed separately, each launch alone with
-    CUDA events and an L2 flush (a 256 MB write) before it, median of the steps."""
+    cotangent; the forward and the forward + VJP are each captured in a CUDA graph
+    (so host launch time does not enter the small shapes' figures) and each replay
+    is timed alone with CUDA events, after an L2 flush (a 256 MB write); median of
+    the steps."""
     import torch
     from ictc_o2_hp_b200 import TensorProduct, ops
     device = torch.device("cuda", 0)
@@ -972,19 +974,31 @@ def run_sweep(args) -> dict:
     steps = max(3, min(args.steps, 10))
     flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=device)
 
-    def median_ms(fn):
+    def median_ms(graph):
         for _ in range(2):
-            fn()
+            graph.replay()
         times = []
         for _ in range(steps):
             flush.fill_(1.0)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            fn()
+            graph.replay()
             b.record()
             b.synchronize()
             times.append(a.elapsed_time(b))
         return statistics.median(times)
+
+    def capture(fn):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                fn()  # warm-up outside the capture (allocations, smem opt-in)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        return graph
 
     shapes = []
     launches = 0
@@ -999,21 +1013,16 @@ def run_sweep(args) -> dict:
                     x = torch.randn(top, W, device=device)
                     y = torch.randn(top, W, device=device)
                     g = torch.ones(top, W, device=device)
+                    w = tp.weight.detach()
+                    cfg = (channels, m_max, parity, "component")
                     for rows in SWEEP_ROWS:
                         xs, ys, gs = x[:rows], y[:rows], g[:rows]
-                        w = tp.weight.detach()
-
-                        def forward():
-                            ops.tp_forward(xs, ys, w, channels, m_max, parity, "component")
-
-                        def forward_vjp():
-                            xx = xs.detach().requires_grad_(True)
-                            yy = ys.detach().requires_grad_(True)
-                            out = tp(xx, yy)
-                            torch.autograd.grad(out, (xx, yy, tp.weight), gs)
-
-                        fwd = median_ms(forward)
-                        both = median_ms(forward_vjp)
+                        fwd_graph = capture(lambda: ops.tp_forward(xs, ys, w, *cfg))
+                        both_graph = capture(lambda: (ops.tp_forward(xs, ys, w, *cfg),
+                                                      ops.tp_backward(xs, ys, w, gs, *cfg)))
+                        fwd = median_ms(fwd_graph)
+                        both = median_ms(both_graph)
+                        del fwd_graph, both_graph
                         launches += 5 * (steps + 2)
                         shapes.append({
                             "channels": channels, "m_max": m_max, "parity": parity,
@@ -1034,8 +1043,9 @@ def run_sweep(args) -> dict:
         "data": "synthetic (seeded iid N(0,1) inputs, seeded init, ones cotangent)",
         "config": {"workload": "m_max 1-6 x C {32,64,96,128,256} x parity {canonical, full} x "
                                "N {16384, 32768, 65536, 131072}; forward and forward + VJP "
-                               "timed separately per launch",
-                   "l2": "L2 flushed (256 MB write) before every timed launch"},
+                               "(forward and backward launches) timed separately, each as a "
+                               "CUDA graph replay",
+                   "l2": "L2 flushed (256 MB write) before every timed replay"},
         "gpu_launches": launches, "clocks": clocks.summary(), "shapes": shapes}
 
 
