@@ -508,28 +508,31 @@ class RadialWorkload(Workload):
 
 
 class RadialMpWorkload(RadialWorkload):
-    """Config 5 as a message-passing layer: node features gathered by source
-    (ictc_o2_gather_rows), the radial product, messages summed into the destination
-    nodes (ictc_o2_segment_sum, fixed order); the VJP covers the node features, the
-    angular inputs and every parameter.  Edges are sharded; each rank gathers from
-    the full node set and its node gradients join the one all-reduce."""
+    """Config 5 as a message-passing layer: node features read by source inside the
+    radial kernels (graph.radial_messages: the gather is folded into the edge tile),
+    the radial product, messages summed into the destination nodes
+    (ictc_o2_segment_sum, fixed order); the VJP covers the node features (per-edge
+    gradients summed by source), the angular inputs and every parameter.  Edges
+    are sharded; each rank reads the full node set and its node gradients join the
+    one all-reduce."""
 
     name = "radial_mp"
 
     def __init__(self, args, device, rank, world):
         super().__init__(args, device, rank, world)
-        from ictc_o2_hp_b200.graph import EdgeIndex, gather, scatter_sum
-        self.gather, self.scatter_sum = gather, scatter_sum
+        from ictc_o2_hp_b200.graph import EdgeIndex, radial_messages, scatter_sum
+        self.radial_messages, self.scatter_sum = radial_messages, scatter_sum
         self.edge_index = EdgeIndex(self.src_shard, self.dst_shard, self.NODES)
         self.g_nodes = self.torch.ones_like(self.nodes)
-        self.launches = 10  # + gather, scatter and their adjoints
+        self.launches = 8  # radial kernels + message sum and the node-gradient sum
 
     def step(self, x=None, y=None, g=None):
         torch = self.torch
         nodes = (self.nodes if x is None else x).detach().requires_grad_(True)
         ang = (self.angular if y is None else y).detach().requires_grad_(True)
         hidden = self.trunk(self.basis(self.r))
-        messages = self.model(self.gather(nodes, self.edge_index), ang, hidden)
+        # the gather by source is folded into the radial kernels (no [E, 896] copy)
+        messages = self.radial_messages(self.model, nodes, self.edge_index, ang, hidden)
         out = self.scatter_sum(messages, self.edge_index)
         grads = torch.autograd.grad(out, [nodes, ang] + self.params,
                                     self.g_nodes if g is None else g)
@@ -548,9 +551,10 @@ class RadialMpWorkload(RadialWorkload):
     def config(self):
         c = super().config()
         c["workload"] = ("message-passing layer (config 5 shapes): node features [65536, 896] "
-                         "gathered by source, Bessel(8) x cosine cutoff, MLP 8-64-64 SiLU, fused "
-                         "affine + V=1 uvu C64 m3, messages summed into destination nodes in a "
-                         "fixed order; VJP to node features, angular and all parameters")
+                         "read by source inside the radial kernels (no gathered copy), Bessel(8) "
+                         "x cosine cutoff, MLP 8-64-64 SiLU, fused affine + V=1 uvu C64 m3, "
+                         "messages summed into destination nodes in a fixed order; VJP to node "
+                         "features, angular and all parameters")
         c["parallelism"] = (f"edge shards on {self.world} GPU(s), full node set per rank, one "
                             "NCCL all_reduce of node-feature and parameter gradients")
         return c
@@ -885,14 +889,15 @@ def run_gpu(args) -> dict | None:
         achieved = work / (kms * 1e-3) / 1e9
         roof = {"kernel": name, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS)",
-                "algorithmic_bytes_per_launch": work, "traffic": TRAFFIC.get(name)}
+                "algorithmic_bytes_per_launch": work, "traffic": traffic_of(wl, name)[0],
+                "traffic_source": traffic_of(wl, name)[1]}
     else:
         achieved = work / (kms * 1e-3) / 1e12
         roof = {"kernel": name, "bound": "fp32", "achieved": achieved, "peak": FP32_PEAK_TFLOPS,
                 "unit": "TFLOP/s", "frac": achieved / FP32_PEAK_TFLOPS,
                 "peak_source": "nominal FP32 FMA peak at the 1965 MHz max SM clock (strict "
                                "FP32, no tensor cores)", "algorithmic_flops_per_launch": work,
-                "traffic": TRAFFIC.get(name)}
+                "traffic": traffic_of(wl, name)[0], "traffic_source": traffic_of(wl, name)[1]}
     total_units = wl.units * world if wl.scaling == "weak" else wl.total
     value = total_units / (ms * 1e-3)
     result = {
@@ -924,11 +929,19 @@ def run_gpu(args) -> dict | None:
     return result
 
 
-# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
-# dominant kernels from ncu captures, scaled to the bench launch by units
-# processed (profiles/tp_*_c128_m6_full.md give the commands and the raw figures:
-# 1,063.0 MB and 624.5 MB at 16,384 rows, x4 for the 65,536-row bench launch).
-TRAFFIC = {"tp_backward": 4.252e9, "tp_forward": 2.498e9}
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one 16,384-row
+# launch of the TensorProduct(128, 6, full) kernels, from ncu; the line carries it
+# scaled by rows to the launch it reports, and says so.
+TRAFFIC_16K_ROWS = {"tp_backward": 1.0626e9, "tp_forward": 0.6245e9}
+
+
+def traffic_of(wl, name):
+    """(bytes per launch, how obtained) for the dominant kernel, or (None, None)."""
+    if wl.name == "tp" and name in TRAFFIC_16K_ROWS:
+        return (TRAFFIC_16K_ROWS[name] * wl.rows / 16384,
+                "ncu DRAM bytes of a 16,384-row launch of the same kernel, scaled by rows to "
+                f"this {wl.rows}-row launch")
+    return None, None
 
 
 def vs_baseline(wl, args, value):
@@ -1023,10 +1036,21 @@ def run_sweep(args) -> dict:
                         fwd = median_ms(fwd_graph)
                         both = median_ms(both_graph)
                         del fwd_graph, both_graph
+                        # each forward kernel the dispatcher chooses between, forced
+                        variants = {}
+                        for variant in ("grouped", "wide"):
+                            os.environ["ICTC_TP_FORWARD"] = variant
+                            try:
+                                vg = capture(lambda: ops.tp_forward(xs, ys, w, *cfg))
+                                variants[variant] = median_ms(vg)
+                                del vg
+                            finally:
+                                del os.environ["ICTC_TP_FORWARD"]
                         launches += 5 * (steps + 2)
                         shapes.append({
                             "channels": channels, "m_max": m_max, "parity": parity,
                             "rows": rows, "width": W, "fwd_ms": fwd, "fwd_vjp_ms": both,
+                            "fwd_variant_ms": variants,
                             "fwd_hbm_frac": 12 * W * rows / (fwd * 1e-3) / 1e9 / hbm,
                             "fwd_vjp_hbm_frac": 32 * W * rows / (both * 1e-3) / 1e9 / hbm})
                     del x, y, g, tp

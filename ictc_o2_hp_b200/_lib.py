@@ -55,6 +55,10 @@ SIGNATURES = {
     "ictc_o2_radial_forward": (_i32, [_vp] * 6 + [_i64] + [_i32] * 8 + [_vp, _vp, _size, _vp]),
     "ictc_o2_radial_backward": (_i32, [_vp] * 11 + [_i64] + [_i32] * 8 +
                                 [_i32, _vp, _vp, _size, _vp]),
+    "ictc_o2_radial_forward_gathered": (_i32, [_vp, _vp, _i64] + [_vp] * 5 + [_i64] +
+                                        [_i32] * 8 + [_vp, _vp, _size, _vp]),
+    "ictc_o2_radial_backward_gathered": (_i32, [_vp, _vp, _i64] + [_vp] * 10 + [_i64] +
+                                         [_i32] * 8 + [_i32, _vp, _vp, _size, _vp]),
     "ictc_o2_gather_rows": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ictc_o2_segment_sum": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ictc_o2_graph_bad_index": (_i32, [ctypes.POINTER(_i32)]),
@@ -227,6 +231,26 @@ def radial_forward(left, angular, hidden, alpha, bias, out, rconfig, table, work
         ptr(left), ptr(angular), ptr(hidden), ptr(alpha), ptr(bias), ptr(out), left.shape[0],
         *rconfig, ptr(table), ptr(workspace), workspace.numel(), stream_of(left.device)),
         "radial_forward")
+
+
+def radial_forward_gathered(nodes, index, angular, hidden, alpha, bias, out, rconfig, table,
+                            workspace):
+    """Raises NotImplementedError for a configuration the edge tile does not cover."""
+    check(load().ictc_o2_radial_forward_gathered(
+        ptr(nodes), ptr(index), nodes.shape[0], ptr(angular), ptr(hidden), ptr(alpha), ptr(bias),
+        ptr(out), index.shape[0], *rconfig, ptr(table), ptr(workspace), workspace.numel(),
+        stream_of(nodes.device)), "radial_forward_gathered")
+
+
+def radial_backward_gathered(nodes, index, angular, hidden, alpha, bias, grad_output, gx, gy, gh,
+                             ga, gb, rconfig, needed, table, workspace):
+    """gx: per-edge gradient of the gathered rows.  Raises NotImplementedError for a
+    request the edge tile does not cover."""
+    check(load().ictc_o2_radial_backward_gathered(
+        ptr(nodes), ptr(index), nodes.shape[0], ptr(angular), ptr(hidden), ptr(alpha), ptr(bias),
+        ptr(grad_output), ptr(gx), ptr(gy), ptr(gh), ptr(ga), ptr(gb), index.shape[0], *rconfig,
+        int(needed), ptr(table), ptr(workspace), workspace.numel(), stream_of(nodes.device)),
+        "radial_backward_gathered")
 
 
 def radial_backward(left, angular, hidden, alpha, bias, grad_output, gx, gy, gh, ga, gb, rconfig,

@@ -221,7 +221,14 @@ struct RadTileArgs {
   bool vec;  // 16-byte access to 4-channel groups of opnd / x / out
   float* gw = nullptr;  // dx mode, optional: edge-weight gradient [rows][Wn]
   int64_t Wn = 0;
+  // optional gather of the first input: row e of x is row xrow[e] of the x source
+  // (forward: opnd, dx mode: x), which has xrows rows; null = row e itself
+  const int64_t* xrow = nullptr;
+  int64_t xrows = 0;
 };
+
+// Device error code of an x-row index outside [0, xrows) (the row reads as zeros).
+constexpr int kBadGatherIndex = 17;
 
 // Thread tiles: 4 edges x NH groups of 4 channels (NH = 2: 256 threads, the 4x8
 // "split" tile; NH = 1: 512 threads, the 4x4 "wide" tile with half the registers
@@ -243,7 +250,8 @@ inline size_t radial_tile_smem(int ut, int H, int W2, int np, int n1, int n2, bo
                         static_cast<size_t>(np) * 8 + (dx ? rt * w2s : 0);
   const size_t aligned_floats = (floats + 3) & ~size_t(3);
   const size_t ints = static_cast<size_t>(np) * 4 + static_cast<size_t>(n1 + n2) * 2 + np;
-  return 128 + (aligned_floats + ints) * 4;
+  const size_t rows64 = rt;  // x row of each edge of the tile
+  return 128 + (aligned_floats + ints) * 4 + 8 + rows64 * 8;
 }
 
 // Loads 4 channels x D values of one entry of one row (zeros past U or rows).
@@ -309,6 +317,9 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
   int2* in1 = reinterpret_cast<int2*>(paths + np);
   int2* in2 = in1 + A.t.n1;
   int* order = reinterpret_cast<int*>(in2 + A.t.n2);
+  // x source row of each edge of the tile (-1: past the rows or a bad index)
+  int64_t* xr = reinterpret_cast<int64_t*>(
+      (reinterpret_cast<uintptr_t>(order + np) + 7) & ~static_cast<uintptr_t>(7));
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * RT;
   // Channel tiles: the forward spreads them over blockIdx.y; the dx mode walks them
   // inside the CTA (dy sums over every channel, so one CTA owns an edge's dy).
@@ -324,6 +335,18 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
   for (int q = tid; q < np * 8; q += NT) coef[q] = __ldg(A.t.coef + q);
   for (int q = tid; q < A.t.n1; q += NT) in1[q] = A.t.in1[q];
   for (int q = tid; q < A.t.n2; q += NT) in2[q] = A.t.in2[q];
+  for (int r = tid; r < RT; r += NT) {
+    const int64_t row = row0 + r;
+    int64_t v = -1;
+    if (row < A.rows) {
+      v = A.xrow != nullptr ? __ldg(A.xrow + row) : row;
+      if (A.xrow != nullptr && (v < 0 || v >= A.xrows)) {
+        atomicExch(&g_ictc_device_error, kBadGatherIndex);
+        v = -1;
+      }
+    }
+    xr[r] = v;
+  }
   for (int idx = tid; idx < RT * A.H; idx += NT) {
     const int r = idx / A.H, h = idx - r * A.H;
     const int64_t row = row0 + r;
@@ -405,10 +428,13 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
 #pragma unroll
       for (int ee = 0; ee < 4; ++ee) {
         const int64_t row = row0 + e0 + ee;
+        const int64_t xrow = xr[e0 + ee];
         if (row < A.rows) {
-          const float* xr = (MODE == kRtFwd ? A.opnd : A.x) + row * A.W1 + ea.x +
-                            static_cast<int64_t>(ub) * ea.y;
-          if (tc * 32 < uspan * ea.y) prefetch_l1(xr + tc * 32);
+          if (xrow >= 0) {
+            const float* xp = (MODE == kRtFwd ? A.opnd : A.x) + xrow * A.W1 + ea.x +
+                              static_cast<int64_t>(ub) * ea.y;
+            if (tc * 32 < uspan * ea.y) prefetch_l1(xp + tc * 32);
+          }
           if (MODE == kRtDx) {
             const float* gr = A.opnd + row * A.W1 + eb.x + static_cast<int64_t>(ub) * eb.y;
             if (tc * 32 < uspan * eb.y) prefetch_l1(gr + tc * 32);
@@ -469,6 +495,9 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
           const int r = e0 + ee;
           const int64_t row = row0 + r;
           const bool row_ok = row < A.rows;
+          const int64_t xrw = xr[r];  // x source row (-1: none)
+          const bool x_ok = xrw >= 0;
+          const int64_t xoff = (x_ok ? xrw : 0) * A.W1;
           const float y0 = angt[r * W2s + ej.x];
           const float y1 = ej.y == 2 ? angt[r * W2s + ej.x + 1] : 0.f;
           // C[kc][a] = sum_b c[4 kc + 2 a + b] y_b
@@ -480,8 +509,8 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
             const int u = ub + half * (UT / NH) + tc * 4;
             if (MODE == kRtFwd) {
               float xv[4 * D1];
-              load4<D1>(xv, A.opnd + row * A.W1 + ei.x + static_cast<int64_t>(u) * D1, row_ok, u,
-                        A.U, A.vec);
+              load4<D1>(xv, A.opnd + xoff + ei.x + static_cast<int64_t>(u) * D1, x_ok, u, A.U,
+                        A.vec);
               // out[kc] += w sum_a C[kc][a] x[a], both kc at once: (C00, C10) x0 + (C01, C11) x1
               const float2 ca0 = make_float2(c00, c10), ca1 = make_float2(c01, c11);
 #pragma unroll
@@ -504,8 +533,8 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
               float gv[4 * D3], xv[4 * D1];
               load4<D3>(gv, A.opnd + row * A.W1 + ek.x + static_cast<int64_t>(u) * D3, row_ok, u,
                         A.U, A.vec);
-              load4<D1>(xv, A.x + row * A.W1 + ei.x + static_cast<int64_t>(u) * D1, row_ok, u,
-                        A.U, A.vec);
+              load4<D1>(xv, A.x + xoff + ei.x + static_cast<int64_t>(u) * D1, x_ok, u, A.U,
+                        A.vec);
               // dx[a] += w sum_kc C[kc][a] g[kc], both a at once: (C00, C01) g0 + (C10, C11) g1
               const float2 ck0 = make_float2(c00, c01), ck1 = make_float2(c10, c11);
               float gwv[4];
@@ -1105,11 +1134,16 @@ extern "C" int32_t ictc_o2_radial_workspace(ICTC_RADIAL_ARGS, int64_t rows, int3
   return ICTC_OK;
 }
 
-extern "C" int32_t ictc_o2_radial_forward(const float* left, const float* angular,
-                                          const float* radial_hidden, const float* alpha,
-                                          const float* bias, float* output, int64_t rows,
-                                          ICTC_RADIAL_ARGS, const void* device_table,
-                                          void* workspace, size_t workspace_bytes, void* stream) {
+namespace {
+
+// Forward over rows of `left`, or, with `xrow`, over rows xrow[e] of `left` (which
+// then has xrows rows): only the edge tile reads gathered rows, so a configuration
+// that needs the row tile answers ICTC_ERR_UNSUPPORTED there.
+int32_t radial_forward_impl(const float* left, const int64_t* xrow, int64_t xrows,
+                            const float* angular, const float* radial_hidden,
+                            const float* alpha, const float* bias, float* output, int64_t rows,
+                            ICTC_RADIAL_ARGS, const void* device_table, void* workspace,
+                            size_t workspace_bytes, void* stream) {
   RadialConfig c{};
   UvuTableH th;
   UvuLayout l;
@@ -1137,7 +1171,12 @@ extern "C" int32_t ictc_o2_radial_forward(const float* left, const float* angula
                    aligned(output, 16);
   RadTileArgs ra{left, nullptr, radial_hidden, angular, at, bias, output, nullptr, rows,
                  c.U, Up, c.H, th.width1, th.width2, t, vec};
+  ra.xrow = xrow;
+  ra.xrows = xrows;
   st = launch_radial_tile<kRtFwd>(ra, s);
+  if (st == ICTC_ERR_UNSUPPORTED && xrow != nullptr)
+    return fail(ICTC_ERR_UNSUPPORTED,
+                "gathered radial forward: hidden width %d does not fit the edge tile", c.H);
   if (st == ICTC_ERR_UNSUPPORTED) {
     // hidden tile too large to stay resident: the generic row tile streams it
     RowtileArgs rr{left, nullptr, radial_hidden, angular, at, bias, output, nullptr, rows,
@@ -1147,12 +1186,16 @@ extern "C" int32_t ictc_o2_radial_forward(const float* left, const float* angula
   return st;
 }
 
-extern "C" int32_t ictc_o2_radial_backward(
-    const float* left, const float* angular, const float* radial_hidden, const float* alpha,
-    const float* bias, const float* grad_output, float* grad_left, float* grad_angular,
-    float* grad_hidden, float* grad_alpha, float* grad_bias, int64_t rows, ICTC_RADIAL_ARGS,
-    int32_t needed, const void* device_table, void* workspace, size_t workspace_bytes,
-    void* stream) {
+// Backward; with `xrow` (gathered first input) only the edge tile and the
+// edge-weight-gradient GEMMs run, so a request they do not cover (no dx / dy
+// requested while dalpha, dbias or dhidden are, or a hidden width the edge tile
+// cannot hold) answers ICTC_ERR_UNSUPPORTED.
+int32_t radial_backward_impl(
+    const float* left, const int64_t* xrow, int64_t xrows, const float* angular,
+    const float* radial_hidden, const float* alpha, const float* bias, const float* grad_output,
+    float* grad_left, float* grad_angular, float* grad_hidden, float* grad_alpha,
+    float* grad_bias, int64_t rows, ICTC_RADIAL_ARGS, int32_t needed, const void* device_table,
+    void* workspace, size_t workspace_bytes, void* stream) {
   RadialConfig c{};
   UvuTableH th;
   UvuLayout l;
@@ -1202,6 +1245,11 @@ extern "C" int32_t ictc_o2_radial_backward(
                                               gp.db_part_bytes;
   const bool tvec = (W1 % 4 == 0) && (c.U % 4 == 0) && aligned(left, 16) &&
                     aligned(grad_output, 16) && aligned(grad_left, 16);
+  if (xrow != nullptr &&
+      (!(needed & 3) || ((needed & 28) && !gw_path) ||
+       !radial_tile_fits(c.U, c.H, W2, l.np, l.n1, l.n2, true)))
+    return fail(ICTC_ERR_UNSUPPORTED,
+                "gathered radial backward covers dx / dy requests on the edge tile only");
   if (needed & 3) {
     // dx and dy together: both need the regenerated edge weights
     if (radial_tile_fits(c.U, c.H, W2, l.np, l.n1, l.n2, true))
@@ -1216,6 +1264,8 @@ extern "C" int32_t ictc_o2_radial_backward(
     if (!gw_path) {
       RadTileArgs ra{grad_output, left, radial_hidden, angular, at, bias, grad_left,
                      grad_angular, rows, c.U, Up, c.H, W1, W2, t, tvec};
+      ra.xrow = xrow;
+      ra.xrows = xrows;
       st = launch_radial_tile<kRtDx>(ra, s);
       if (st == ICTC_ERR_UNSUPPORTED) {
         if (c.U > kUT)
@@ -1243,11 +1293,14 @@ extern "C" int32_t ictc_o2_radial_backward(
       bool gw_done = false;
       if (needed & 3) {
         // dx, dy of the block; the tile also writes the block's gw
-        RadTileArgs ra{grad_output + r0 * W1, left + r0 * W1, radial_hidden + r0 * c.H,
-                       angular + r0 * W2, at, bias, grad_left + r0 * W1, grad_angular + r0 * W2,
-                       nb, c.U, Up, c.H, W1, W2, t, tvec};
+        RadTileArgs ra{grad_output + r0 * W1, xrow ? left : left + r0 * W1,
+                       radial_hidden + r0 * c.H, angular + r0 * W2, at, bias,
+                       grad_left + r0 * W1, grad_angular + r0 * W2, nb, c.U, Up, c.H, W1, W2, t,
+                       tvec};
         ra.gw = gw;
         ra.Wn = Wn;
+        ra.xrow = xrow ? xrow + r0 : nullptr;
+        ra.xrows = xrows;
         st = launch_radial_tile<kRtDx>(ra, s);
         if (st == ICTC_ERR_UNSUPPORTED) {  // hidden tile too large: row tile, gw separately
           if (c.U > kUT)
@@ -1340,4 +1393,58 @@ extern "C" int32_t ictc_o2_radial_backward(
   }
   e = cudaGetLastError();
   return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "radial backward launch");
+}
+
+}  // namespace
+
+extern "C" int32_t ictc_o2_radial_forward(const float* left, const float* angular,
+                                          const float* radial_hidden, const float* alpha,
+                                          const float* bias, float* output, int64_t rows,
+                                          ICTC_RADIAL_ARGS, const void* device_table,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+  return radial_forward_impl(left, nullptr, 0, angular, radial_hidden, alpha, bias, output, rows,
+                             channels, m_max, parity, m_max_in2, parity_in2, normalization,
+                             path_normalization, hidden, device_table, workspace,
+                             workspace_bytes, stream);
+}
+
+extern "C" int32_t ictc_o2_radial_backward(
+    const float* left, const float* angular, const float* radial_hidden, const float* alpha,
+    const float* bias, const float* grad_output, float* grad_left, float* grad_angular,
+    float* grad_hidden, float* grad_alpha, float* grad_bias, int64_t rows, ICTC_RADIAL_ARGS,
+    int32_t needed, const void* device_table, void* workspace, size_t workspace_bytes,
+    void* stream) {
+  return radial_backward_impl(left, nullptr, 0, angular, radial_hidden, alpha, bias, grad_output,
+                              grad_left, grad_angular, grad_hidden, grad_alpha, grad_bias, rows,
+                              channels, m_max, parity, m_max_in2, parity_in2, normalization,
+                              path_normalization, hidden, needed, device_table, workspace,
+                              workspace_bytes, stream);
+}
+
+extern "C" int32_t ictc_o2_radial_forward_gathered(
+    const float* nodes, const int64_t* left_index, int64_t node_rows, const float* angular,
+    const float* radial_hidden, const float* alpha, const float* bias, float* output,
+    int64_t rows, ICTC_RADIAL_ARGS, const void* device_table, void* workspace,
+    size_t workspace_bytes, void* stream) {
+  if (rows > 0 && (left_index == nullptr || node_rows < 1))
+    return fail(ICTC_ERR_INVALID, "left_index and node_rows >= 1 are required");
+  return radial_forward_impl(nodes, left_index, node_rows, angular, radial_hidden, alpha, bias,
+                             output, rows, channels, m_max, parity, m_max_in2, parity_in2,
+                             normalization, path_normalization, hidden, device_table, workspace,
+                             workspace_bytes, stream);
+}
+
+extern "C" int32_t ictc_o2_radial_backward_gathered(
+    const float* nodes, const int64_t* left_index, int64_t node_rows, const float* angular,
+    const float* radial_hidden, const float* alpha, const float* bias, const float* grad_output,
+    float* grad_left_edges, float* grad_angular, float* grad_hidden, float* grad_alpha,
+    float* grad_bias, int64_t rows, ICTC_RADIAL_ARGS, int32_t needed, const void* device_table,
+    void* workspace, size_t workspace_bytes, void* stream) {
+  if (rows > 0 && (left_index == nullptr || node_rows < 1))
+    return fail(ICTC_ERR_INVALID, "left_index and node_rows >= 1 are required");
+  return radial_backward_impl(nodes, left_index, node_rows, angular, radial_hidden, alpha, bias,
+                              grad_output, grad_left_edges, grad_angular, grad_hidden, grad_alpha,
+                              grad_bias, rows, channels, m_max, parity, m_max_in2, parity_in2,
+                              normalization, path_normalization, hidden, needed, device_table,
+                              workspace, workspace_bytes, stream);
 }

@@ -1120,11 +1120,15 @@ StagedPlan plan_staged(int device, int64_t rows, const TpLayout& L, bool full, i
 }
 
 // Channel-tiled backward (tp_backward_tiled): used where the untiled staged CTA
-// would hold fewer than kStagedWarps warps (full parity, e.g. C = 96: 6 warps) or
-// cannot be formed (more than kStagedWarps channel groups, e.g. C = 256 full).
-// Tiles of Ct channels (Ct in 128, 64, 32, 16, a multiple of the channels per
-// warp, dividing C) with gt = Ct / channels-per-warp groups and R = 8 / gt rows per
-// stage; floor(SMs / ntiles) CTAs per tile, so every tile has as many CTAs.
+// cannot be formed (more than kStagedWarps channel groups, e.g. C = 256 full) and
+// rows are long enough (m_max >= 3).  Measured over the benchmark sweep (65,536
+// rows, fraction of HBM): C = 256 full m_max 3-6 backward 0.70-0.74 against the
+// direct kernel's 0.40-0.54, but m_max 1-2 0.42 / 0.60 against 0.69 / 0.67, and a
+// 32-channel tiling of C = 96 full lost to the 6-warp untiled CTA at every m_max
+// below 6, so those keep the untiled kernels.  Tiles of Ct channels (Ct in 128,
+// 64, 32, 16, a multiple of the channels per warp, dividing C) with gt = Ct /
+// channels-per-warp groups and R = 8 / gt rows per stage; floor(SMs / ntiles)
+// CTAs per tile, so every tile has as many CTAs.
 struct TiledPlan {
   bool ok, weights_in_smem;
   int Ct, gt, R, ntiles, stages;
@@ -1136,9 +1140,9 @@ TiledPlan plan_tiled(int device, int64_t rows, const TpLayout& L, bool full, int
   TiledPlan p{};
   const int cpw = full ? 16 : 32;
   const int groups = static_cast<int>(ceil_div(L.C, cpw));
-  const bool untiled_short =
-      groups > kStagedWarps || (full && (kStagedWarps / groups) * groups < kStagedWarps);
-  if (!untiled_short || rows == 0 || rows > INT32_MAX || L.C % 16 != 0) return p;
+  const int m_max = static_cast<int>((L.width / L.C / (full ? 2 : 1) - 1) / 2);
+  if (groups <= kStagedWarps || m_max < 3 || rows == 0 || rows > INT32_MAX || L.C % 16 != 0)
+    return p;
   for (int ct : {128, 64, 32, 16}) {
     if (ct % cpw == 0 && ct < L.C && L.C % ct == 0) {
       p.Ct = ct;
@@ -1149,7 +1153,6 @@ TiledPlan plan_tiled(int device, int64_t rows, const TpLayout& L, bool full, int
   p.gt = p.Ct / cpw;
   p.R = kStagedWarps / p.gt;
   p.ntiles = L.C / p.Ct;
-  const int m_max = static_cast<int>((L.width / L.C / (full ? 2 : 1) - 1) / 2);
   const TpLayout Lt = tp_layout(p.Ct, m_max, full, L.cm);
   const size_t stage_bytes = static_cast<size_t>(3) * p.R * Lt.width * sizeof(float);
   const size_t wbytes = static_cast<size_t>(chunks) * p.gt * 32 * sizeof(float4);

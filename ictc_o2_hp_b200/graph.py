@@ -140,3 +140,147 @@ def scatter_sum(messages: Tensor, edges: EdgeIndex, which: str = "dst") -> Tenso
     if messages.shape[0] != edges.num_edges:
         raise ValueError("messages must have one row per edge of the EdgeIndex")
     return segment_sum(messages, *edges.csr(which))
+
+
+# ------------------------------------------------- radial product over gathered rows
+
+
+@torch.library.custom_op(f"{NAMESPACE}::radial_forward_gathered", mutates_args=())
+def radial_forward_gathered(nodes: Tensor, index: Tensor, order: Tensor, offsets: Tensor,
+                            angular: Tensor, hidden: Tensor, alpha: Tensor, bias: Tensor,
+                            table: Tensor, rconfig: list[int], has_bias: bool) -> Tensor:
+    """uvu(nodes[index], angular, hidden @ alpha^T + bias): the radial product with
+    the node gather folded into the edge kernels (ictc_o2_radial_forward_gathered);
+    order / offsets (the CSR of index) serve the adjoint.  Configurations the edge
+    tile does not cover gather the rows first."""
+    from .ops import require_cuda_float32
+    require_cuda_float32("radial messages", nodes, angular, hidden, alpha)
+    nodes, angular, hidden = nodes.contiguous(), angular.contiguous(), hidden.contiguous()
+    alpha = alpha.contiguous()
+    bias_c = bias.contiguous() if has_bias else None
+    out = nodes.new_empty(index.shape[0], nodes.shape[1])
+    with torch.cuda.device(nodes.device):
+        fwd, _ = _lib.radial_workspace(rconfig, index.shape[0], nodes.device)
+        workspace = torch.empty(max(fwd, 16), dtype=torch.uint8, device=nodes.device)
+        try:
+            _lib.radial_forward_gathered(nodes, index, angular, hidden, alpha, bias_c, out,
+                                         rconfig, table, workspace)
+        except NotImplementedError:
+            left = nodes.index_select(0, index)
+            _lib.radial_forward(left, angular, hidden, alpha, bias_c, out, rconfig, table,
+                                workspace)
+    return out
+
+
+@radial_forward_gathered.register_fake
+def _radial_forward_gathered_fake(nodes, index, order, offsets, angular, hidden, alpha, bias,
+                                  table, rconfig, has_bias):
+    return nodes.new_empty(index.shape[0], nodes.shape[1])
+
+
+@torch.library.custom_op(f"{NAMESPACE}::radial_backward_gathered", mutates_args=())
+def radial_backward_gathered(nodes: Tensor, index: Tensor, angular: Tensor, hidden: Tensor,
+                             alpha: Tensor, bias: Tensor, grad_output: Tensor, table: Tensor,
+                             rconfig: list[int], has_bias: bool, needed: int
+                             ) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """(per-edge gradient of the gathered rows, g_angular, g_hidden, g_alpha, g_bias)
+    for the role mask `needed` (1, 2, 4, 8, 16); absent roles are empty."""
+    from .ops import require_cuda_float32
+    require_cuda_float32("radial messages backward", nodes, angular, hidden, alpha, grad_output)
+    nodes, angular, hidden = nodes.contiguous(), angular.contiguous(), hidden.contiguous()
+    alpha, grad_output = alpha.contiguous(), grad_output.contiguous()
+    if not has_bias:
+        needed &= ~16
+    bias_c = bias.contiguous() if has_bias else None
+    rows = index.shape[0]
+    want_xy = bool(needed & 3)
+    gx = nodes.new_empty(rows, nodes.shape[1]) if want_xy else nodes.new_empty(0)
+    gy = torch.empty_like(angular) if want_xy else angular.new_empty(0)
+    gh = torch.empty_like(hidden) if needed & 4 else hidden.new_empty(0)
+    ga = torch.empty_like(alpha) if needed & 24 else alpha.new_empty(0)
+    gb = torch.empty_like(bias) if needed & 16 else alpha.new_empty(0)
+    mask = needed | (3 if want_xy else 0) | (8 if needed & 16 else 0)
+    args = (gx if want_xy else None, gy if want_xy else None, gh if needed & 4 else None,
+            ga if needed & 24 else None, gb if needed & 16 else None)
+    with torch.cuda.device(nodes.device):
+        _, bwd = _lib.radial_workspace(rconfig, rows, nodes.device)
+        workspace = torch.empty(max(bwd, 16), dtype=torch.uint8, device=nodes.device)
+        try:
+            _lib.radial_backward_gathered(nodes, index, angular, hidden, alpha, bias_c,
+                                          grad_output, *args, rconfig, mask, table, workspace)
+        except NotImplementedError:
+            left = nodes.index_select(0, index)
+            _lib.radial_backward(left, angular, hidden, alpha, bias_c, grad_output, *args,
+                                 rconfig, mask, table, workspace)
+    return (gx if needed & 1 else nodes.new_empty(0), gy if needed & 2 else angular.new_empty(0),
+            gh, ga if needed & 8 else alpha.new_empty(0), gb)
+
+
+@radial_backward_gathered.register_fake
+def _radial_backward_gathered_fake(nodes, index, angular, hidden, alpha, bias, grad_output, table,
+                                   rconfig, has_bias, needed):
+    if not has_bias:
+        needed &= ~16
+    rows = index.shape[0]
+    return (nodes.new_empty(rows, nodes.shape[1]) if needed & 1 else nodes.new_empty(0),
+            torch.empty_like(angular) if needed & 2 else angular.new_empty(0),
+            torch.empty_like(hidden) if needed & 4 else hidden.new_empty(0),
+            torch.empty_like(alpha) if needed & 8 else alpha.new_empty(0),
+            torch.empty_like(bias) if needed & 16 else alpha.new_empty(0))
+
+
+def _gathered_setup(ctx, inputs, output):
+    nodes, index, order, offsets, angular, hidden, alpha, bias, table, rconfig, has_bias = inputs
+    ctx.save_for_backward(nodes, index, order, offsets, angular, hidden, alpha, bias, table)
+    ctx.rconfig, ctx.has_bias = rconfig, has_bias
+
+
+def _gathered_autograd(ctx, grad_output):
+    if torch.is_grad_enabled():
+        raise NotImplementedError(
+            "second derivatives through radial_messages are not available; use "
+            "gather(nodes, edges) and the RadialUvuTensorProduct module for them")
+    nodes, index, order, offsets, angular, hidden, alpha, bias, table = ctx.saved_tensors
+    need = ctx.needs_input_grad
+    flags = [need[0], need[4], need[5], need[6], need[7] and ctx.has_bias]
+    needed = sum(int(f) << i for i, f in enumerate(flags))
+    if needed == 0:
+        return (None,) * 11
+    gx, gy, gh, ga, gb = radial_backward_gathered(nodes, index, angular, hidden, alpha, bias,
+                                                  grad_output.contiguous(), table, ctx.rconfig,
+                                                  ctx.has_bias, needed)
+    g_nodes = segment_sum(gx, index, order, offsets) if flags[0] else None
+    return (g_nodes, None, None, None, gy if flags[1] else None, gh if flags[2] else None,
+            ga if flags[3] else None, gb if flags[4] else None, None, None, None)
+
+
+radial_forward_gathered.register_autograd(_gathered_autograd, setup_context=_gathered_setup)
+
+
+def radial_messages(model, nodes: Tensor, edges: EdgeIndex, angular: Tensor,
+                    radial_hidden: Tensor, which: str = "src") -> Tensor:
+    """Per-edge messages ``model(gather(nodes, edges, which), angular, radial_hidden)``
+    of a RadialUvuTensorProduct ``model``, with the gather folded into the radial
+    kernels: the [num_edges, width1] gathered copy of the node features is never
+    written.  The node-feature gradient sums the per-edge gradients in the edges'
+    CSR order (deterministic), as the adjoint of ``gather`` does, so the result is
+    the same as that of ``model(gather(nodes, edges, which), ...)``, bit for bit.
+    Second derivatives are not available through this fused form; use ``gather``
+    and the module for them."""
+    tp = model.tp
+    if nodes.dim() != 2 or nodes.shape[1] != tp.input1_dimension:
+        raise ValueError("nodes must be [num_nodes, tp.input1_dimension]")
+    if nodes.shape[0] != edges.num_nodes:
+        raise ValueError("nodes must have one row per node of the EdgeIndex")
+    E = edges.num_edges
+    if angular.shape != (E, tp.input2_dimension):
+        raise ValueError("angular must be [num_edges, tp.input2_dimension]")
+    if radial_hidden.shape != (E, model.radial_out.in_features):
+        raise ValueError("radial_hidden must be [num_edges, radial_out.in_features]")
+    index, order, offsets = edges.csr(which)
+    bias = model.radial_out.bias
+    has_bias = bias is not None
+    return radial_forward_gathered(nodes, index, order, offsets, angular, radial_hidden,
+                                   model.radial_out.weight,
+                                   bias if has_bias else model.radial_out.weight.new_empty(0),
+                                   tp._table, model._rconfig(), has_bias)

@@ -57,7 +57,8 @@ ICTC_API int32_t ictc_o2_abi_version(void);
  * and that kernel stopped early, so its outputs are invalid.  Codes: 1-4
  * TensorProduct staged kernels (stage ring, drain, weight copy), 5-6 radial edge
  * tile, 7-8 shared-weight uvu tile, 9-10 per-row uvu streamed kernel, 11-12
- * per-row uvu quad kernel, 13 the wait probe.  No counterpart in the reference,
+ * per-row uvu quad kernel, 13 the wait probe; 17 is not a wait: a gathered radial
+ * call met a node index out of range.  No counterpart in the reference,
  * whose Triton kernels have no waits. */
 ICTC_API int32_t ictc_o2_device_error(int32_t* code);
 
@@ -232,6 +233,33 @@ ICTC_API int32_t ictc_o2_radial_backward(const float* left, const float* angular
                                          int32_t path_normalization, int32_t hidden,
                                          int32_t needed, const void* device_table,
                                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* The radial product with the node gather folded into its first input (no
+ * counterpart in the reference, whose chain starts at per-edge inputs,
+ * docs/RADIAL.md:97-99): row e of `left` is row left_index[e] of nodes
+ * [node_rows, width1], read in place by the edge kernels instead of a gathered
+ * [N, width1] copy.  The backward writes the gradient of each edge's gathered row,
+ * grad_left_edges [N, width1] (sum it into the nodes with ictc_o2_segment_sum over
+ * the edges grouped by left_index).  Only the edge-tile kernels read gathered
+ * rows: a hidden width they cannot hold, or a backward request without the left /
+ * angular roles but with hidden, alpha or bias, answers ICTC_ERR_UNSUPPORTED
+ * (gather with ictc_o2_gather_rows and use the entries above instead).  An index
+ * outside [0, node_rows) reads a zero row and sets device error code 17. */
+ICTC_API int32_t ictc_o2_radial_forward_gathered(
+    const float* nodes, const int64_t* left_index, int64_t node_rows, const float* angular,
+    const float* radial_hidden, const float* alpha, const float* bias, float* output,
+    int64_t rows, int32_t channels, int32_t m_max, int32_t parity, int32_t m_max_in2,
+    int32_t parity_in2, int32_t normalization, int32_t path_normalization, int32_t hidden,
+    const void* device_table, void* workspace, size_t workspace_bytes, void* stream);
+
+ICTC_API int32_t ictc_o2_radial_backward_gathered(
+    const float* nodes, const int64_t* left_index, int64_t node_rows, const float* angular,
+    const float* radial_hidden, const float* alpha, const float* bias, const float* grad_output,
+    float* grad_left_edges, float* grad_angular, float* grad_hidden, float* grad_alpha,
+    float* grad_bias, int64_t rows, int32_t channels, int32_t m_max, int32_t parity,
+    int32_t m_max_in2, int32_t parity_in2, int32_t normalization, int32_t path_normalization,
+    int32_t hidden, int32_t needed, const void* device_table, void* workspace,
+    size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------
  * Message-passing plumbing around the radial product (the node gather and the

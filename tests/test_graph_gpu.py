@@ -127,3 +127,44 @@ def test_segment_sum_rejects_non_csr_offsets(cuda_device):
     assert _lib.graph_bad_index() == 1
     assert torch.equal(out[0], values[0] + values[1])
     assert torch.count_nonzero(out[1]) == 0 and torch.count_nonzero(out[2]) == 0
+
+
+@pytest.mark.parametrize("u,m_max,hidden,bias,nodes,edges", [
+    (64, 3, 64, False, 700, 5000),   # config-5 shape
+    (16, 2, 8, True, 50, 333),
+    (32, 2, 512, True, 40, 150),     # hidden too wide for the edge tile: gathers first
+])
+def test_radial_messages_match_gather_then_module(u, m_max, hidden, bias, nodes, edges,
+                                                  cuda_device):
+    """radial_messages (the gather folded into the radial kernels) against
+    model(gather(nodes, edges), angular, hidden): messages and every gradient
+    (node features, angular, hidden, alpha, bias), bit for bit."""
+    from ictc_o2_hp_b200 import RadialUvuTensorProduct, UvuTensorProduct
+    from ictc_o2_hp_b200.graph import EdgeIndex, gather, radial_messages
+    torch.manual_seed(u + edges)
+    tp = UvuTensorProduct(u, 1, m_max, parity="full", parity_in2="canonical",
+                          shared_weights=False)
+    model = RadialUvuTensorProduct(tp, torch.nn.Linear(hidden, tp.weight_numel, bias=bias))
+    model = model.to(cuda_device)
+    src = torch.randint(0, nodes, (edges,), device=cuda_device)
+    dst = torch.randint(0, nodes, (edges,), device=cuda_device)
+    ei = EdgeIndex(src, dst, nodes)
+    feats = torch.randn(nodes, tp.input1_dimension, device=cuda_device, requires_grad=True)
+    ang = torch.randn(edges, tp.input2_dimension, device=cuda_device, requires_grad=True)
+    h = torch.randn(edges, hidden, device=cuda_device, requires_grad=True)
+    g = torch.randn(edges, tp.representation_dimension, device=cuda_device)
+    params = [model.radial_out.weight] + ([model.radial_out.bias] if bias else [])
+    fused = radial_messages(model, feats, ei, ang, h)
+    ref = model(gather(feats, ei), ang, h)
+    assert torch.equal(fused, ref)
+    gf = torch.autograd.grad(fused, (feats, ang, h, *params), g)
+    gr = torch.autograd.grad(ref, (feats, ang, h, *params), g)
+    for a, b in zip(gf, gr):
+        assert torch.equal(a, b)
+    # parameter gradients alone (no node or angular role): the unfused kernels run
+    only = torch.autograd.grad(radial_messages(model, feats, ei, ang, h), params, g)
+    for a, b in zip(only, gr[3:]):
+        assert torch.equal(a, b)
+    with pytest.raises(NotImplementedError):
+        (dx,) = torch.autograd.grad(radial_messages(model, feats, ei, ang, h), (feats,), g,
+                                    create_graph=True)

@@ -93,12 +93,13 @@ SHAPES = [
     (5, 7, "full", "component", 11),
     (3, 8, "canonical", "norm", 6),
     (48, 1, "full", "component", 1000),
-    # channel-tiled backward (tiles of 32 / 16 / 64 / 128 channels)
+    # channel-tiled backward (more channel groups than a staged CTA holds, m_max >= 3:
+    # tiles of 64 / 128 channels) and the shapes next to it that keep the untiled kernels
     (96, 3, "full", "component", 300),
-    (48, 2, "full", "norm", 77),
     (192, 4, "full", "component", 21),
+    (256, 3, "full", "norm", 33),
     (256, 2, "full", "component", 13),
-    (320, 1, "canonical", "component", 40),
+    (320, 3, "canonical", "component", 40),
 ]
 
 
@@ -246,7 +247,7 @@ def test_tuple_and_component_major_layouts(cuda_device):
     (128, 6, "full", 2048, None),      # the benchmark configuration's width (staged kernels)
     (9, 4, "full", 50, "direct"),      # odd channel count, direct kernels
     (32, 2, "full", 640, "grouped"),
-    (96, 3, "full", 200, None),        # channel-tiled backward
+    (256, 3, "full", 200, None),       # channel-tiled backward
 ])
 def test_component_major_in_place(channels, m_max, parity, rows, variant, cuda_device,
                                   monkeypatch):
@@ -339,9 +340,9 @@ def test_layout_classes_against_reference(name, cuda_device):
 
 
 @pytest.mark.parametrize("channels,m_max,parity,rows", [
-    (96, 6, "full", 333),
-    (256, 3, "full", 70),
-    (160, 2, "full", 129),
+    (256, 6, "full", 333),
+    (192, 3, "full", 70),
+    (320, 4, "canonical", 129),
 ])
 def test_tiled_backward_matches_untiled(channels, m_max, parity, rows, cuda_device, monkeypatch):
     """The channel-tiled backward (ICTC_TP_BACKWARD unset or "tiled") against the
