@@ -47,9 +47,9 @@ __global__ void __launch_bounds__(256, 1) uvu_dw_stage(DwArgs A) {
   const int p = blockIdx.x;
   const int4 pt = A.t.paths[p];
   const int2 ei = A.t.in1[pt.x], ej = A.t.in2[pt.y], ek = A.t.in1[pt.z];
-  float c[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) c[e] = __ldg(A.t.coef + 8 * p + e);
+  // coefficient pairs over b: (c[4 kc + 2 a], c[4 kc + 2 a + 1])
+  const float2* cp = reinterpret_cast<const float2*>(A.t.coef + 8 * p);
+  const float2 c0 = __ldg(cp), c1 = __ldg(cp + 1), c2 = __ldg(cp + 2), c3 = __ldg(cp + 3);
   const int64_t rbeg = static_cast<int64_t>(blockIdx.y) * A.chunk_rows;
   const int64_t rend = rbeg + A.chunk_rows < A.rows ? rbeg + A.chunk_rows : A.rows;
   const int64_t nsteps = rend > rbeg ? (rend - rbeg + kDwRows - 1) / kDwRows : 0;
@@ -104,9 +104,12 @@ __global__ void __launch_bounds__(256, 1) uvu_dw_stage(DwArgs A) {
       const int r = gh * (kDwRows / 2) + rr;
       const float2 xv = dy_slot(&S.xs[buf][r][gu * ei.y], ei.y);
       const float2 gv = dy_slot(&S.gs[buf][r][gu * ek.y], ek.y);
-      const float x0 = xv.x, x1 = xv.y, g0 = gv.x, g1 = gv.y;
-      S.S[2 * r][gu] = g0 * fmaf(c[2], x1, c[0] * x0) + g1 * fmaf(c[6], x1, c[4] * x0);
-      S.S[2 * r + 1][gu] = g0 * fmaf(c[3], x1, c[1] * x0) + g1 * fmaf(c[7], x1, c[5] * x0);
+      // (s0, s1) = g0 (c0 x0 + c1 x1) + g1 (c2 x0 + c3 x1), both b at once (f32x2)
+      const float2 t0 = fma2(xv.y, c1, __fmul2_rn(make_float2(xv.x, xv.x), c0));
+      const float2 t1 = fma2(xv.y, c3, __fmul2_rn(make_float2(xv.x, xv.x), c2));
+      const float2 sv = fma2(gv.y, t1, __fmul2_rn(make_float2(gv.x, gv.x), t0));
+      S.S[2 * r][gu] = sv.x;
+      S.S[2 * r + 1][gu] = sv.y;
     }
     // Y[(r, b)][v] = y_j[r, v, b] (zero for b >= d2)
     for (int q = tid; q < 2 * kDwRows * kDwV; q += 256) {

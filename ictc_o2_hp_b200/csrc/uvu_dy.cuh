@@ -125,19 +125,19 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
     const int p = A.t.by_j[pos];
     const int4 pt = A.t.paths[p];
     const int2 ei = A.t.in1[pt.x], ej = A.t.in2[pt.y], ek = A.t.in1[pt.z];
-    float c[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) c[e] = __ldg(A.t.coef + 8 * p + e);
-    // s[b] = sum_{kc,a} c[4 kc + 2 a + b] g[kc] x[a]
+    // coefficient pairs over b: (c[4 kc + 2 a], c[4 kc + 2 a + 1])
+    const float2* cp = reinterpret_cast<const float2*>(A.t.coef + 8 * p);
+    const float2 c0 = __ldg(cp), c1 = __ldg(cp + 1), c2 = __ldg(cp + 2), c3 = __ldg(cp + 3);
+    // (s0, s1) = g0 (c0 x0 + c1 x1) + g1 (c2 x0 + c3 x1), both b at once (f32x2)
 #pragma unroll 4
     for (int rr = 0; rr < kDyRows / 2; ++rr) {
       const int r = gh * (kDyRows / 2) + rr;
       const float2 xv = dy_slot(&S.xs[r][gu * ei.y], ei.y);
       const float2 gv = dy_slot(&S.gs[r][gu * ek.y], ek.y);
-      const float x0 = xv.x, x1 = xv.y, g0 = gv.x, g1 = gv.y;
-      const float s0 = g0 * fmaf(c[2], x1, c[0] * x0) + g1 * fmaf(c[6], x1, c[4] * x0);
-      const float s1 = g0 * fmaf(c[3], x1, c[1] * x0) + g1 * fmaf(c[7], x1, c[5] * x0);
-      *reinterpret_cast<float2*>(&S.S[gu][2 * r]) = make_float2(s0, s1);
+      const float2 t0 = fma2(xv.y, c1, __fmul2_rn(make_float2(xv.x, xv.x), c0));
+      const float2 t1 = fma2(xv.y, c3, __fmul2_rn(make_float2(xv.x, xv.x), c2));
+      *reinterpret_cast<float2*>(&S.S[gu][2 * r]) =
+          fma2(gv.y, t1, __fmul2_rn(make_float2(gv.x, gv.x), t0));
     }
     __syncthreads();  // S built; x / g free for the next path
     issue_xg(pos + 1);

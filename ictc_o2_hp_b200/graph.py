@@ -145,6 +145,13 @@ def scatter_sum(messages: Tensor, edges: EdgeIndex, which: str = "dst") -> Tenso
 # ------------------------------------------------- radial product over gathered rows
 
 
+def _fused_gather() -> bool:
+    """ICTC_RADIAL_GATHER=materialize gathers the rows into a copy first and runs the
+    plain radial kernels (same results; for comparisons)."""
+    import os
+    return os.environ.get("ICTC_RADIAL_GATHER", "fused") != "materialize"
+
+
 @torch.library.custom_op(f"{NAMESPACE}::radial_forward_gathered", mutates_args=())
 def radial_forward_gathered(nodes: Tensor, index: Tensor, order: Tensor, offsets: Tensor,
                             angular: Tensor, hidden: Tensor, alpha: Tensor, bias: Tensor,
@@ -163,6 +170,8 @@ def radial_forward_gathered(nodes: Tensor, index: Tensor, order: Tensor, offsets
         fwd, _ = _lib.radial_workspace(rconfig, index.shape[0], nodes.device)
         workspace = torch.empty(max(fwd, 16), dtype=torch.uint8, device=nodes.device)
         try:
+            if not _fused_gather():
+                raise NotImplementedError
             _lib.radial_forward_gathered(nodes, index, angular, hidden, alpha, bias_c, out,
                                          rconfig, table, workspace)
         except NotImplementedError:
@@ -206,6 +215,8 @@ def radial_backward_gathered(nodes: Tensor, index: Tensor, angular: Tensor, hidd
         _, bwd = _lib.radial_workspace(rconfig, rows, nodes.device)
         workspace = torch.empty(max(bwd, 16), dtype=torch.uint8, device=nodes.device)
         try:
+            if not _fused_gather():
+                raise NotImplementedError
             _lib.radial_backward_gathered(nodes, index, angular, hidden, alpha, bias_c,
                                           grad_output, *args, rconfig, mask, table, workspace)
         except NotImplementedError:
