@@ -291,7 +291,9 @@ __device__ __forceinline__ void store4(float* __restrict__ dst, const float (&v)
   }
 }
 
-template <int MODE, int UT, int NH>
+// GX: the first input is gathered (row e of x is row A.xrow[e] of the source); the
+// kernel is compiled without the per-edge row lookups when it is not.
+template <int MODE, int UT, int NH, bool GX>
 __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArgs A) {
   using Sh = RtShape<UT, NH>;
   constexpr int RT = Sh::RT, TC = Sh::TC, NT = Sh::NT;
@@ -335,17 +337,19 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
   for (int q = tid; q < np * 8; q += NT) coef[q] = __ldg(A.t.coef + q);
   for (int q = tid; q < A.t.n1; q += NT) in1[q] = A.t.in1[q];
   for (int q = tid; q < A.t.n2; q += NT) in2[q] = A.t.in2[q];
-  for (int r = tid; r < RT; r += NT) {
-    const int64_t row = row0 + r;
-    int64_t v = -1;
-    if (row < A.rows) {
-      v = A.xrow != nullptr ? __ldg(A.xrow + row) : row;
-      if (A.xrow != nullptr && (v < 0 || v >= A.xrows)) {
-        atomicExch(&g_ictc_device_error, kBadGatherIndex);
-        v = -1;
+  if constexpr (GX) {
+    for (int r = tid; r < RT; r += NT) {
+      const int64_t row = row0 + r;
+      int64_t v = -1;
+      if (row < A.rows) {
+        v = __ldg(A.xrow + row);
+        if (v < 0 || v >= A.xrows) {
+          atomicExch(&g_ictc_device_error, kBadGatherIndex);
+          v = -1;
+        }
       }
+      xr[r] = v;
     }
-    xr[r] = v;
   }
   for (int idx = tid; idx < RT * A.H; idx += NT) {
     const int r = idx / A.H, h = idx - r * A.H;
@@ -428,7 +432,7 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
 #pragma unroll
       for (int ee = 0; ee < 4; ++ee) {
         const int64_t row = row0 + e0 + ee;
-        const int64_t xrow = xr[e0 + ee];
+        const int64_t xrow = GX ? xr[e0 + ee] : row;
         if (row < A.rows) {
           if (xrow >= 0) {
             const float* xp = (MODE == kRtFwd ? A.opnd : A.x) + xrow * A.W1 + ea.x +
@@ -495,7 +499,7 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
           const int r = e0 + ee;
           const int64_t row = row0 + r;
           const bool row_ok = row < A.rows;
-          const int64_t xrw = xr[r];  // x source row (-1: none)
+          const int64_t xrw = GX ? xr[r] : (row_ok ? row : -1);  // x source row (-1: none)
           const bool x_ok = xrw >= 0;
           const int64_t xoff = (x_ok ? xrw : 0) * A.W1;
           const float y0 = angt[r * W2s + ej.x];
@@ -640,17 +644,23 @@ inline bool radial_tile_fits(int U, int H, int W2, int np, int n1, int n2, bool 
   return radial_tile_smem(radial_ut(U), H, W2, np, n1, n2, dx) <= 225 * 1024;
 }
 
-template <int MODE, int UT, int NH>
-int launch_radial_tile_shape(const RadTileArgs& ra, size_t smem, cudaStream_t s) {
+template <int MODE, int UT, int NH, bool GX>
+int launch_radial_tile_gx(const RadTileArgs& ra, size_t smem, cudaStream_t s) {
   using Sh = RtShape<UT, NH>;
-  const void* fn = reinterpret_cast<const void*>(&radial_tile<MODE, UT, NH>);
+  const void* fn = reinterpret_cast<const void*>(&radial_tile<MODE, UT, NH, GX>);
   const int st = allow_smem(fn, smem);
   if (st != ICTC_OK) return st;
   const dim3 grid(static_cast<unsigned>(ceil_div(ra.rows, Sh::RT)),
                   MODE == kRtDx ? 1u : static_cast<unsigned>(ceil_div(ra.U, UT)));
-  radial_tile<MODE, UT, NH><<<grid, Sh::NT, smem, s>>>(ra);
+  radial_tile<MODE, UT, NH, GX><<<grid, Sh::NT, smem, s>>>(ra);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "radial tile launch");
+}
+
+template <int MODE, int UT, int NH>
+int launch_radial_tile_shape(const RadTileArgs& ra, size_t smem, cudaStream_t s) {
+  return ra.xrow != nullptr ? launch_radial_tile_gx<MODE, UT, NH, true>(ra, smem, s)
+                            : launch_radial_tile_gx<MODE, UT, NH, false>(ra, smem, s);
 }
 
 // Thread tile of the edge tile kernel: "wide" (4 x 4 per thread, 512 threads, the
