@@ -15,7 +15,10 @@ from run to run (no atomics).
 Edge-sharded data parallelism: each rank builds the EdgeIndex of its edge shard
 against the full node set; the per-rank node sums are partial and add up with one
 all-reduce (``ictc_o2_hp_b200.parallel.allreduce_gradients`` or
-``torch.distributed.all_reduce``).
+``torch.distributed.all_reduce``).  With the nodes partitioned over the ranks
+instead, ``parallel.all_gather_rows`` brings every node's features to each rank and
+``parallel.reduce_scatter_rows`` sums the partial node outputs onto their owners;
+autograd turns the all-gather into the reduce-scatter of the node gradients.
 """
 
 from __future__ import annotations

@@ -4,7 +4,10 @@ Every row of a tensor-product batch is independent; the only cross-row quantity 
 the weight gradient (and, for the radial product, the affine-layer gradients).  So
 each rank processes a contiguous shard of the rows with the single-GPU kernels and
 the gradients of the module's parameters are summed with ONE all-reduce of one flat
-buffer over NCCL (NVLink / NVSwitch).  No other exchange happens.
+buffer over NCCL (NVLink / NVSwitch).  No other exchange happens on the product
+path.  For message passing over graphs whose nodes are partitioned over the ranks,
+all_gather_rows / reduce_scatter_rows move node rows (the node-gradient
+reduce-scatter is the adjoint of the node-feature all-gather).
 
 The reference is single-GPU (it has no collective code); this module is the added
 scaling layer.  Host logic is tested with the gloo backend on CPU.
@@ -104,6 +107,113 @@ class RowParallel(torch.nn.Module):
 
     def sync_gradients(self, average: bool = False) -> None:
         allreduce_gradients(self.module.parameters(), self.group, average)
+
+
+# ------------------------------------------------------------ node-partitioned graphs
+#
+# For graphs whose nodes are partitioned over the ranks (rank r owns the contiguous
+# node block shard_bounds(num_nodes, world, r)), a message-passing layer needs every
+# node's features on the rank that holds an edge, and each node's summed messages
+# (and each node's gradient) only on its owner:
+#
+#     h_all = all_gather_rows(h_own, counts)        # backward: node-gradient reduce-scatter
+#     msg = graph.radial_messages(model, h_all, local_edges, angular, hidden)
+#     partial = graph.scatter_sum(msg, local_edges) # this rank's edges' sums, every node
+#     out_own = reduce_scatter_rows(partial, counts)  # backward: all-gather
+#
+# The two collectives are each other's adjoint, so autograd turns the forward
+# all-gather of node features into a reduce-scatter of the node gradients: each rank
+# receives the gradient of the nodes it owns, summed over every rank's edges, instead
+# of an all-reduce of the whole node-gradient table.  Unequal blocks (the remainder on
+# the last ranks) travel padded to the largest block.
+
+
+def node_counts(num_nodes: int, world: int) -> list[int]:
+    """Node-block sizes of the ranks (shard_bounds partition)."""
+    return [b - a for a, b in (shard_bounds(num_nodes, world, r) for r in range(world))]
+
+
+def _check_counts(counts: Sequence[int], group) -> int:
+    world = dist.get_world_size(group)
+    if len(counts) != world or any(int(c) < 0 for c in counts):
+        raise ValueError(f"counts must hold {world} non-negative block sizes")
+    return world
+
+
+def _padded_all_gather(local: torch.Tensor, counts: Sequence[int], group) -> torch.Tensor:
+    world = _check_counts(counts, group)
+    rank = dist.get_rank(group)
+    if local.shape[0] != counts[rank]:
+        raise ValueError(f"rank {rank} holds {local.shape[0]} rows, counts say {counts[rank]}")
+    biggest = max(counts)
+    send = local.contiguous()
+    if local.shape[0] != biggest:
+        send = local.new_zeros((biggest, *local.shape[1:]))
+        send[:local.shape[0]] = local
+    recv = local.new_empty((world * biggest, *local.shape[1:]))
+    dist.all_gather_into_tensor(recv, send, group=group)
+    if all(c == biggest for c in counts):
+        return recv
+    return torch.cat([recv[r * biggest:r * biggest + n] for r, n in enumerate(counts)], dim=0)
+
+
+def _padded_reduce_scatter(full: torch.Tensor, counts: Sequence[int], group) -> torch.Tensor:
+    world = _check_counts(counts, group)
+    rank = dist.get_rank(group)
+    if full.shape[0] != sum(counts):
+        raise ValueError(f"expected {sum(counts)} rows (all blocks), got {full.shape[0]}")
+    biggest = max(counts)
+    if all(c == biggest for c in counts):
+        send = full.contiguous()
+    else:
+        send = full.new_zeros((world * biggest, *full.shape[1:]))
+        start = 0
+        for r, n in enumerate(counts):
+            send[r * biggest:r * biggest + n] = full[start:start + n]
+            start += n
+    recv = full.new_empty((biggest, *full.shape[1:]))
+    dist.reduce_scatter_tensor(recv, send, op=dist.ReduceOp.SUM, group=group)
+    return recv[:counts[rank]]
+
+
+class _AllGatherRows(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, local, counts, group):
+        ctx.counts, ctx.group = counts, group
+        return _padded_all_gather(local, counts, group)
+
+    @staticmethod
+    def backward(ctx, grad_full):
+        return _padded_reduce_scatter(grad_full, ctx.counts, ctx.group), None, None
+
+
+class _ReduceScatterRows(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, full, counts, group):
+        ctx.counts, ctx.group = counts, group
+        return _padded_reduce_scatter(full, counts, group)
+
+    @staticmethod
+    def backward(ctx, grad_local):
+        return _padded_all_gather(grad_local, ctx.counts, ctx.group), None, None
+
+
+def all_gather_rows(local: torch.Tensor, counts: Sequence[int],
+                    group: dist.ProcessGroup | None = None) -> torch.Tensor:
+    """Every rank's row block, concatenated in rank order, on every rank.
+    Differentiable: the gradient is the reduce-scatter of the incoming gradient, so
+    each rank receives the sum over all ranks for the rows it owns."""
+    counts = [int(c) for c in counts]
+    return _AllGatherRows.apply(local, counts, group)
+
+
+def reduce_scatter_rows(full: torch.Tensor, counts: Sequence[int],
+                        group: dist.ProcessGroup | None = None) -> torch.Tensor:
+    """The rows of this rank's block, summed over every rank's `full` (one row per
+    node of all blocks).  Differentiable: the gradient is the all-gather of the
+    owners' gradients."""
+    counts = [int(c) for c in counts]
+    return _ReduceScatterRows.apply(full, counts, group)
 
 
 def gather_rows(local: torch.Tensor, counts: Sequence[int],

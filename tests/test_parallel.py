@@ -13,7 +13,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from ictc_o2_hp_b200.parallel import allreduce_gradients, shard_bounds, shard_rows
+from ictc_o2_hp_b200.parallel import (all_gather_rows, allreduce_gradients, node_counts,
+                                      reduce_scatter_rows, shard_bounds, shard_rows)
 
 
 @pytest.mark.parametrize("rows", [0, 1, 5, 64, 65537])
@@ -115,3 +116,61 @@ def test_missing_rank_ends_collective_with_error(tmp_path):
     status, elapsed = (tmp_path / "rank0.txt").read_text().splitlines()[:2]
     assert status.startswith("error"), status
     assert float(elapsed) < 90
+
+
+def _graph_problem():
+    """A small graph (float64): node features, per-edge factors, a node cotangent."""
+    gen = torch.Generator().manual_seed(7)
+    nodes, edges, width = 11, 40, 5
+    h = torch.randn(nodes, width, dtype=torch.float64, generator=gen)
+    src = torch.randint(0, nodes, (edges,), generator=gen)
+    dst = torch.randint(0, nodes, (edges,), generator=gen)
+    a = torch.randn(edges, width, dtype=torch.float64, generator=gen)
+    cot = torch.randn(nodes, width, dtype=torch.float64, generator=gen)
+    return h, src, dst, a, cot
+
+
+def _layer(h_all, src, dst, a, nodes):
+    """Messages h[src] * a summed into the destinations (index_select / index_add_
+    stand in for the gather and segment-sum kernels on the CPU)."""
+    msg = h_all.index_select(0, src) * a
+    return torch.zeros(nodes, h_all.shape[1], dtype=h_all.dtype).index_add(0, dst, msg)
+
+
+def _node_worker(rank, world, port, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    h, src, dst, a, cot = _graph_problem()
+    counts = node_counts(h.shape[0], world)
+    n0, n1 = shard_bounds(h.shape[0], world, rank)
+    e0, e1 = shard_bounds(src.shape[0], world, rank)
+    h_own = h[n0:n1].clone().requires_grad_(True)
+    h_all = all_gather_rows(h_own, counts)
+    partial = _layer(h_all, src[e0:e1], dst[e0:e1], a[e0:e1], h.shape[0])
+    out_own = reduce_scatter_rows(partial, counts)
+    (out_own * cot[n0:n1]).sum().backward()
+    np.save(os.path.join(result_dir, f"out{rank}.npy"), out_own.detach().numpy())
+    np.save(os.path.join(result_dir, f"dh{rank}.npy"), h_own.grad.numpy())
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_node_partitioned_message_passing(tmp_path, world):
+    """Nodes split over gloo ranks (11 nodes: unequal blocks), edges sharded: the
+    all-gather of node features and the reduce-scatter of the message sums give each
+    rank its own nodes' outputs, and autograd's reduce-scatter of the node gradients
+    gives each rank its own nodes' gradients, equal to the single-process layer."""
+    port = _free_port()
+    mp.spawn(_node_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True)
+    h, src, dst, a, cot = _graph_problem()
+    hh = h.clone().requires_grad_(True)
+    out = _layer(hh, src, dst, a, h.shape[0])
+    (out * cot).sum().backward()
+    for rank in range(world):
+        n0, n1 = shard_bounds(h.shape[0], world, rank)
+        got_out = np.load(tmp_path / f"out{rank}.npy")
+        got_dh = np.load(tmp_path / f"dh{rank}.npy")
+        assert np.abs(got_out - out[n0:n1].detach().numpy()).max() < 1e-12
+        assert np.abs(got_dh - hh.grad[n0:n1].numpy()).max() < 1e-12
