@@ -521,8 +521,17 @@ class RadialMpWorkload(RadialWorkload):
     def __init__(self, args, device, rank, world):
         super().__init__(args, device, rank, world)
         from ictc_o2_hp_b200.graph import EdgeIndex, radial_messages, scatter_sum
+        from ictc_o2_hp_b200 import parallel
         self.radial_messages, self.scatter_sum = radial_messages, scatter_sum
+        self.parallel = parallel
         self.edge_index = EdgeIndex(self.src_shard, self.dst_shard, self.NODES)
+        # --node-partition (N > 1): rank r owns node block r; node features are
+        # all-gathered, node outputs and node gradients reduce-scattered to the owners
+        self.node_partition = bool(getattr(args, "node_partition", False)) and world > 1
+        self.counts = parallel.node_counts(self.NODES, world)
+        n0, n1 = parallel.shard_bounds(self.NODES, world, rank)
+        if self.node_partition:
+            self.nodes = self.nodes[n0:n1].contiguous()
         self.g_nodes = self.torch.ones_like(self.nodes)
         self.launches = 8  # radial kernels + message sum and the node-gradient sum
 
@@ -531,13 +540,18 @@ class RadialMpWorkload(RadialWorkload):
         nodes = (self.nodes if x is None else x).detach().requires_grad_(True)
         ang = (self.angular if y is None else y).detach().requires_grad_(True)
         hidden = self.trunk(self.basis(self.r))
+        table = (self.parallel.all_gather_rows(nodes, self.counts) if self.node_partition
+                 else nodes)
         # the gather by source is folded into the radial kernels (no [E, 896] copy)
-        messages = self.radial_messages(self.model, nodes, self.edge_index, ang, hidden)
+        messages = self.radial_messages(self.model, table, self.edge_index, ang, hidden)
         out = self.scatter_sum(messages, self.edge_index)
+        if self.node_partition:
+            out = self.parallel.reduce_scatter_rows(out, self.counts)
         grads = torch.autograd.grad(out, [nodes, ang] + self.params,
                                     self.g_nodes if g is None else g)
         if self.world > 1:
-            shared = [grads[0]] + list(grads[2:])
+            # node gradients are already reduced onto their owners when partitioned
+            shared = ([] if self.node_partition else [grads[0]]) + list(grads[2:])
             flat = torch.cat([t.reshape(-1) for t in shared])
             torch.distributed.all_reduce(flat)
         return out, grads
@@ -546,7 +560,8 @@ class RadialMpWorkload(RadialWorkload):
         return (self.nodes, self.angular, self.g_nodes)
 
     def collective_numel(self):
-        return self.nodes.numel() + sum(p.numel() for p in self.params)
+        nodes = 0 if self.node_partition else self.nodes.numel()
+        return nodes + sum(p.numel() for p in self.params)
 
     def config(self):
         c = super().config()
@@ -555,8 +570,14 @@ class RadialMpWorkload(RadialWorkload):
                          "x cosine cutoff, MLP 8-64-64 SiLU, fused affine + V=1 uvu C64 m3, "
                          "messages summed into destination nodes in a fixed order; VJP to node "
                          "features, angular and all parameters")
-        c["parallelism"] = (f"edge shards on {self.world} GPU(s), full node set per rank, one "
-                            "NCCL all_reduce of node-feature and parameter gradients")
+        if self.node_partition:
+            c["parallelism"] = (f"edge shards and node blocks on {self.world} GPU(s): node "
+                                "features all-gathered, node outputs and node gradients "
+                                "reduce-scattered to their owners (NCCL), one all_reduce of "
+                                "the parameter gradients")
+        else:
+            c["parallelism"] = (f"edge shards on {self.world} GPU(s), full node set per rank, "
+                                "one NCCL all_reduce of node-feature and parameter gradients")
         return c
 
 
@@ -1122,6 +1143,9 @@ def main(argv=None) -> int:
                         help="rows per host core per CPU-baseline step; 0 = default")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--node-partition", action="store_true",
+                        help="radial_mp with N > 1: node blocks per rank (all-gather of node "
+                             "features, reduce-scatter of node outputs and node gradients)")
     parser.add_argument("--no-radial-scaling", action="store_true",
                         help="tp workload: skip the config-5 strong-scaling companion line")
     args = parser.parse_args(argv)

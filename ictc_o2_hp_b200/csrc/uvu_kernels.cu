@@ -486,6 +486,16 @@ UvuTableH table_of(const UvuConfig& c) {
 // stays near 2e-6, and the chunk partials are summed in a fixed order after.
 constexpr int64_t kDwChunkRows = 1024;
 
+// Whether every second-input entry is read by some path (otherwise its gradient
+// rows are never written by the dy kernels and are cleared first).
+bool entries_all_used(const UvuTableH& t) {
+  std::vector<char> used(t.in2.size(), 0);
+  for (const UvuPathH& p : t.paths) used[p.j] = 1;
+  for (char u : used)
+    if (!u) return false;
+  return true;
+}
+
 int64_t dw_chunks(int device, int64_t rows, int P, int U, int V) {
   const int64_t tiles = static_cast<int64_t>(P) * ((U + 127) / 128) * ((V + 31) / 32);
   int64_t chunks = (2 * sm_count(device) + tiles - 1) / tiles;
@@ -763,6 +773,11 @@ extern "C" int32_t ictc_o2_uvu_backward(const float* left, const float* right, c
   e = cudaGetDevice(&device);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   const int W1 = th.width1, W2 = th.width2;
+  if ((needed & 2) && !entries_all_used(th)) {
+    // second-input entries that no path reads get a zero gradient
+    e = cudaMemsetAsync(grad_right, 0, static_cast<size_t>(rows) * W2 * sizeof(float), s);
+    if (e != cudaSuccess) return cuda_fail(e, "memset");
+  }
   if (!shared) {
     RowStreamArgs ra{left, right, weight, grad_output, grad_left, grad_right, grad_weight, rows,
                      Wn, c.U, c.V, W1, W2, t, needed};

@@ -56,6 +56,9 @@ CASES = [
     (16, 8, 2, "canonical", 2, "full", "component", "none", False, 21),   # streamed per row
     (200, 16, 1, "full", 1, "full", "norm", "none", False, 5),       # two channel chunks
     (96, 64, 2, "full", 1, "canonical", "component", "path", False, 4),  # V = 64
+    (8, 4, 1, "full", 3, "full", "component", "none", True, 50),  # second entries no path reads
+    (8, 4, 1, "full", 3, "full", "component", "none", False, 20),  # the same, per-row weights
+    (128, 32, 3, "full", 3, "full", "component", "none", True, 520),  # two dw row chunks
 ]
 
 
