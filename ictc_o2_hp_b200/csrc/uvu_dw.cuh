@@ -4,12 +4,14 @@
 //   s_p[r,u,b] = sum_{kc,a} c_p[kc][a][b] g_k[r,u,kc] x_i[r,u,a]
 //
 // A CTA (256 threads) owns one path and one chunk of rows.  It walks the rows in
-// steps of 16 (about 95 KB of shared memory, two CTAs per SM): the slices x_i,
-// g_k [16 rows][U d] and y_j [16 rows][V d2] arrive
-// by cp.async one step ahead (double buffer); s is built from shared memory into
-// S[(row, b)][u] and y into Y[(row, b)][v]; then the GEMM over K = (row, b)
-// accumulates dw_p (4 u x 4 v per thread).  Chunks are summed in a fixed order
-// afterwards.  Needs U <= 128, V <= 32 and 16-byte aligned rows.
+// steps of 16 (about 100 KB of shared memory, two CTAs per SM): the slices x_i,
+// g_k [16 rows][U d] and y_j [16 rows][V d2] arrive by cp.async one step ahead
+// (double buffer); s is built from shared memory into S[u][(row, b)] and y into
+// Y[(row, b)][v]; then the GEMM over K = (row, b) accumulates dw_p.  Each thread
+// holds an 8 u x 8 v tile (channels uo + 16 i, v = 8 vo .. 8 vo + 7) over a quarter of
+// each step's 32 (row, b) values; the four quarters are summed in a fixed order at
+// the end.  Chunks are summed in a fixed order afterwards.  Needs U <= 128, V <= 32
+// and 16-byte aligned rows.
 //
 // This header is included inside the anonymous namespace of uvu_kernels.cu.
 #pragma once
@@ -17,8 +19,9 @@
 constexpr int kDwRows = 16;
 constexpr int kDwU = 128;
 constexpr int kDwV = 32;
-constexpr int kDwLdS = kDwU + 4;  // S row stride (floats)
-constexpr int kDwLdY = kDwV + 4;  // Y row stride (floats)
+constexpr int kDwSx = 2 * kDwU + 16;     // slice row stride: conflict-free s generation reads
+constexpr int kDwLdS = 2 * kDwRows + 4;  // S row stride (floats)
+constexpr int kDwLdY = kDwV + 4;         // Y row stride (floats)
 
 struct DwArgs {
   const float* x; const float* y; const float* g; float* dst;  // dst: [chunks][Wn]
@@ -28,19 +31,23 @@ struct DwArgs {
 };
 
 struct DwSmem {
-  float xs[2][kDwRows][kDwU * 2];
-  float gs[2][kDwRows][kDwU * 2];
+  float xs[2][kDwRows][kDwSx];
+  float gs[2][kDwRows][kDwSx];
   float ys[2][kDwRows][kDwV * 2];
-  float S[2 * kDwRows][kDwLdS];
+  float S[kDwU][kDwLdS];
   float Y[2 * kDwRows][kDwLdY];
 };
+// K-quarter sums parked for the final reduction: [quarter 1..3][value][thread], in
+// the x / g slice area once every step is done.
+static_assert(3 * 64 * 64 * sizeof(float) <= 2 * sizeof(float) * 2 * kDwRows * kDwSx,
+              "quarter sums must fit the slice buffers");
 
 inline bool uvu_dw_stage_fits(int U, int V, int W1, int W2, bool aligned_rows) {
   return U <= kDwU && V <= kDwV && U % 4 == 0 && V % 4 == 0 && W1 % 4 == 0 && W2 % 4 == 0 &&
          aligned_rows;
 }
 
-__global__ void __launch_bounds__(256, 1) uvu_dw_stage(DwArgs A) {
+__global__ void __launch_bounds__(256, 2) uvu_dw_stage(DwArgs A) {
   extern __shared__ __align__(16) unsigned char dw_raw[];
   DwSmem& S = *reinterpret_cast<DwSmem*>(dw_raw);
   const int tid = threadIdx.x;
@@ -78,38 +85,39 @@ __global__ void __launch_bounds__(256, 1) uvu_dw_stage(DwArgs A) {
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  for (int q = tid; q < 2 * kDwRows * kDwU * 2; q += 256) {
+  for (int q = tid; q < 2 * kDwRows * kDwSx; q += 256) {
     (&S.xs[0][0][0])[q] = 0.f;
     (&S.gs[0][0][0])[q] = 0.f;
   }
   for (int q = tid; q < 2 * kDwRows * kDwV * 2; q += 256) (&S.ys[0][0][0])[q] = 0.f;
   __syncthreads();
   issue(0, 0);
-  // generation: channel gu, rows gh * kDwRows / 2 .. +kDwRows / 2 - 1; y: (row, b) gr, v quad gv
-  const int gu = tid & 127, gh = tid >> 7;
-  // GEMM: u quad uq (0..31), v quad vq (0..7)
-  const int uq = tid >> 3, vq = tid & 7;
-  float2 acc[4][2];  // paired along v
+  // generation: channel 8 (warp + 8 (k & 1)) + lane % 8, row 4 (k / 2) + lane / 8 (a
+  // half warp stores 8 channels x 2 rows: conflict-free float2 stores)
+  const int lane = tid & 31, warp = tid >> 5;
+  // GEMM: K quarter kq, channels uo + 16 i, v octet vo (v = 8 vo .. 8 vo + 7)
+  const int kq = tid >> 6, uo = (tid & 63) >> 2, vo = tid & 3;
+  float2 acc[8][4];  // [channel][v pair]
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+  for (int a = 0; a < 8; ++a)
 #pragma unroll
-    for (int b = 0; b < 2; ++b) acc[a][b] = make_float2(0.f, 0.f);
+    for (int b = 0; b < 4; ++b) acc[a][b] = make_float2(0.f, 0.f);
   for (int64_t step = 0; step < nsteps; ++step) {
     const int buf = static_cast<int>(step & 1);
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();  // slices of step visible; previous GEMM done with S and Y
     issue(step + 1, buf ^ 1);
-#pragma unroll 4
-    for (int rr = 0; rr < kDwRows / 2; ++rr) {
-      const int r = gh * (kDwRows / 2) + rr;
-      const float2 xv = dy_slot(&S.xs[buf][r][gu * ei.y], ei.y);
-      const float2 gv = dy_slot(&S.gs[buf][r][gu * ek.y], ek.y);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int u = 8 * (warp + 8 * (k & 1)) + (lane & 7);
+      const int r = 4 * (k >> 1) + (lane >> 3);
+      const float2 xv = dy_slot(&S.xs[buf][r][u * ei.y], ei.y);
+      const float2 gv = dy_slot(&S.gs[buf][r][u * ek.y], ek.y);
       // (s0, s1) = g0 (c0 x0 + c1 x1) + g1 (c2 x0 + c3 x1), both b at once (f32x2)
       const float2 t0 = fma2(xv.y, c1, __fmul2_rn(make_float2(xv.x, xv.x), c0));
       const float2 t1 = fma2(xv.y, c3, __fmul2_rn(make_float2(xv.x, xv.x), c2));
-      const float2 sv = fma2(gv.y, t1, __fmul2_rn(make_float2(gv.x, gv.x), t0));
-      S.S[2 * r][gu] = sv.x;
-      S.S[2 * r + 1][gu] = sv.y;
+      *reinterpret_cast<float2*>(&S.S[u][2 * r]) =
+          fma2(gv.y, t1, __fmul2_rn(make_float2(gv.x, gv.x), t0));
     }
     // Y[(r, b)][v] = y_j[r, v, b] (zero for b >= d2)
     for (int q = tid; q < 2 * kDwRows * kDwV; q += 256) {
@@ -118,28 +126,65 @@ __global__ void __launch_bounds__(256, 1) uvu_dw_stage(DwArgs A) {
       S.Y[rb][v] = (b < ej.y && v < A.V) ? S.ys[buf][r][v * ej.y + b] : 0.f;
     }
     __syncthreads();
-#pragma unroll 8
-    for (int k = 0; k < 2 * kDwRows; ++k) {
-      const float4 a4 = *reinterpret_cast<const float4*>(&S.S[k][uq * 4]);
-      const float4 b4 = *reinterpret_cast<const float4*>(&S.Y[k][vq * 4]);
-      const float av[4] = {a4.x, a4.y, a4.z, a4.w};
-      const float2 bv[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
+    // this quarter's 8 (row, b) values, two at a time
+#pragma unroll 1
+    for (int k0 = 8 * kq; k0 < 8 * kq + 8; k0 += 2) {
+      float2 sa[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < 8; ++i) sa[i] = *reinterpret_cast<const float2*>(&S.S[uo + 16 * i][k0]);
+      float4 yb[2][2];
 #pragma unroll
-        for (int j = 0; j < 2; ++j) acc[i][j] = fma2(av[i], bv[j], acc[i][j]);
+      for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          yb[kk][h] = *reinterpret_cast<const float4*>(&S.Y[k0 + kk][8 * vo + 4 * h]);
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        const float2 bv[4] = {make_float2(yb[kk][0].x, yb[kk][0].y),
+                              make_float2(yb[kk][0].z, yb[kk][0].w),
+                              make_float2(yb[kk][1].x, yb[kk][1].y),
+                              make_float2(yb[kk][1].z, yb[kk][1].w)};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float a = kk == 0 ? sa[i].x : sa[i].y;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fma2(a, bv[j], acc[i][j]);
+        }
+      }
     }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
-  float* out = A.dst + static_cast<int64_t>(blockIdx.y) * A.Wn + static_cast<int64_t>(p) * A.U * A.V;
+  // sum the K quarters in order: quarters 1..3 park their tiles, quarter 0 adds them
+  __syncthreads();  // every thread is done with the slice buffers
+  float* red = &S.xs[0][0][0];  // [3][64 values][64 threads]
+  const int t64 = tid & 63;
+  if (kq > 0) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int u = uq * 4 + i;
-    if (u >= A.U) continue;
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int v = vq * 4 + j;
-      if (v < A.V) out[static_cast<int64_t>(u) * A.V + v] = pair_at(acc[i], j);
+      for (int j = 0; j < 8; ++j) red[((kq - 1) * 64 + i * 8 + j) * 64 + t64] = pair_at(acc[i], j);
+  }
+  __syncthreads();
+  if (kq == 0) {
+    float* out =
+        A.dst + static_cast<int64_t>(blockIdx.y) * A.Wn + static_cast<int64_t>(p) * A.U * A.V;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int u = uo + 16 * i;
+      float sum[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        sum[j] = pair_at(acc[i], j);
+#pragma unroll
+        for (int q = 0; q < 3; ++q) sum[j] += red[(q * 64 + i * 8 + j) * 64 + t64];
+      }
+      if (u < A.U) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int v = 8 * vo + j;
+          if (v < A.V) out[static_cast<int64_t>(u) * A.V + v] = sum[j];
+        }
+      }
     }
   }
 }

@@ -6,10 +6,10 @@
 // A CTA (256 threads) owns 16 rows and walks the paths grouped by second entry
 // j.  For each path the slices x_i[16 rows][U d1], g_k[16 rows][U d3] and the
 // weights w_p[U][V] arrive by cp.async one path ahead; s_p is built from shared
-// memory into S[u][(row, b)] and then contracted over u (GEMM: 4 (row, b) x 4 v
-// per thread, the u range split in four quarters that are summed in a fixed
-// order when the j group ends).  Needs U <= 128, V <= 32 and
-// 16-byte aligned rows; other shapes use uvu_dy_tile.
+// memory into S[u][(row, b)] and then contracted over u (GEMM: an 8 (row, b) x 4 v
+// tile per thread; warp w takes the channels u = w + 8 i; the eight warps' sums are
+// added in a fixed order, a three-round tree, when the j group ends).  Needs U <= 128, V <= 32 and 16-byte aligned rows; other shapes use
+// uvu_dy_tile.
 //
 // This header is included inside the anonymous namespace of uvu_kernels.cu.
 #pragma once
@@ -18,7 +18,8 @@ constexpr int kDyRows = 16;
 constexpr int kDyU = 128;
 constexpr int kDyV = 32;
 constexpr int kDyLd = 2 * kDyRows + 4;  // S row stride (floats): 32 (row, b) + pad
-constexpr int kDyKs = 4;                // u range split over thread quarters
+constexpr int kDyLdW = kDyV + 4;        // weight row stride (floats)
+constexpr int kDySx = 2 * kDyU + 16;    // slice row stride: conflict-free s generation reads
 
 struct DyArgs {
   const float* x; const float* g; const float* w; float* dy;
@@ -27,14 +28,15 @@ struct DyArgs {
   UvuDev t;
 };
 
-// About 82 KB: two CTAs per SM.  x / g slices are single-buffered (the next path's
+// About 102 KB: two CTAs per SM.  x / g slices are single-buffered (the next path's
 // slices are copied while this path's GEMM runs, after S has been built from
 // them); the weights are double-buffered.
 struct DySmem {
-  float xs[kDyRows][kDyU * 2];
-  float gs[kDyRows][kDyU * 2];
-  float wp[2][kDyU][kDyV];
+  float xs[kDyRows][kDySx];
+  float gs[kDyRows][kDySx];
+  float wp[2][kDyU][kDyLdW];
   float S[kDyU][kDyLd];
+  float red[4][32][32];  // warp-sum tree: [warp][value][lane]
 };
 
 inline bool uvu_dy_stage_fits(int U, int V, int W1, bool aligned_rows) {
@@ -99,23 +101,23 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
     }
   };
   // zero the parts of the buffers that copies do not cover (channels >= U, v >= V)
-  for (int q = tid; q < kDyRows * kDyU * 2; q += 256) {
+  for (int q = tid; q < kDyRows * kDySx; q += 256) {
     (&S.xs[0][0])[q] = 0.f;
     (&S.gs[0][0])[q] = 0.f;
   }
-  for (int q = tid; q < 2 * kDyU * kDyV; q += 256) (&S.wp[0][0][0])[q] = 0.f;
+  for (int q = tid; q < 2 * kDyU * kDyLdW; q += 256) (&S.wp[0][0][0])[q] = 0.f;
   __syncthreads();
   issue_xg(0);
   issue_w(0, 0);
   asm volatile("cp.async.commit_group;" ::: "memory");
-  // generation: channel gu, rows gh * 8 .. +7
-  const int gu = tid & 127, gh = tid >> 7;
-  // GEMM: (row, b) quad rq (0..7), v quad vq (0..7), u quarter ug (0..3)
-  const int ug = tid >> 6, rq = (tid & 63) >> 3, vq = tid & 7;
-  constexpr int kUq = kDyU / kDyKs;
-  float2 acc[4][2];  // paired along v
+  // generation: channel 8 (warp + 8 (k & 1)) + lane % 8, row 4 (k / 2) + lane / 8 (a
+  // half warp stores 8 channels x 2 rows: conflict-free float2 stores)
+  const int lane = tid & 31, warp = tid >> 5;
+  // GEMM: channels u = warp + 8 i, (row, b) octet ro, v quad vq
+  const int ro = lane >> 3, vq = lane & 7;
+  float2 acc[8][2];  // [(row, b)][v pair]
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+  for (int a = 0; a < 8; ++a)
 #pragma unroll
     for (int b = 0; b < 2; ++b) acc[a][b] = make_float2(0.f, 0.f);
   for (int pos = 0; pos < np; ++pos) {
@@ -129,69 +131,77 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
     const float2* cp = reinterpret_cast<const float2*>(A.t.coef + 8 * p);
     const float2 c0 = __ldg(cp), c1 = __ldg(cp + 1), c2 = __ldg(cp + 2), c3 = __ldg(cp + 3);
     // (s0, s1) = g0 (c0 x0 + c1 x1) + g1 (c2 x0 + c3 x1), both b at once (f32x2)
-#pragma unroll 4
-    for (int rr = 0; rr < kDyRows / 2; ++rr) {
-      const int r = gh * (kDyRows / 2) + rr;
-      const float2 xv = dy_slot(&S.xs[r][gu * ei.y], ei.y);
-      const float2 gv = dy_slot(&S.gs[r][gu * ek.y], ek.y);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int u = 8 * (warp + 8 * (k & 1)) + (lane & 7);
+      const int r = 4 * (k >> 1) + (lane >> 3);
+      const float2 xv = dy_slot(&S.xs[r][u * ei.y], ei.y);
+      const float2 gv = dy_slot(&S.gs[r][u * ek.y], ek.y);
       const float2 t0 = fma2(xv.y, c1, __fmul2_rn(make_float2(xv.x, xv.x), c0));
       const float2 t1 = fma2(xv.y, c3, __fmul2_rn(make_float2(xv.x, xv.x), c2));
-      *reinterpret_cast<float2*>(&S.S[gu][2 * r]) =
+      *reinterpret_cast<float2*>(&S.S[u][2 * r]) =
           fma2(gv.y, t1, __fmul2_rn(make_float2(gv.x, gv.x), t0));
     }
     __syncthreads();  // S built; x / g free for the next path
     issue_xg(pos + 1);
     issue_w(pos + 1, buf ^ 1);
     asm volatile("cp.async.commit_group;" ::: "memory");
-    // dy[(r,b)][v] += sum_u S[u][(r,b)] w[u][v] over this thread's channel quarter
-    const int ubeg = ug * kUq;
-#pragma unroll 8
-    for (int uu = 0; uu < kUq; ++uu) {
-      const int u = ubeg + uu;
-      const float4 a4 = *reinterpret_cast<const float4*>(&S.S[u][rq * 4]);
-      const float4 b4 = *reinterpret_cast<const float4*>(&S.wp[buf][u][vq * 4]);
-      const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+    // dy[(r,b)][v] += sum_u S[u][(r,b)] w[u][v] over this warp's channels
+#pragma unroll 4
+    for (int i = 0; i < kDyU / 8; ++i) {
+      const int u = warp + 8 * i;
+      const float4 a0 = *reinterpret_cast<const float4*>(&S.S[u][8 * ro]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&S.S[u][8 * ro + 4]);
+      const float4 b4 = *reinterpret_cast<const float4*>(&S.wp[buf][u][4 * vq]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
       const float2 bv[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int m = 0; m < 8; ++m)
 #pragma unroll
-        for (int k = 0; k < 2; ++k) acc[i][k] = fma2(av[i], bv[k], acc[i][k]);
+        for (int k = 0; k < 2; ++k) acc[m][k] = fma2(av[m], bv[k], acc[m][k]);
     }
     const bool last = pos + 1 == np || A.t.paths[A.t.by_j[pos + 1]].y != pt.y;
     if (last) {
-      // sum the channel quarters in order: quarters 1..3 park their sums, 0 adds
-      __syncthreads();  // every thread is done reading S
-      float* red = &S.S[0][0];  // [3 quarters][64 threads][17]: odd stride, no bank conflicts
-      if (ug > 0) {
+      // sum the eight warps in a fixed order: w + 4, w + 2, w + 1 into w
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+      for (int half = 4; half >= 1; half >>= 1) {
+        if (warp >= half && warp < 2 * half) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            red[((ug - 1) * 64 + (tid & 63)) * 17 + i * 4 + k] = pair_at(acc[i], k);
+          for (int m = 0; m < 8; ++m)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) S.red[warp - half][m * 4 + k][lane] = pair_at(acc[m], k);
+        }
+        __syncthreads();
+        if (warp < half) {
+#pragma unroll
+          for (int m = 0; m < 8; ++m)
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              acc[m][k].x += S.red[warp][m * 4 + 2 * k][lane];
+              acc[m][k].y += S.red[warp][m * 4 + 2 * k + 1][lane];
+            }
+        }
+        __syncthreads();
       }
-      __syncthreads();
-      if (ug == 0) {
-        // (r, b) = rq*4 + i: rows rq*2 + i/2, component i%2
+      if (warp == 0) {
+        // (r, b) = 8 ro + m: row 4 ro + m / 2, component m % 2; v = 4 vq + k
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = rq * 2 + (i >> 1), b = i & 1;
+        for (int m = 0; m < 8; ++m) {
+          const int r = 4 * ro + (m >> 1), b = m & 1;
           const int64_t row = row0 + r;
           if (row < A.rows && b < ej.y) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              const int v = vq * 4 + k;
-              float sum = pair_at(acc[i], k);
-#pragma unroll
-              for (int q = 0; q < kDyKs - 1; ++q) sum += red[(q * 64 + tid) * 17 + i * 4 + k];
-              if (v < A.V) A.dy[row * A.W2 + ej.x + v * ej.y + b] = sum;
+              const int v = 4 * vq + k;
+              if (v < A.V) A.dy[row * A.W2 + ej.x + v * ej.y + b] = pair_at(acc[m], k);
             }
           }
         }
       }
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int m = 0; m < 8; ++m)
 #pragma unroll
-        for (int k = 0; k < 2; ++k) acc[i][k] = make_float2(0.f, 0.f);
+        for (int k = 0; k < 2; ++k) acc[m][k] = make_float2(0.f, 0.f);
     }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");
