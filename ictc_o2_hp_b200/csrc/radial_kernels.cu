@@ -14,6 +14,7 @@
 //     a path-tiled reduction over edges (fixed row chunks, fixed-order sum).
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 
@@ -236,14 +237,17 @@ constexpr int kBadGatherIndex = 17;
 // edges per CTA.
 template <int UT, int NH = 2>
 struct RtShape {
-  static constexpr int NT = NH == 2 ? 256 : 512;  // threads per CTA
-  static constexpr int TC = UT / (4 * NH);        // threads along the channels
-  static constexpr int TR = NT / TC;              // thread rows
-  static constexpr int RT = TR * 4;               // edges per CTA
+  static constexpr int NC = NH == 2 ? 2 : 1;                  // channel groups per thread
+  static constexpr int NT = NH == 2 ? 256 : (NH == 1 ? 512 : 384);  // threads per CTA
+  static constexpr int TC = UT / (4 * NC);                    // threads along the channels
+  static constexpr int TR = NT / TC;                          // thread rows
+  static constexpr int RT = TR * 4;                           // edges per CTA
 };
 
-inline size_t radial_tile_smem(int ut, int H, int W2, int np, int n1, int n2, bool dx) {
-  const size_t rt = static_cast<size_t>(kRtThreads / (ut / 8)) * 4;
+inline size_t radial_tile_smem(int ut, int H, int W2, int np, int n1, int n2, bool dx,
+                               int rt_edges = 0) {
+  const size_t rt = rt_edges > 0 ? static_cast<size_t>(rt_edges)
+                                 : static_cast<size_t>(kRtThreads / (ut / 8)) * 4;
   const size_t kc = static_cast<size_t>(H < kRtKC ? H : kRtKC);
   const size_t w2s = static_cast<size_t>(odd_stride(W2));
   const size_t floats = static_cast<size_t>(H) * rt + kRtStages * kc * ut + rt * w2s +
@@ -296,8 +300,8 @@ __device__ __forceinline__ void store4(float* __restrict__ dst, const float (&v)
 template <int MODE, int UT, int NH, bool GX>
 __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArgs A) {
   using Sh = RtShape<UT, NH>;
-  constexpr int RT = Sh::RT, TC = Sh::TC, NT = Sh::NT;
-  constexpr int CW = 4 * NH;  // channels per thread
+  constexpr int RT = Sh::RT, TC = Sh::TC, NT = Sh::NT, NC = Sh::NC;
+  constexpr int CW = 4 * NC;  // channels per thread
   extern __shared__ __align__(128) unsigned char rt_raw[];
   // [0, 128): stage barriers (full) and release counters
   uint64_t* full = reinterpret_cast<uint64_t*>(rt_raw);
@@ -454,8 +458,8 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
       const float av[4] = {a4.x, a4.y, a4.z, a4.w};
       float2 bv[CW / 2];
 #pragma unroll
-      for (int h = 0; h < NH; ++h) {
-        const float4 b4 = *reinterpret_cast<const float4*>(Wb + k * UT + h * (UT / NH) + tc * 4);
+      for (int h = 0; h < NC; ++h) {
+        const float4 b4 = *reinterpret_cast<const float4*>(Wb + k * UT + h * (UT / NC) + tc * 4);
         bv[2 * h] = make_float2(b4.x, b4.y);
         bv[2 * h + 1] = make_float2(b4.z, b4.w);
       }
@@ -509,8 +513,8 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
           const float c10 = fmaf(c[4], y0, c[5] * y1), c11 = fmaf(c[6], y0, c[7] * y1);
           float2 dyp = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int half = 0; half < NH; ++half) {
-            const int u = ub + half * (UT / NH) + tc * 4;
+          for (int half = 0; half < NC; ++half) {
+            const int u = ub + half * (UT / NC) + tc * 4;
             if (MODE == kRtFwd) {
               float xv[4 * D1];
               load4<D1>(xv, A.opnd + xoff + ei.x + static_cast<int64_t>(u) * D1, x_ok, u, A.U,
@@ -606,8 +610,8 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
           const int64_t row = row0 + e0 + ee;
           const bool row_ok = row < A.rows;
 #pragma unroll
-          for (int half = 0; half < NH; ++half) {
-            const int u = ub + half * (UT / NH) + tc * 4;
+          for (int half = 0; half < NC; ++half) {
+            const int u = ub + half * (UT / NC) + tc * 4;
             float v[4][2];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -663,12 +667,49 @@ int launch_radial_tile_shape(const RadTileArgs& ra, size_t smem, cudaStream_t s)
                             : launch_radial_tile_gx<MODE, UT, NH, false>(ra, smem, s);
 }
 
-// Thread tile of the edge tile kernel: "wide" (4 x 4 per thread, 512 threads, the
-// default: forward -9 %, dx/dy -6 % at the config-5 shapes) or, with
-// ICTC_RADIAL_TILE=split, the 4 x 8 tile on 256 threads; tests cover both.
-inline bool radial_tile_wide() {
+// Thread tile of the edge tile kernel, all 4 edges x 4 channels per thread except
+// "split": "wide" = 512 threads (128 registers, 16 warps per SM: the forward's shape),
+// "mid" = 384 threads (up to 170 registers, 12 warps per SM), "split" = 4 x 8 on 256
+// threads.  Both wide and mid run one CTA per SM.  At 512 threads the dx tile spills;
+// the mid tile took it 32.7 -> 31.0 ms at config 5 (1,048,576 edges), but its smaller
+// edge tile leaves a fuller last wave at some sizes (C64 m6 at 131,072 edges: 9.2 waves
+// of mid CTAs, 13.9 vs 14.3 ms for wide), so the dx tile takes mid when its speed
+// (about 5 %) outweighs the difference in last-wave fill.  ICTC_RADIAL_TILE=
+// wide|mid|split forces one shape for both modes (tests cover each).
+enum RtTile { kTileWide = 1, kTileSplit = 2, kTileMid = 3 };
+
+template <int UT>
+inline int radial_tile_shape(int mode, int64_t rows) {
   const char* v = getenv("ICTC_RADIAL_TILE");
-  return v == nullptr || strcmp(v, "split") != 0;
+  if (v != nullptr) {
+    if (strcmp(v, "split") == 0) return kTileSplit;
+    if (strcmp(v, "mid") == 0) return kTileMid;
+    if (strcmp(v, "wide") == 0) return kTileWide;
+  }
+  if (mode != kRtDx) return kTileWide;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return kTileWide;
+  const double sms = sm_count(device);
+  auto fill = [&](int rt) {  // busy fraction of the SM-waves the launch occupies
+    const double ctas = static_cast<double>((rows + rt - 1) / rt);
+    return ctas / (sms * std::ceil(ctas / sms));
+  };
+  return fill(RtShape<UT, 3>::RT) * 1.05 >= fill(RtShape<UT, 1>::RT) ? kTileMid : kTileWide;
+}
+
+template <int MODE, int UT>
+int launch_radial_tile_ut(const RadTileArgs& ra, cudaStream_t s) {
+  auto smem = [&](int rt) {
+    return radial_tile_smem(UT, ra.H, ra.W2, ra.t.np, ra.t.n1, ra.t.n2, MODE == kRtDx, rt);
+  };
+  switch (radial_tile_shape<UT>(MODE, ra.rows)) {
+    case kTileSplit:
+      return launch_radial_tile_shape<MODE, UT, 2>(ra, smem(RtShape<UT, 2>::RT), s);
+    case kTileMid:
+      return launch_radial_tile_shape<MODE, UT, 3>(ra, smem(RtShape<UT, 3>::RT), s);
+    default:
+      return launch_radial_tile_shape<MODE, UT, 1>(ra, smem(RtShape<UT, 1>::RT), s);
+  }
 }
 
 template <int MODE>
@@ -676,12 +717,7 @@ int launch_radial_tile(const RadTileArgs& ra, cudaStream_t s) {
   const int ut = radial_ut(ra.U);
   const size_t smem = radial_tile_smem(ut, ra.H, ra.W2, ra.t.np, ra.t.n1, ra.t.n2, MODE == kRtDx);
   if (smem > 225 * 1024) return ICTC_ERR_UNSUPPORTED;  // caller falls back to the row tile
-  const bool wide = radial_tile_wide();
-  if (ut == 64)
-    return wide ? launch_radial_tile_shape<MODE, 64, 1>(ra, smem, s)
-                : launch_radial_tile_shape<MODE, 64, 2>(ra, smem, s);
-  return wide ? launch_radial_tile_shape<MODE, 128, 1>(ra, smem, s)
-              : launch_radial_tile_shape<MODE, 128, 2>(ra, smem, s);
+  return ut == 64 ? launch_radial_tile_ut<MODE, 64>(ra, s) : launch_radial_tile_ut<MODE, 128>(ra, s);
 }
 
 // ------------------------------------------------------------ dhidden

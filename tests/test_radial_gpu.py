@@ -87,14 +87,16 @@ def test_against_oracle(u, m_max, hidden, bias, rows, cuda_device):
         assert err <= TOL, f"{key}: {err:.3e}"
 
 
+@pytest.mark.parametrize("shape", ["split", "wide", "mid"])
 @pytest.mark.parametrize("u,m_max,hidden,bias,rows", [
-    (64, 3, 64, True, 300),    # channel tile of 64 (4 x 8 tile: 256 threads)
+    (64, 3, 64, True, 300),    # channel tile of 64
     (160, 2, 24, True, 70),    # channel tiles of 128, the last partial
 ])
-def test_split_thread_tile(u, m_max, hidden, bias, rows, cuda_device, monkeypatch):
-    """The 4 x 8 per-thread tile (ICTC_RADIAL_TILE=split) against the oracle; the
-    default 4 x 4 tile runs every other case."""
-    monkeypatch.setenv("ICTC_RADIAL_TILE", "split")
+def test_thread_tile_shapes(shape, u, m_max, hidden, bias, rows, cuda_device, monkeypatch):
+    """Every edge-tile shape for both the forward and the dx tile
+    (ICTC_RADIAL_TILE=split: 4 x 8 on 256 threads, wide: 4 x 4 on 512, mid: 4 x 4 on 384)
+    against the oracle; the defaults (wide forward, mid dx tile) run every other case."""
+    monkeypatch.setenv("ICTC_RADIAL_TILE", shape)
     test_against_oracle(u, m_max, hidden, bias, rows, cuda_device)
 
 
