@@ -1087,18 +1087,24 @@ struct StagedPlan {
   size_t smem;
 };
 
+// ctas_per_sm > 1: the stage ring shares the SM's shared memory with that many CTAs
+// (the caller checks that their registers fit), and the grid has that many per SM.
 StagedPlan plan_staged(int device, int64_t rows, const TpLayout& L, bool full, int tensors,
                        size_t weight_bytes, int max_warps = kStagedWarps, int max_stages = kMaxStages,
-                       bool weights_required = false) {
+                       bool weights_required = false, int ctas_per_sm = 1) {
   StagedPlan p{};
+  // per-SM shared memory of sm_100 (228 KB) less the 1 KB each CTA reserves, and a margin
+  const size_t budget =
+      ctas_per_sm > 1 ? (228 * 1024) / static_cast<size_t>(ctas_per_sm) - 2 * 1024
+                      : kStagedSmemBudget;
   p.groups = static_cast<int>(ceil_div(L.C, full ? 16 : 32));
   if (p.groups > max_warps || L.width % 4 != 0 || rows == 0) return p;
   p.R = max_warps / p.groups;
   p.warps = p.R * p.groups;
   const size_t stage_bytes = static_cast<size_t>(tensors) * p.R * L.width * sizeof(float);
-  if (weight_bytes > 0 && kStagedSmemBudget > kBarrierBytes + weight_bytes) {
+  if (weight_bytes > 0 && budget > kBarrierBytes + weight_bytes) {
     const int fit =
-        static_cast<int>((kStagedSmemBudget - kBarrierBytes - weight_bytes) / stage_bytes);
+        static_cast<int>((budget - kBarrierBytes - weight_bytes) / stage_bytes);
     if (fit >= (weights_required ? 2 : 3)) {
       p.weights_in_smem = true;
       p.stages = fit < max_stages ? fit : max_stages;
@@ -1107,13 +1113,13 @@ StagedPlan plan_staged(int device, int64_t rows, const TpLayout& L, bool full, i
   }
   if (!p.weights_in_smem) {
     if (weights_required) return p;
-    const int fit = static_cast<int>((kStagedSmemBudget - kBarrierBytes) / stage_bytes);
+    const int fit = static_cast<int>((budget - kBarrierBytes) / stage_bytes);
     p.stages = fit < kMaxStages ? fit : kMaxStages;
     if (p.stages < 2) return p;
     p.smem = kBarrierBytes + static_cast<size_t>(p.stages) * stage_bytes;
   }
   const int64_t nblocks = ceil_div(rows, p.R);
-  p.grid = sm_count(device);
+  p.grid = static_cast<int64_t>(sm_count(device)) * ctas_per_sm;
   if (p.grid > nblocks) p.grid = nblocks;
   p.ok = true;
   return p;
@@ -1185,17 +1191,85 @@ bool aligned16(std::initializer_list<const void*> ptrs) {
   return true;
 }
 
+// Two staged backward CTAs per SM where registers allow (default);
+// ICTC_TP_BACKWARD_PAIRS=0 keeps one (tests cover both).
+bool staged_pairs_enabled() {
+  const char* v = getenv("ICTC_TP_BACKWARD_PAIRS");
+  return v == nullptr || strcmp(v, "0") != 0;
+}
+
 // Backward workspace: [per-thread float4 weight chunks][slots x numel partials].
 size_t weight_chunk_bytes(const Kernels& k, int C, bool full) {
   const int64_t T = ceil_div(C, full ? 16 : 32) * 32;
   return static_cast<size_t>(k.chunks) * static_cast<size_t>(T) * sizeof(float4);
 }
 
+// CTAs of `warps` warps of kernel fn whose registers fit one SM together (at most 2).
+int ctas_by_registers(const void* fn, int warps) {
+  static std::mutex mu;
+  static const void* seen[64] = {};
+  static int regs_of[64] = {};
+  int regs = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    int slot = -1;
+    for (int i = 0; i < 64; ++i) {
+      if (seen[i] == fn) {
+        regs = regs_of[i];
+        break;
+      }
+      if (seen[i] == nullptr) {
+        slot = i;
+        break;
+      }
+    }
+    if (regs == 0) {
+      cudaFuncAttributes a{};
+      if (cudaFuncGetAttributes(&a, fn) != cudaSuccess) {
+        cudaGetLastError();
+        return 1;
+      }
+      regs = a.numRegs;
+      if (slot >= 0) {
+        seen[slot] = fn;
+        regs_of[slot] = regs;
+      }
+    }
+  }
+  const int per_cta = ((regs + 7) / 8) * 8 * warps * 32;  // allocation in 8-register steps
+  const int n = per_cta > 0 ? 65536 / per_cta : 1;
+  return n < 1 ? 1 : (n > 2 ? 2 : n);
+}
+
+// Plan of the staged backward: where the kernel's registers let two CTAs share an SM
+// (small orders: m_max <= 2 full, <= 3 canonical, m_max 3 full at C = 96), each gets half
+// the shared memory for its stage ring and the grid doubles, so twice the warps hide the
+// per-row latencies of those short rows.  Measured over the benchmark sweep (backward
+// time, one CTA per SM / two): full parity 1.13-1.63x at every such shape; canonical
+// 1.03-1.34x where the single CTA has fewer than 8 warps (C = 96) or m_max = 1 at
+// C >= 64, but 0.79-0.92x at m_max 2-3 otherwise (their single CTA already reaches
+// 0.8-0.98 of HBM at 65,536 rows) and 0.84x at C = 32, m_max 1; those keep one CTA.
+StagedPlan plan_staged_backward(int device, const Kernels& k, int64_t rows, const TpLayout& L,
+                                bool full) {
+  const size_t wb = weight_chunk_bytes(k, L.C, full);
+  const StagedPlan p = plan_staged(device, rows, L, full, 3, wb);
+  if (!p.ok || !staged_pairs_enabled()) return p;
+  const int m_max = static_cast<int>((L.width - L.fbase) / L.fstride);
+  if (!full && p.warps >= kStagedWarps && !(m_max == 1 && L.C >= 64)) return p;
+  const int ctas = ctas_by_registers(reinterpret_cast<const void*>(k.bwd_staged), p.warps);
+  if (ctas > 1) {
+    const StagedPlan q =
+        plan_staged(device, rows, L, full, 3, wb, kStagedWarps, kMaxStages, false, ctas);
+    if (q.ok) return q;
+  }
+  return p;
+}
+
 int64_t backward_slots(int device, const Kernels& k, int64_t rows, const TpLayout& L, bool full,
                        int* status) {
   DirectPlan d{};
   *status = plan_direct(reinterpret_cast<const void*>(k.bwd_direct), device, rows, L.C, full, &d);
-  const StagedPlan s = plan_staged(device, rows, L, full, 3, weight_chunk_bytes(k, L.C, full));
+  const StagedPlan s = plan_staged_backward(device, k, rows, L, full);
   int64_t slots = d.slots;
   if (s.ok && s.grid * s.R > slots) slots = s.grid * s.R;
   const TiledPlan t = plan_tiled(device, rows, L, full, k.chunks);
@@ -1432,7 +1506,7 @@ int32_t tp_backward_impl(const float* left, const float* right, const float* wei
       tiled = encode_row_tile_maps(ops[t], rows, channels, m_max, full, L.cm != 0, L.width,
                                    tp.Ct, &maps.m[2 * t]) == 0;
   }
-  const StagedPlan sp = tiled ? StagedPlan{} : plan_staged(device, rows, L, full, 3, wbytes);
+  const StagedPlan sp = tiled ? StagedPlan{} : plan_staged_backward(device, k, rows, L, full);
   const bool staged = !tiled && sp.ok && al16;
   DirectPlan dp{};
   if (!staged && !tiled) {

@@ -360,3 +360,28 @@ def test_tiled_backward_matches_untiled(channels, m_max, parity, rows, cuda_devi
     plain = torch.ops.ictc_o2_b200.tp_backward(x, y, w, g, *args)
     assert torch.equal(tiled[0], plain[0]) and torch.equal(tiled[1], plain[1])
     assert O.max_error(tiled[2].cpu().numpy(), plain[2].cpu().numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("channels,m_max,parity,rows", [
+    (128, 2, "full", 4000),
+    (96, 3, "full", 3001),
+    (96, 2, "canonical", 5000),
+    (64, 1, "canonical", 777),
+])
+def test_paired_staged_backward_matches_single(channels, m_max, parity, rows, cuda_device,
+                                               monkeypatch):
+    """Small orders run two staged-backward CTAs per SM (registers permitting, half the
+    stage ring each); against one CTA per SM (ICTC_TP_BACKWARD_PAIRS=0) on the same rows:
+    dx and dy bit for bit, dw to float32 summation-order differences (twice the slots)."""
+    from ictc_o2_hp_b200 import TensorProduct
+    torch.manual_seed(channels + rows)
+    tp = TensorProduct(channels, m_max, parity=parity).to(cuda_device)
+    W = tp.representation_dimension
+    x, y, g = (torch.randn(rows, W, device=cuda_device) for _ in range(3))
+    w = tp.weight.detach()
+    args = (channels, m_max, parity, "component")
+    paired = torch.ops.ictc_o2_b200.tp_backward(x, y, w, g, *args)
+    monkeypatch.setenv("ICTC_TP_BACKWARD_PAIRS", "0")
+    single = torch.ops.ictc_o2_b200.tp_backward(x, y, w, g, *args)
+    assert torch.equal(paired[0], single[0]) and torch.equal(paired[1], single[1])
+    assert O.max_error(paired[2].cpu().numpy(), single[2].cpu().numpy()) < 1e-6
