@@ -352,6 +352,121 @@ __device__ __forceinline__ void store_partial(float* __restrict__ dst, const TpL
   });
 }
 
+// ------------------------------------------------------------ row-paired adjoint
+//
+// Two rows of the same (channel, world) run the same paths with the same weights and
+// signs, so the backward can carry them as the two halves of f32x2 values: every
+// product and dx / dy update of both rows is one paired FMA (each half rounded
+// exactly as the scalar form), and only the weight-gradient accumulator, shared by
+// the rows, takes two scalar FMAs.
+
+template <bool FIRST, int SIGN>
+__device__ __forceinline__ void mac2(float2& acc, float2 x, float2 y) {
+  if constexpr (FIRST) {
+    acc = SIGN > 0 ? __fmul2_rn(x, y) : __fmul2_rn(make_float2(-x.x, -x.y), y);
+  } else {
+    acc = SIGN > 0 ? __ffma2_rn(x, y, acc) : __ffma2_rn(make_float2(-x.x, -x.y), y, acc);
+  }
+}
+
+__device__ __forceinline__ float2 fma2w(float w, float2 x, float2 acc) {
+  return __ffma2_rn(make_float2(w, w), x, acc);
+}
+
+// path_vjp for a row pair (same factorizations, chosen the same way).
+template <int M, bool FULL, int I>
+__device__ __forceinline__ void path_vjp2(const float2* a, const float2* b, const float2* g,
+                                          float2* dx, float2* dy, float& acc, float w) {
+  using P = Paths<M, FULL>;
+  constexpr ChanPath cp = P::table.p[I];
+  constexpr int d1 = slot_dim(cp.in1), d2 = slot_dim(cp.in2), d3 = slot_dim(cp.out);
+  constexpr int cost0 = 2 * d3 + 3 * cp.nt;
+  constexpr int cost1 = 2 * cp.nt + 2 * d1 + d2;
+  constexpr int cost2 = 2 * cp.nt + d1 + 2 * d2;
+  if constexpr (cost0 <= cost1 && cost0 <= cost2) {
+    float2 s[2];
+    static_for<cp.nt>([&](auto T) {
+      constexpr Term t = P::table.p[I].t[T];
+      mac2<first_term<M, FULL, I, T, 0>(), t.s>(s[t.k], a[P::table.p[I].in1 + t.i],
+                                                 b[P::table.p[I].in2 + t.j]);
+    });
+    float2 wg[2];
+    acc = fmaf(g[cp.out].x, s[0].x, acc);
+    acc = fmaf(g[cp.out].y, s[0].y, acc);
+    wg[0] = __fmul2_rn(make_float2(w, w), g[cp.out]);
+    if constexpr (d3 == 2) {
+      acc = fmaf(g[cp.out + 1].x, s[1].x, acc);
+      acc = fmaf(g[cp.out + 1].y, s[1].y, acc);
+      wg[1] = __fmul2_rn(make_float2(w, w), g[cp.out + 1]);
+    }
+    static_for<cp.nt>([&](auto T) {
+      constexpr Term t = P::table.p[I].t[T];
+      constexpr int i1 = P::table.p[I].in1 + t.i;
+      constexpr int i2 = P::table.p[I].in2 + t.j;
+      mac2<false, t.s>(dx[i1], wg[t.k], b[i2]);
+      mac2<false, t.s>(dy[i2], wg[t.k], a[i1]);
+    });
+  } else {
+    float2 tv[2], uv[2];
+    static_for<cp.nt>([&](auto T) {
+      constexpr Term t = P::table.p[I].t[T];
+      constexpr int i1 = P::table.p[I].in1 + t.i;
+      constexpr int i2 = P::table.p[I].in2 + t.j;
+      constexpr int i3 = P::table.p[I].out + t.k;
+      mac2<first_term<M, FULL, I, T, 1>(), t.s>(tv[t.i], b[i2], g[i3]);
+      mac2<first_term<M, FULL, I, T, 2>(), t.s>(uv[t.j], a[i1], g[i3]);
+    });
+    static_for<d1>([&](auto i) { dx[cp.in1 + i] = fma2w(w, tv[i], dx[cp.in1 + i]); });
+    static_for<d2>([&](auto j) { dy[cp.in2 + j] = fma2w(w, uv[j], dy[cp.in2 + j]); });
+    if constexpr (cost1 <= cost2) {
+      static_for<d1>([&](auto i) {
+        acc = fmaf(a[cp.in1 + i].x, tv[i].x, acc);
+        acc = fmaf(a[cp.in1 + i].y, tv[i].y, acc);
+      });
+    } else {
+      static_for<d2>([&](auto j) {
+        acc = fmaf(b[cp.in2 + j].x, uv[j].x, acc);
+        acc = fmaf(b[cp.in2 + j].y, uv[j].y, acc);
+      });
+    }
+  }
+}
+
+// row_vjp for a row pair.
+template <int M, bool FULL, class Chunks>
+__device__ __forceinline__ void row_vjp2(const float2 (&a)[2 * M + 2],
+                                         const float2 (&b)[2 * M + 2],
+                                         const float2 (&g)[2 * M + 2], const Chunks& wsrc, int q,
+                                         float2 (&dx)[2 * M + 2], float2 (&dy)[2 * M + 2],
+                                         float (&acc)[Paths<M, FULL>::n]) {
+  using P = Paths<M, FULL>;
+#pragma unroll
+  for (int s = 0; s < 2 * M + 2; ++s) {
+    dx[s] = make_float2(0.f, 0.f);
+    dy[s] = make_float2(0.f, 0.f);
+  }
+  float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto step = [&](auto K) {
+    constexpr int I = P::vjp.idx[K];
+    if constexpr (K % 4 == 0) w4 = wsrc.ld(K / 4);
+    const float wv = K % 4 == 0 ? w4.x : (K % 4 == 1 ? w4.y : (K % 4 == 2 ? w4.z : w4.w));
+    path_vjp2<M, FULL, I>(a, b, g, dx, dy, acc[K], wv);
+  };
+  static_for<P::nfreq>(step);
+  if (!FULL || q == 0) {
+    static_for<P::n - P::nfreq>([&](auto J) { step(std::integral_constant<int, P::nfreq + J>{}); });
+  }
+  if (FULL) {
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+      dx[s].x += __shfl_xor_sync(0xffffffffu, dx[s].x, 16);
+      dx[s].y += __shfl_xor_sync(0xffffffffu, dx[s].y, 16);
+      dy[s].x += __shfl_xor_sync(0xffffffffu, dy[s].x, 16);
+      dy[s].y += __shfl_xor_sync(0xffffffffu, dy[s].y, 16);
+    }
+  }
+}
+
 // Lane -> (channel, world) of a warp that owns channel group `group`.
 template <bool FULL>
 struct LaneMap {
@@ -469,7 +584,7 @@ __device__ __forceinline__ void issue_stage(const StageRing& ring, int s, int64_
 // COUNT: the stage index and its fill round are carried from block to block (the
 // backward: 0.946 -> 0.908 ms at TP(128, 6, full), 65,536 rows) or recomputed from the
 // block count by division (the forwards: 0.462 ms against 0.470 ms with counters).
-template <int NT, bool COUNT, class Body>
+template <int NT, bool COUNT, int RPW = 1, class Body>
 __device__ __forceinline__ void staged_loop(unsigned char* smem, unsigned char* base, int stages,
                                             int R, int64_t rows, int64_t W,
                                             const float* const* src, Body&& body) {
@@ -478,7 +593,8 @@ __device__ __forceinline__ void staged_loop(unsigned char* smem, unsigned char* 
   unsigned* done = reinterpret_cast<unsigned*>(ring.empty);
   const int nwarps = blockDim.x >> 5;
   const int r = (threadIdx.x >> 5) / (nwarps / R);
-  const int64_t nblocks = (rows + R - 1) / R;
+  const int RB = R * RPW;  // rows per block: RPW per warp row slot
+  const int64_t nblocks = (rows + RB - 1) / RB;
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&ring.full[s], 1);
@@ -490,7 +606,7 @@ __device__ __forceinline__ void staged_loop(unsigned char* smem, unsigned char* 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       const int64_t block = blockIdx.x + static_cast<int64_t>(s) * gridDim.x;
-      if (block < nblocks) issue_stage<NT>(ring, s, block, R, rows, W, src);
+      if (block < nblocks) issue_stage<NT>(ring, s, block, RB, rows, W, src);
     }
   }
   int s = 0;
@@ -504,8 +620,8 @@ __device__ __forceinline__ void staged_loop(unsigned char* smem, unsigned char* 
     }
     ok = mbar_wait(&ring.full[s], round & 1, 1);
     if (!ok) break;
-    const int64_t row = block * R + r;
-    if (row < rows) body(ring.buf + static_cast<int64_t>(s) * NT * R * W + r * W, row);
+    const int64_t row = block * RB + r * RPW;
+    if (row < rows) body(ring.buf + static_cast<int64_t>(s) * NT * RB * W + r * RPW * W, row);
     __syncwarp();
     if ((threadIdx.x & 31) == 0) {
       unsigned prev;
@@ -518,7 +634,7 @@ __device__ __forceinline__ void staged_loop(unsigned char* smem, unsigned char* 
         // asynchronous copy that overwrites it, then refill
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         const int64_t next = block + static_cast<int64_t>(stages) * gridDim.x;
-        if (next < nblocks) issue_stage<NT>(ring, s, next, R, rows, W, src);
+        if (next < nblocks) issue_stage<NT>(ring, s, next, RB, rows, W, src);
       }
     }
     if constexpr (COUNT) {
@@ -748,6 +864,88 @@ __global__ void __launch_bounds__(kStagedWarps * 32, 1)
   } else {
     const GlobalChunks chunks{ws + t, T};
     staged_loop<3, true>(smem, smem, stages, R, rows, W, src, body(chunks));
+  }
+  if (lm.active) {
+    const int64_t slot = static_cast<int64_t>(blockIdx.x) * R + r;
+    store_partial<M, FULL>(partial + slot * numel, L, mags, lm.c, lm.q, acc);
+  }
+}
+
+// Staged backward over row pairs: a stage holds 2 R rows per operand and each warp
+// carries rows 2 r and 2 r + 1 of it through row_vjp2 (paired f32x2 arithmetic).  dx and
+// dy of each row equal those of tp_backward_staged bit for bit; the weight-gradient slot
+// takes the two rows' terms path by path (another float32 summation order).  A missing
+// second row (odd row count) computes on zeros and stores nothing.
+template <int M, bool FULL, bool CM = false>
+__global__ void __launch_bounds__(kStagedWarps * 32, 1)
+    tp_backward_paired(const float* __restrict__ x, const float* __restrict__ y,
+                       const float4* __restrict__ ws, const float* __restrict__ go,
+                       float* __restrict__ gx, float* __restrict__ gy,
+                       float* __restrict__ partial, int64_t numel, int64_t rows, TpLayout L,
+                       Mags mags, int groups, int R, int stages, int weights_in_smem) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  using P = Paths<M, FULL>;
+  constexpr int S = 2 * M + 2;
+  const int warp = threadIdx.x >> 5;
+  const int r = warp / groups;
+  const int T = groups * 32;
+  const int t = (warp % groups) * 32 + (threadIdx.x & 31);
+  const LaneMap<FULL> lm(warp % groups, threadIdx.x & 31, L.C);
+  const size_t wbytes = static_cast<size_t>(P::chunks) * T * sizeof(float4);
+  const int RB = 2 * R;  // rows per stage block
+  float acc[P::n];
+#pragma unroll
+  for (int i = 0; i < P::n; ++i) acc[i] = 0.0f;
+  const float* src[3] = {x, y, go};
+  const int64_t W = L.width;
+  auto body = [&](const auto& chunks) {
+    return [&](const float* stage, int64_t row) {
+      const bool two = row + 1 < rows;
+      float2 a[S], b[S], g[S], dx[S], dy[S];
+      auto load_pair = [&](const float* base, float2 (&v)[S]) {
+        float u0[S], u1[S];
+        load_slots<M, FULL, CM>(SharedRow(base), L, lm.c, lm.q, u0);
+        load_slots<M, FULL, CM>(SharedRow(base + W), L, lm.c, lm.q, u1);
+#pragma unroll
+        for (int k = 0; k < S; ++k) v[k] = make_float2(u0[k], two ? u1[k] : 0.f);
+      };
+      load_pair(stage, a);
+      load_pair(stage + RB * W, b);
+      load_pair(stage + 2 * RB * W, g);
+      row_vjp2<M, FULL>(a, b, g, chunks, lm.q, dx, dy, acc);
+      if (lm.active) {
+        auto store_pair = [&](float* dst, const float2 (&v)[S]) {
+          float v0[S], v1[S];
+#pragma unroll
+          for (int k = 0; k < S; ++k) {
+            v0[k] = v[k].x;
+            v1[k] = v[k].y;
+          }
+          store_slots<M, FULL, CM>(dst + row * W, L, lm.c, lm.q, true, v0);
+          if (two) store_slots<M, FULL, CM>(dst + (row + 1) * W, L, lm.c, lm.q, true, v1);
+        };
+        store_pair(gx, dx);
+        store_pair(gy, dy);
+      }
+    };
+  };
+  if (weights_in_smem) {
+    uint64_t* wbar = reinterpret_cast<uint64_t*>(smem) + 2 * kMaxStages;
+    float4* wsm = reinterpret_cast<float4*>(smem + kBarrierBytes);
+    if (threadIdx.x == 0) {
+      mbar_init(wbar, 1);
+      fence_mbarrier_init();
+      mbar_arrive_expect_tx(wbar, static_cast<uint32_t>(wbytes));
+      bulk_g2s(wsm, ws, static_cast<uint32_t>(wbytes), wbar);
+    }
+    __syncthreads();
+    if (!mbar_wait(wbar, 0, 4)) return;
+    const SharedChunks chunks{static_cast<uint32_t>(__cvta_generic_to_shared(wsm + t)),
+                              T * static_cast<int>(sizeof(float4))};
+    staged_loop<3, true, 2>(smem, smem + wbytes, stages, R, rows, W, src, body(chunks));
+  } else {
+    const GlobalChunks chunks{ws + t, T};
+    staged_loop<3, true, 2>(smem, smem, stages, R, rows, W, src, body(chunks));
   }
   if (lm.active) {
     const int64_t slot = static_cast<int64_t>(blockIdx.x) * R + r;
@@ -998,7 +1196,18 @@ struct Kernels {
   int chunks;  // float4 weight chunks per thread (Paths::chunks)
   ForwardGroupedFn fwd_grouped;
   BackwardTiledFn bwd_tiled;
+  BackwardStagedFn bwd_paired;  // row pairs through paired f32x2 arithmetic, or null
 };
+
+// Row-paired backward where the sweep measured it faster than the scalar staged kernel:
+// full parity, m_max 3 and 4 (backward 1.11-1.22x at C = 32-128; at m_max 5-6 the
+// paired per-row state spills at 255 registers and it lost 0.81-0.93x, and below 3 two
+// scalar CTAs per SM win).  Both layouts, so they stay bit-identical to each other.
+template <int M, bool FULL, bool CM>
+constexpr BackwardStagedFn paired_for() {
+  if constexpr (FULL && (M == 3 || M == 4)) return &tp_backward_paired<M, FULL, CM>;
+  else return nullptr;
+}
 
 // Kernels of one (order, parity, frequency-block layout); the layout is a template
 // parameter so that each layout runs its own straight-line slot accesses.
@@ -1010,9 +1219,11 @@ constexpr Kernels kernels_for() {
     return Kernels{wide, &tp_forward_direct<M, FULL, CM>, &tp_backward_direct<M, FULL, CM>,
                    &tp_forward_staged<M, FULL, CM>, &tp_backward_staged<M, FULL, CM>,
                    &prescale_kernel<M, FULL>, Paths<M, FULL>::chunks,
-                   &tp_forward_grouped<M, FULL, CM>, &tp_backward_tiled<M, FULL, CM>};
+                   &tp_forward_grouped<M, FULL, CM>, &tp_backward_tiled<M, FULL, CM>,
+                   paired_for<M, FULL, CM>()};
   } else {
-    return Kernels{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0, nullptr, nullptr};
+    return Kernels{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0, nullptr, nullptr,
+                   nullptr};
   }
 }
 
@@ -1081,7 +1292,7 @@ int plan_direct(const void* kernel, int device, int64_t rows, int C, bool full, 
 // With `weight_bytes` > 0 the weights go to shared memory in front of the stages
 // when at least three stages still fit.
 struct StagedPlan {
-  bool ok, weights_in_smem;
+  bool ok, weights_in_smem, paired;
   int groups, R, warps, stages;
   int64_t grid;
   size_t smem;
@@ -1091,7 +1302,7 @@ struct StagedPlan {
 // (the caller checks that their registers fit), and the grid has that many per SM.
 StagedPlan plan_staged(int device, int64_t rows, const TpLayout& L, bool full, int tensors,
                        size_t weight_bytes, int max_warps = kStagedWarps, int max_stages = kMaxStages,
-                       bool weights_required = false, int ctas_per_sm = 1) {
+                       bool weights_required = false, int ctas_per_sm = 1, int rows_per_warp = 1) {
   StagedPlan p{};
   // per-SM shared memory of sm_100 (228 KB) less the 1 KB each CTA reserves, and a margin
   const size_t budget =
@@ -1101,7 +1312,8 @@ StagedPlan plan_staged(int device, int64_t rows, const TpLayout& L, bool full, i
   if (p.groups > max_warps || L.width % 4 != 0 || rows == 0) return p;
   p.R = max_warps / p.groups;
   p.warps = p.R * p.groups;
-  const size_t stage_bytes = static_cast<size_t>(tensors) * p.R * L.width * sizeof(float);
+  const size_t stage_bytes =
+      static_cast<size_t>(tensors) * p.R * rows_per_warp * L.width * sizeof(float);
   if (weight_bytes > 0 && budget > kBarrierBytes + weight_bytes) {
     const int fit =
         static_cast<int>((budget - kBarrierBytes - weight_bytes) / stage_bytes);
@@ -1118,7 +1330,7 @@ StagedPlan plan_staged(int device, int64_t rows, const TpLayout& L, bool full, i
     if (p.stages < 2) return p;
     p.smem = kBarrierBytes + static_cast<size_t>(p.stages) * stage_bytes;
   }
-  const int64_t nblocks = ceil_div(rows, p.R);
+  const int64_t nblocks = ceil_div(rows, static_cast<int64_t>(p.R) * rows_per_warp);
   p.grid = static_cast<int64_t>(sm_count(device)) * ctas_per_sm;
   if (p.grid > nblocks) p.grid = nblocks;
   p.ok = true;
@@ -1198,6 +1410,13 @@ bool staged_pairs_enabled() {
   return v == nullptr || strcmp(v, "0") != 0;
 }
 
+// Row-paired backward where compiled (default); ICTC_TP_BACKWARD_ROWPAIR=0 runs the
+// scalar staged kernel instead (tests cover both).
+bool row_pairs_enabled() {
+  const char* v = getenv("ICTC_TP_BACKWARD_ROWPAIR");
+  return v == nullptr || strcmp(v, "0") != 0;
+}
+
 // Backward workspace: [per-thread float4 weight chunks][slots x numel partials].
 size_t weight_chunk_bytes(const Kernels& k, int C, bool full) {
   const int64_t T = ceil_div(C, full ? 16 : 32) * 32;
@@ -1249,18 +1468,31 @@ int ctas_by_registers(const void* fn, int warps) {
 // 1.03-1.34x where the single CTA has fewer than 8 warps (C = 96) or m_max = 1 at
 // C >= 64, but 0.79-0.92x at m_max 2-3 otherwise (their single CTA already reaches
 // 0.8-0.98 of HBM at 65,536 rows) and 0.84x at C = 32, m_max 1; those keep one CTA.
+// Where one CTA per SM remains and a row-paired kernel is compiled (full parity, m_max
+// 3-4), each warp takes two rows at a time (stages of 2 R rows).
 StagedPlan plan_staged_backward(int device, const Kernels& k, int64_t rows, const TpLayout& L,
                                 bool full) {
   const size_t wb = weight_chunk_bytes(k, L.C, full);
   const StagedPlan p = plan_staged(device, rows, L, full, 3, wb);
-  if (!p.ok || !staged_pairs_enabled()) return p;
+  if (!p.ok) return p;
   const int m_max = static_cast<int>((L.width - L.fbase) / L.fstride);
-  if (!full && p.warps >= kStagedWarps && !(m_max == 1 && L.C >= 64)) return p;
-  const int ctas = ctas_by_registers(reinterpret_cast<const void*>(k.bwd_staged), p.warps);
+  const int ctas = !staged_pairs_enabled() ||
+                           (!full && p.warps >= kStagedWarps && !(m_max == 1 && L.C >= 64))
+                       ? 1
+                       : ctas_by_registers(reinterpret_cast<const void*>(k.bwd_staged), p.warps);
   if (ctas > 1) {
     const StagedPlan q =
         plan_staged(device, rows, L, full, 3, wb, kStagedWarps, kMaxStages, false, ctas);
     if (q.ok) return q;
+  }
+  if (k.bwd_paired != nullptr && row_pairs_enabled()) {
+    // two rows per warp: stages of 2 R rows
+    StagedPlan q =
+        plan_staged(device, rows, L, full, 3, wb, kStagedWarps, kMaxStages, false, 1, 2);
+    if (q.ok) {
+      q.paired = true;
+      return q;
+    }
   }
   return p;
 }
@@ -1534,9 +1766,9 @@ int32_t tp_backward_impl(const float* left, const float* right, const float* wei
         maps, chunks, grad_left, grad_right, partial, numel, rows, L, Lt, mags, tp.gt, tp.R,
         tp.stages, tp.ntiles, tp.weights_in_smem ? 1 : 0);
   } else if (staged) {
-    if ((st = allow_smem(reinterpret_cast<const void*>(k.bwd_staged), sp.smem)) != ICTC_OK)
-      return st;
-    k.bwd_staged<<<static_cast<unsigned>(sp.grid), sp.warps * 32, sp.smem, s>>>(
+    const BackwardStagedFn fn = sp.paired ? k.bwd_paired : k.bwd_staged;
+    if ((st = allow_smem(reinterpret_cast<const void*>(fn), sp.smem)) != ICTC_OK) return st;
+    fn<<<static_cast<unsigned>(sp.grid), sp.warps * 32, sp.smem, s>>>(
         left, right, chunks, grad_output, grad_left, grad_right, partial, numel, rows, L, mags,
         sp.groups, sp.R, sp.stages, sp.weights_in_smem ? 1 : 0);
   } else {

@@ -385,3 +385,27 @@ def test_paired_staged_backward_matches_single(channels, m_max, parity, rows, cu
     single = torch.ops.ictc_o2_b200.tp_backward(x, y, w, g, *args)
     assert torch.equal(paired[0], single[0]) and torch.equal(paired[1], single[1])
     assert O.max_error(paired[2].cpu().numpy(), single[2].cpu().numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("channels,m_max,parity,rows", [
+    (128, 3, "full", 4001),    # odd: the last warp pair has one row
+    (64, 4, "full", 3000),
+    (32, 3, "full", 777),
+])
+def test_row_paired_backward_matches_scalar(channels, m_max, parity, rows, cuda_device,
+                                            monkeypatch):
+    """Full parity at m_max 3-4 runs the row-paired staged backward (two rows per warp in
+    paired f32x2 arithmetic); against the scalar staged kernel (ICTC_TP_BACKWARD_ROWPAIR=0)
+    on the same rows: dx and dy bit for bit, dw to float32 summation-order differences."""
+    from ictc_o2_hp_b200 import TensorProduct
+    torch.manual_seed(channels + rows)
+    tp = TensorProduct(channels, m_max, parity=parity).to(cuda_device)
+    W = tp.representation_dimension
+    x, y, g = (torch.randn(rows, W, device=cuda_device) for _ in range(3))
+    w = tp.weight.detach()
+    args = (channels, m_max, parity, "component")
+    paired = torch.ops.ictc_o2_b200.tp_backward(x, y, w, g, *args)
+    monkeypatch.setenv("ICTC_TP_BACKWARD_ROWPAIR", "0")
+    scalar = torch.ops.ictc_o2_b200.tp_backward(x, y, w, g, *args)
+    assert torch.equal(paired[0], scalar[0]) and torch.equal(paired[1], scalar[1])
+    assert O.max_error(paired[2].cpu().numpy(), scalar[2].cpu().numpy()) < 1e-6
