@@ -17,9 +17,10 @@
 // triton_o2.py:744-780, 948-959).
 //
 // Two kernel families share this per-row arithmetic:
-//   * staged: persistent CTAs (one per SM) that stream blocks of whole rows into
-//     shared memory with bulk asynchronous copies (TMA) through an mbarrier ring,
-//     so HBM latency hides behind the arithmetic of earlier rows;
+//   * staged: persistent CTAs (one per SM, two for small orders) that stream blocks of
+//     whole rows into shared memory with bulk asynchronous copies (TMA) through an
+//     mbarrier ring, so HBM latency hides behind the arithmetic of earlier rows; the
+//     row-paired backward carries two rows per warp as f32x2 halves;
 //   * direct: plain coalesced global loads, for operands that are not 16-byte
 //     aligned or rows wider than one CTA.
 #include <cuda_runtime.h>
@@ -1107,14 +1108,18 @@ __global__ void __launch_bounds__(kStagedWarps * 32, 1)
 // Magnitude-scaled weights in the per-thread order of row_vjp: chunk k of thread
 // t (channel group t / 32, lane t % 32) holds the weights of paths vjp[4k..4k+3]
 // for that lane's (channel, world), at ws[k * T + t]; unused entries are zero.
+// blockIdx.y is the chunk, so the chunks are written by as many CTAs in parallel
+// (one CTA writing every chunk took 9 us at TP(128, 6, full)).
 template <int M, bool FULL, bool CM = false>
 __global__ void prescale_kernel(const float* __restrict__ w, float4* __restrict__ ws,
                                 TpLayout L, Mags mags, int groups) {
   using P = Paths<M, FULL>;
   const int T = groups * 32;
+  const int chunk = blockIdx.y;
   for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
     const LaneMap<FULL> lm(t / 32, t % 32, L.C);
     static_for<P::chunks>([&](auto k) {
+      if (k != chunk) return;
       float v[4];
       static_for<4>([&](auto e) {
         constexpr int pos = 4 * k + e;
@@ -1754,7 +1759,9 @@ int32_t tp_backward_impl(const float* left, const float* right, const float* wei
   float* partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + wbytes);
   const Mags mags = tp_mags(normalization);
   const int groups = static_cast<int>(ceil_div(channels, full ? 16 : 32));
-  k.prescale<<<static_cast<unsigned>(ceil_div(groups * 32, 256)), 256, 0, s>>>(weight, chunks, L,
+  k.prescale<<<dim3(static_cast<unsigned>(ceil_div(groups * 32, 256)),
+                   static_cast<unsigned>(k.chunks)),
+               256, 0, s>>>(weight, chunks, L,
                                                                                mags, groups);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "prescale launch");
