@@ -524,6 +524,11 @@ class RadialMpWorkload(RadialWorkload):
         from ictc_o2_hp_b200 import parallel
         self.radial_messages, self.scatter_sum = radial_messages, scatter_sum
         self.parallel = parallel
+        # edges stored in source order (CSR by source, as graph libraries keep them):
+        # the same edges, relabelled, so consecutive edges share their node row
+        perm = self.torch.sort(self.src_shard, stable=True).indices
+        self.src_shard, self.dst_shard = self.src_shard[perm], self.dst_shard[perm]
+        self.r, self.angular = self.r[perm].contiguous(), self.angular[perm].contiguous()
         self.edge_index = EdgeIndex(self.src_shard, self.dst_shard, self.NODES)
         # --node-partition (N > 1): rank r owns node block r; node features are
         # all-gathered, node outputs and node gradients reduce-scattered to the owners
@@ -565,7 +570,8 @@ class RadialMpWorkload(RadialWorkload):
 
     def config(self):
         c = super().config()
-        c["workload"] = ("message-passing layer (config 5 shapes): node features [65536, 896] "
+        c["workload"] = ("message-passing layer (config 5 shapes): edges stored in source "
+                         "order, node features [65536, 896] "
                          "read by source inside the radial kernels (no gathered copy), Bessel(8) "
                          "x cosine cutoff, MLP 8-64-64 SiLU, fused affine + V=1 uvu C64 m3, "
                          "messages summed into destination nodes in a fixed order; VJP to node "
