@@ -15,7 +15,8 @@
 // sum, so one pair of kernels serves both directions.
 //
 // Both kernels are HBM-bound streams: one warp per output row, 16-byte column
-// chunks when the width and pointers allow, plain loads otherwise.
+// chunks when the width and pointers allow (the segment sum then keeps each lane's
+// columns in registers across the segment's edges), plain loads otherwise.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -48,6 +49,67 @@ __global__ void __launch_bounds__(kGraphThreads) gather_rows_kernel(
       for (int64_t c = lane; c < width / 4; c += 32) d4[c] = __ldg(s4 + c);
     } else {
       for (int64_t c = lane; c < width; c += 32) dst[c] = __ldg(row + c);
+    }
+  }
+}
+
+// 16-byte segment sum with each lane's column block in registers: a warp reads up to 32
+// edge indices of its segment at once (one per lane) and hands them out by shuffle, then
+// every lane loads its K float4 columns of one edge row together, so K loads per lane
+// are in flight per edge instead of one index load and one value load in sequence.
+// Columns are summed over the segment's edges in increasing e, as segment_sum_kernel
+// does: the results are bit-identical.
+constexpr int kSegCols = 8;  // float4 columns per lane held in registers
+
+__global__ void __launch_bounds__(kGraphThreads) segment_sum_vec_kernel(
+    const float* __restrict__ values, const int64_t* __restrict__ offsets,
+    const int64_t* __restrict__ order, float* __restrict__ out, int64_t segments, int64_t width,
+    int64_t value_rows, int* bad) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kGraphThreads / 32);
+  const int64_t w4 = width / 4;
+  for (int64_t s = static_cast<int64_t>(blockIdx.x) * (kGraphThreads / 32) + (threadIdx.x >> 5);
+       s < segments; s += warps) {
+    int64_t e0 = __ldg(offsets + s), e1 = __ldg(offsets + s + 1);
+    if (e0 < 0 || e1 < e0 || e1 > value_rows) {
+      // not a CSR range of the value / order rows: flag it, sum nothing
+      if (lane == 0) atomicExch(bad, 1);
+      e0 = e1 = 0;
+    }
+    float4* d4 = reinterpret_cast<float4*>(out + s * width);
+    for (int64_t cb = 0; cb < w4; cb += 32 * kSegCols) {
+      float4 acc[kSegCols];
+#pragma unroll
+      for (int k = 0; k < kSegCols; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int64_t eb = e0; eb < e1; eb += 32) {
+        const int n = e1 - eb < 32 ? static_cast<int>(e1 - eb) : 32;
+        int64_t mine = -1;
+        if (lane < n) {
+          const int64_t r = order ? __ldg(order + eb + lane) : eb + lane;
+          if (r >= 0 && r < value_rows) mine = r;
+          else if (cb == 0) atomicExch(bad, 1);
+        }
+        for (int j = 0; j < n; ++j) {
+          const int64_t r = __shfl_sync(0xffffffffu, mine, j);
+          if (r < 0) continue;
+          const float4* row = reinterpret_cast<const float4*>(values + r * width);
+          float4 v[kSegCols];
+#pragma unroll
+          for (int k = 0; k < kSegCols; ++k) {
+            const int64_t c = cb + lane + 32 * k;
+            v[k] = c < w4 ? __ldg(row + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int k = 0; k < kSegCols; ++k) {
+            acc[k].x += v[k].x; acc[k].y += v[k].y; acc[k].z += v[k].z; acc[k].w += v[k].w;
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kSegCols; ++k) {
+        const int64_t c = cb + lane + 32 * k;
+        if (c < w4) d4[c] = acc[k];
+      }
     }
   }
 }
@@ -150,9 +212,16 @@ extern "C" int32_t ictc_o2_segment_sum(const float* values, const int64_t* offse
   int* bad = bad_flag();
   if (!bad) return fail(ICTC_ERR_CUDA, "device flag lookup failed");
   const bool vec = width % 4 == 0 && (value_rows == 0 || aligned(values, 16)) && aligned(out, 16);
-  segment_sum_kernel<<<graph_grid(segments), kGraphThreads, 0,
-                       static_cast<cudaStream_t>(stream)>>>(values, offsets, order, out, segments,
-                                                            width, value_rows, vec, bad);
+  if (vec)
+    segment_sum_vec_kernel<<<graph_grid(segments), kGraphThreads, 0,
+                             static_cast<cudaStream_t>(stream)>>>(values, offsets, order, out,
+                                                                  segments, width, value_rows,
+                                                                  bad);
+  else
+    segment_sum_kernel<<<graph_grid(segments), kGraphThreads, 0,
+                         static_cast<cudaStream_t>(stream)>>>(values, offsets, order, out,
+                                                              segments, width, value_rows, false,
+                                                              bad);
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "segment_sum launch");
 }
