@@ -39,6 +39,21 @@ struct DySmem {
   float red[4][32][32];  // warp-sum tree: [warp][value][lane]
 };
 
+// Path record of path position pos (by_j order), built once per CTA after DySmem in
+// shared memory, so the per-path reads are shared-memory loads rather than a chain of
+// dependent global loads: {path, x_i offset, g_k offset, y_j offset | dims | last of j},
+// the dims d1 - 1, d3 - 1, d2 - 1 in bits 24-26 and "last path of its j group" in
+// bit 27 of the fourth word (y_j offsets are below 2^24); then the path's 8
+// coefficients.
+struct DyPath {
+  int4 rec;
+  float2 c[4];
+};
+
+inline size_t uvu_dy_stage_smem(int np) {
+  return sizeof(DySmem) + static_cast<size_t>(np) * sizeof(DyPath);
+}
+
 inline bool uvu_dy_stage_fits(int U, int V, int W1, bool aligned_rows) {
   return U <= kDyU && V <= kDyV && U % 4 == 0 && V % 4 == 0 && W1 % 4 == 0 && aligned_rows;
 }
@@ -60,16 +75,32 @@ __device__ __forceinline__ float2 dy_slot(const float* p, int dim) {
 __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
   extern __shared__ __align__(16) unsigned char dy_raw[];
   DySmem& S = *reinterpret_cast<DySmem*>(dy_raw);
+  DyPath* recs = reinterpret_cast<DyPath*>(dy_raw + sizeof(DySmem));
   const int tid = threadIdx.x;
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kDyRows;
   const int nvalid = A.rows - row0 < kDyRows ? static_cast<int>(A.rows - row0) : kDyRows;
   const int np = A.t.np;
+  for (int q = tid; q < np; q += 256) {
+    const int p = A.t.by_j[q];
+    const int4 pt = A.t.paths[p];
+    const int2 ei = A.t.in1[pt.x], ej = A.t.in2[pt.y], ek = A.t.in1[pt.z];
+    const bool last = q + 1 == np || A.t.paths[A.t.by_j[q + 1]].y != pt.y;
+    DyPath d;
+    d.rec = make_int4(p, ei.x, ek.x,
+                      ej.x | ((ei.y - 1) << 24) | ((ek.y - 1) << 25) | ((ej.y - 1) << 26) |
+                          (last ? 1 << 27 : 0));
+    const float2* cp = reinterpret_cast<const float2*>(A.t.coef + 8 * p);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) d.c[k] = __ldg(cp + k);
+    recs[q] = d;
+  }
+  __syncthreads();  // path records visible
   // x / g slices of path position pos (zero-filled past the rows)
   auto issue_xg = [&](int pos) {
     if (pos < np) {
-      const int p = A.t.by_j[pos];
-      const int4 pt = A.t.paths[p];
-      const int2 ei = A.t.in1[pt.x], ek = A.t.in1[pt.z];
+      const int4 rc = recs[pos].rec;
+      const int2 ei = make_int2(rc.y, ((rc.w >> 24) & 1) + 1);
+      const int2 ek = make_int2(rc.z, ((rc.w >> 25) & 1) + 1);
       const int nx = A.U * ei.y / 4, ng = A.U * ek.y / 4;  // float4 per row (<= 64)
       // thread -> float4 column tid % 64 of rows tid / 64 + 4 k: no index division
       const int c = tid & 63, rb = tid >> 6;
@@ -87,7 +118,7 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
   // weights w_p [U][V] of path position pos into buffer buf
   auto issue_w = [&](int pos, int buf) {
     if (pos < np) {
-      const int p = A.t.by_j[pos];
+      const int p = recs[pos].rec.x;
       const float* wsrc = A.w + static_cast<int64_t>(p) * A.U * A.V;
       // thread -> float4 column tid % 8 of channels tid / 8 + 32 k (V <= 32, U <= 128)
       const int c = tid & 7, ub = tid >> 3;
@@ -124,12 +155,13 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
     const int buf = pos & 1;
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();  // slices of pos visible; previous GEMM done with S and wp[buf ^ 1]
-    const int p = A.t.by_j[pos];
-    const int4 pt = A.t.paths[p];
-    const int2 ei = A.t.in1[pt.x], ej = A.t.in2[pt.y], ek = A.t.in1[pt.z];
+    const int4 rc = recs[pos].rec;
+    const int2 ei = make_int2(rc.y, ((rc.w >> 24) & 1) + 1);
+    const int2 ek = make_int2(rc.z, ((rc.w >> 25) & 1) + 1);
+    const int2 ej = make_int2(rc.w & 0xffffff, ((rc.w >> 26) & 1) + 1);
     // coefficient pairs over b: (c[4 kc + 2 a], c[4 kc + 2 a + 1])
-    const float2* cp = reinterpret_cast<const float2*>(A.t.coef + 8 * p);
-    const float2 c0 = __ldg(cp), c1 = __ldg(cp + 1), c2 = __ldg(cp + 2), c3 = __ldg(cp + 3);
+    const float2 c0 = recs[pos].c[0], c1 = recs[pos].c[1], c2 = recs[pos].c[2],
+                 c3 = recs[pos].c[3];
     // (s0, s1) = g0 (c0 x0 + c1 x1) + g1 (c2 x0 + c3 x1), both b at once (f32x2)
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
@@ -160,7 +192,7 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
 #pragma unroll
         for (int k = 0; k < 2; ++k) acc[m][k] = fma2(av[m], bv[k], acc[m][k]);
     }
-    const bool last = pos + 1 == np || A.t.paths[A.t.by_j[pos + 1]].y != pt.y;
+    const bool last = (rc.w >> 27) & 1;
     if (last) {
       // sum the eight warps in a fixed order: w + 4, w + 2, w + 1 into w
 #pragma unroll

@@ -821,11 +821,13 @@ extern "C" int32_t ictc_o2_uvu_backward(const float* left, const float* right, c
   }
   if ((needed & 2) && uvu_dy_stage_fits(c.U, c.V, W1, aligned(left, 16) &&
                                                      aligned(grad_output, 16) &&
-                                                     aligned(weight, 16))) {
+                                                     aligned(weight, 16)) &&
+      uvu_dy_stage_smem(l.np) <= 227 * 1024) {
     const void* fn = reinterpret_cast<const void*>(&uvu_dy_stage);
-    if ((st = allow_smem(fn, sizeof(DySmem))) != ICTC_OK) return st;
+    const size_t dy_smem = uvu_dy_stage_smem(l.np);
+    if ((st = allow_smem(fn, dy_smem)) != ICTC_OK) return st;
     DyArgs da{left, grad_output, weight, grad_right, rows, c.U, c.V, W1, W2, t};
-    uvu_dy_stage<<<static_cast<unsigned>(ceil_div(rows, kDyRows)), 256, sizeof(DySmem), s>>>(da);
+    uvu_dy_stage<<<static_cast<unsigned>(ceil_div(rows, kDyRows)), 256, dy_smem, s>>>(da);
   } else if (needed & 2) {
     const size_t smem = 128 * kDpStride * sizeof(float) > 4 * 64 * 32 * sizeof(float)
                             ? 128 * kDpStride * sizeof(float)
