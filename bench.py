@@ -956,17 +956,21 @@ def run_gpu(args) -> dict | None:
     return result
 
 
-# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one 16,384-row
-# launch of the TensorProduct(128, 6, full) kernels, from ncu; the line carries it
-# scaled by rows to the launch it reports, and says so.
-TRAFFIC_16K_ROWS = {"tp_backward": 1.0626e9, "tp_forward": 0.6245e9}
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one 65,536-row launch
+# of the TensorProduct(128, 6, full) kernels (the default workload's own launch), from a
+# one-pass ncu capture of this bench command; other row counts carry it scaled by rows,
+# and the line says which.
+TRAFFIC_65K_ROWS = {"tp_backward": 2.6174e9 + 1.7112e9, "tp_forward": 1.7450e9 + 0.8421e9}
 
 
 def traffic_of(wl, name):
     """(bytes per launch, how obtained) for the dominant kernel, or (None, None)."""
-    if wl.name == "tp" and name in TRAFFIC_16K_ROWS:
-        return (TRAFFIC_16K_ROWS[name] * wl.rows / 16384,
-                "ncu DRAM bytes of a 16,384-row launch of the same kernel, scaled by rows to "
+    if wl.name == "tp" and name in TRAFFIC_65K_ROWS:
+        if wl.rows == 65536:
+            return (TRAFFIC_65K_ROWS[name],
+                    "ncu DRAM bytes (read + write) of this 65,536-row launch of the kernel")
+        return (TRAFFIC_65K_ROWS[name] * wl.rows / 65536,
+                "ncu DRAM bytes of a 65,536-row launch of the same kernel, scaled by rows to "
                 f"this {wl.rows}-row launch")
     return None, None
 
