@@ -1137,13 +1137,131 @@ def run_reference(args) -> dict | None:
     }
 
 
+# ------------------------------------------------------------------ reference GPU path
+
+def run_reference_gpu(args) -> dict | None:
+    """The reference package's own public API on this GPU (its Triton kernels, which
+    it picks for CUDA float32 inputs), on the same workload, seeds and timing as the
+    ours arm: TensorProduct config 2 (default), uvu config 4 (shared weights) or the
+    radial product of config 5 (--workload tp | uvu | radial; the radial network in
+    front of the product is the same PyTorch MLP).  It needs the reference installed
+    under baseline/_ref (pip install --target); without it the line says unavailable.
+    One GPU, rank 0 (other ranks exit without work)."""
+    import torch
+    if int(os.environ.get("RANK", "0")) != 0:
+        return None
+    ref_dir = ROOT / "baseline" / "_ref"
+    base = {"impl": "reference_gpu", "metric": METRICS.get(args.workload, args.workload)}
+    if not (ref_dir / "ictc_o2_hp").is_dir():
+        return {**base, "unavailable": "the reference package is not installed under "
+                                       "baseline/_ref"}
+    if args.workload not in ("tp", "uvu", "radial"):
+        return {**base, "unavailable": f"no reference GPU leg for workload {args.workload}"}
+    sys.path.insert(0, str(ref_dir))
+    import ictc_o2_hp as ref
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    torch.set_float32_matmul_precision("highest")
+    gen = torch.Generator(device=device)
+    if args.workload == "tp":
+        rows = args.rows or 65536
+        torch.manual_seed(0)
+        tp = ref.TensorProduct(128, 6, parity="full").to(device)
+        W = tp.representation_dimension
+        gen.manual_seed(1000)
+        x = torch.randn(rows, W, device=device, generator=gen).requires_grad_(True)
+        y = torch.randn(rows, W, device=device, generator=gen).requires_grad_(True)
+        g = torch.ones(rows, W, device=device)
+        params, inputs = [tp.weight], (x, y)
+
+        def step():
+            return torch.autograd.grad(tp(x, y), [x, y] + params, g)
+        workload = ("TensorProduct(128, 6, parity='full') forward + VJP (dx, dy, dw), "
+                    f"{rows} rows, ones cotangent")
+    elif args.workload == "uvu":
+        rows = args.rows or 131072
+        torch.manual_seed(0)
+        tp = ref.UvuTensorProduct(128, 32, 3).to(device)
+        with torch.no_grad():
+            tp.weight.copy_(torch.randn(tp.weight_numel, device=device) / 32 ** 0.5)
+        gen.manual_seed(2000)
+        x = torch.randn(rows, tp.input1_dimension, device=device, generator=gen)
+        y = torch.randn(rows, tp.input2_dimension, device=device, generator=gen)
+        x.requires_grad_(True)
+        y.requires_grad_(True)
+        g = torch.ones(rows, tp.input1_dimension, device=device)
+        params = [tp.weight]
+
+        def step():
+            return torch.autograd.grad(tp(x, y), [x, y] + params, g)
+        workload = (f"UvuTensorProduct(128, 32, 3, parity='full') shared weights, forward + "
+                    f"VJP (dx, dy, dw), {rows} rows")
+    else:
+        rows = args.rows or RadialWorkload.EDGES
+        torch.manual_seed(0)
+        tp = ref.UvuTensorProduct(64, 1, 3, parity="full", parity_in2="canonical",
+                                  shared_weights=False)
+        trunk = torch.nn.Sequential(torch.nn.Linear(8, 64), torch.nn.SiLU(),
+                                    torch.nn.Linear(64, 64), torch.nn.SiLU()).to(device)
+        model = ref.RadialUvuTensorProduct(
+            tp, torch.nn.Linear(64, tp.weight_numel, bias=False)).to(device)
+        gen.manual_seed(3000)
+        nodes = torch.randn(RadialWorkload.NODES, tp.input1_dimension, device=device,
+                            generator=gen)
+        src = torch.randint(0, RadialWorkload.NODES, (rows,), device=device, generator=gen)
+        torch.randint(1, RadialWorkload.NODES, (rows,), device=device, generator=gen)
+        r = torch.rand(rows, device=device, generator=gen) * 4.5 + 0.5
+        theta = torch.rand(rows, device=device, generator=gen) * 2 * math.pi
+        x = nodes[src].contiguous().requires_grad_(True)
+        y = torch.stack([torch.ones_like(theta)] + [
+            f(m * theta) for m in range(1, 4) for f in (torch.cos, torch.sin)],
+            dim=-1).contiguous().requires_grad_(True)
+        g = torch.ones(rows, tp.input1_dimension, device=device)
+        params = list(trunk.parameters()) + list(model.parameters())
+        n = torch.arange(1, 9, device=device, dtype=r.dtype)
+        rc = RadialWorkload.RC
+
+        def step():
+            basis = (math.sqrt(2 / rc) * torch.sin(n * math.pi * r[:, None] / rc) / r[:, None]
+                     * (0.5 * (torch.cos(math.pi * r / rc) + 1))[:, None])
+            out = model(x, y, trunk(basis))
+            return torch.autograd.grad(out, [x, y] + params, g)
+        workload = (f"RadialUvuTensorProduct C64 m3 (config 5 product), {rows} edges, radial MLP "
+                    "8-64-64 SiLU in front, forward + VJP through the radial network")
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        time.sleep(0.3)
+        a.record()
+        for _ in range(args.steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        time.sleep(0.2)
+    ms = a.elapsed_time(b) / args.steps
+    unit = "edges/s" if args.workload == "radial" else "rows/s"
+    return {**base, "value": rows / (ms * 1e-3), "unit": unit, "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "dtype": "f32", "data": "synthetic (same seeds as the "
+            "ours arm)", "config": {"workload": workload, "path": "reference public API, CUDA "
+                                    "float32 inputs (its Triton kernels)"},
+            "clocks": clocks.summary()}
+
+
 def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description=__doc__,
                                      formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=5)
-    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--impl", choices=("ours", "reference", "reference_gpu"), default="ours",
+                        help="reference: the reference algorithm on the host cores (the "
+                             "comparison arm); reference_gpu: the reference package's own "
+                             "Triton path on this GPU, when installed under baseline/_ref")
     parser.add_argument("--workload", choices=tuple(WORKLOADS) + ("sweep",), default="tp")
     parser.add_argument("--rows", type=int, default=0,
                         help="rows per GPU (tp, uvu) or total edges (radial); 0 = config")
@@ -1162,8 +1280,8 @@ def main(argv=None) -> int:
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
 
-    if args.impl == "reference":
-        result = run_reference(args)
+    if args.impl in ("reference", "reference_gpu"):
+        result = run_reference(args) if args.impl == "reference" else run_reference_gpu(args)
         if result is not None:
             print(json.dumps(result), flush=True)
         return 0
