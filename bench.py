@@ -130,6 +130,81 @@ def cpu_units_per_second(workload: str, rows_per_worker: int, steps: int, warmup
 # The force-loss workload has no CPU leg: the numpy oracle has no second derivatives.
 CPU_ROWS = {"tp": 1024, "uvu": 16, "uvu_rowwise": 4, "radial": 256, "radial_m6": 64}
 
+# Rows (edges) per step of the reference package's own CPU path: about a second of
+# work per step on 16 host threads.
+REF_CPU_ROWS = {"tp": 4096, "uvu": 512, "uvu_rowwise": 32, "radial": 1024, "radial_m6": 256}
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def reference_cpu_available() -> bool:
+    return (REF_DIR / "ictc_o2_hp").is_dir()
+
+
+def reference_cpu_units_per_second(workload: str, rows: int, steps: int, warmup: int,
+                                   channels: int = 64) -> dict:
+    """Times the reference package's own CPU PyTorch path (installed under baseline/_ref;
+    CPU tensors take its PyTorch algebra, fast_o2.py / uvu_o2.py / radial_uvu.py) on all
+    host threads: forward + VJP of a seeded sample of `rows` rows per step, float32,
+    median over `steps` steps after `warmup`.  Runs before any CUDA work of the process."""
+    import torch
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    import ictc_o2_hp as ref
+    prev = torch.get_num_threads()
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    try:
+        gen = torch.Generator().manual_seed(0)
+        torch.manual_seed(0)
+        if workload == "tp":
+            tp = ref.TensorProduct(128, 6, parity="full")
+            W = tp.representation_dimension
+            x, y = (torch.randn(rows, W, generator=gen) for _ in range(2))
+            g = torch.ones(rows, W)
+            leaves, call = [tp.weight], (lambda xx, yy: tp(xx, yy))
+        elif workload in ("uvu", "uvu_rowwise"):
+            shared = workload == "uvu"
+            tp = ref.UvuTensorProduct(128, 32, 3, shared_weights=shared,
+                                      internal_weights=shared)
+            x = torch.randn(rows, tp.input1_dimension, generator=gen)
+            y = torch.randn(rows, tp.input2_dimension, generator=gen)
+            g = torch.ones(rows, tp.input1_dimension)
+            if shared:
+                leaves, call = [tp.weight], (lambda xx, yy: tp(xx, yy))
+            else:
+                w = (torch.randn(rows, tp.weight_numel, generator=gen) / 32 ** 0.5)
+                w.requires_grad_(True)
+                leaves, call = [w], (lambda xx, yy: tp(xx, yy, w))
+        else:
+            m6 = workload.startswith("radial_m6")
+            tp = ref.UvuTensorProduct(channels if m6 else 64, 1, 6 if m6 else 3, parity="full",
+                                      parity_in2="canonical", shared_weights=False)
+            model = ref.RadialUvuTensorProduct(
+                tp, torch.nn.Linear(64, tp.weight_numel, bias=False))
+            x = torch.randn(rows, tp.input1_dimension, generator=gen)
+            y = torch.randn(rows, tp.input2_dimension, generator=gen)
+            h = torch.randn(rows, 64, generator=gen).requires_grad_(True)
+            g = torch.ones(rows, tp.input1_dimension)
+            leaves = [h] + list(model.parameters())
+            call = lambda xx, yy: model(xx, yy, h)  # noqa: E731
+        x.requires_grad_(True)
+        y.requires_grad_(True)
+        values = []
+        for step in range(warmup + steps):
+            start = time.perf_counter()
+            torch.autograd.grad(call(x, y), [x, y] + leaves, g)
+            elapsed = time.perf_counter() - start
+            if step >= warmup:
+                values.append(rows / elapsed)
+    finally:
+        torch.set_num_threads(prev)
+    unit = "edges/s" if workload.startswith("radial") else "rows/s"
+    return {"value": statistics.median(values), "unit": unit, "cores": cores,
+            "kind": "reference",
+            "sample": f"{rows} rows per step through the reference package's own CPU path "
+                      f"(float32 PyTorch, {cores} threads, {workload} fwd+VJP), median of "
+                      f"{steps} steps"}
+
 
 # ------------------------------------------------------------------ clocks
 
@@ -1116,21 +1191,29 @@ def run_reference(args) -> dict | None:
                         "runs on the single-config workloads"}.get(
             args.workload, "the CPU oracle has no second derivatives (force-loss metric)")
         return {"impl": "reference", "unavailable": why}
-    rows = args.cpu_rows or CPU_ROWS[args.workload]
-    base = cpu_units_per_second(args.workload, rows, args.steps, max(1, min(args.warmup, 1)),
-                                args.channels)
+    if reference_cpu_available():
+        rows = args.cpu_rows or REF_CPU_ROWS[args.workload]
+        base = reference_cpu_units_per_second(args.workload, rows, args.steps,
+                                              max(1, min(args.warmup, 1)), args.channels)
+        how = "reference package's own CPU path"
+        per_step_ms = rows / base["value"] * 1e3
+    else:
+        rows = args.cpu_rows or CPU_ROWS[args.workload]
+        base = cpu_units_per_second(args.workload, rows, args.steps,
+                                    max(1, min(args.warmup, 1)), args.channels)
+        how = "reference algorithm, numpy port, per core"
+        per_step_ms = rows * base["cores"] / base["value"] * 1e3
     value = base["value"]
     return {
         "metric": METRICS[args.workload].format(channels=args.channels), "impl": "reference",
         "value": value,
         "unit": base["unit"], "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
         "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": rows * base["cores"] / value * 1e3, "higher_is_better": True,
+        "ms_per_step": per_step_ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded iid N(0,1) inputs, ones cotangent)",
-        "config": {"workload": f"{args.workload} forward + VJP on the host CPU (reference "
-                               f"algorithm, numpy port), bounded sample of {rows} rows per core "
-                               f"per step"},
+        "config": {"workload": f"{args.workload} forward + VJP on the host CPU ({how}), "
+                               f"bounded sample of {rows} rows per step"},
         "cpu_baseline": base,
         "e2e": {"value": value, "unit": base["unit"], "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -1295,8 +1378,12 @@ def main(argv=None) -> int:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload in CPU_ROWS:
         # The process pool starts before the first CUDA call (spawned workers).
-        cpu = cpu_units_per_second(args.workload, args.cpu_rows or CPU_ROWS[args.workload], 3, 1,
-                                   args.channels)
+        if reference_cpu_available():
+            cpu = reference_cpu_units_per_second(
+                args.workload, args.cpu_rows or REF_CPU_ROWS[args.workload], 3, 1, args.channels)
+        else:
+            cpu = cpu_units_per_second(args.workload, args.cpu_rows or CPU_ROWS[args.workload],
+                                       3, 1, args.channels)
     result = run_gpu(args)
     if result is not None:
         if cpu is not None:
