@@ -119,38 +119,56 @@ __global__ void __launch_bounds__(256, 2) uvu_dw_stage(DwArgs A) {
       *reinterpret_cast<float2*>(&S.S[u][2 * r]) =
           fma2(gv.y, t1, __fmul2_rn(make_float2(gv.x, gv.x), t0));
     }
-    // Y[(r, b)][v] = y_j[r, v, b] (zero for b >= d2)
-    for (int q = tid; q < 2 * kDwRows * kDwV; q += 256) {
-      const int rb = q / kDwV, v = q - rb * kDwV;
-      const int r = rb >> 1, b = rb & 1;
-      S.Y[rb][v] = (b < ej.y && v < A.V) ? S.ys[buf][r][v * ej.y + b] : 0.f;
+    // Y[(r, b)][v] = y_j[r, v, b] for b < d2.  The slice columns past V d2 and the
+    // rows past the chunk are zero (zero fill), so Y is zero there too.  A
+    // one-component y_j leaves the b = 1 rows of Y unused: its GEMM skips them.
+    if (ej.y == 2) {
+      // one float4 (v pair x b pair) per thread: 16 rows x 16 pairs
+      const int r = tid >> 4, vp = tid & 15;
+      const float4 q = *reinterpret_cast<const float4*>(&S.ys[buf][r][4 * vp]);
+      *reinterpret_cast<float2*>(&S.Y[2 * r][2 * vp]) = make_float2(q.x, q.z);
+      *reinterpret_cast<float2*>(&S.Y[2 * r + 1][2 * vp]) = make_float2(q.y, q.w);
+    } else if (tid < kDwRows * kDwV / 4) {
+      const int r = tid >> 3, vq = tid & 7;
+      *reinterpret_cast<float4*>(&S.Y[2 * r][4 * vq]) =
+          *reinterpret_cast<const float4*>(&S.ys[buf][r][4 * vq]);
     }
     __syncthreads();
-    // this quarter's 8 (row, b) values, two at a time
+    // this quarter's 8 (row, b) values, two at a time; b = 1 (kk = 1) only for a
+    // two-component y_j (otherwise its terms are s x 0 and leave dw unchanged)
+    auto gemm = [&](auto two) {
+      constexpr int NKK = decltype(two)::value ? 2 : 1;
 #pragma unroll 1
-    for (int k0 = 8 * kq; k0 < 8 * kq + 8; k0 += 2) {
-      float2 sa[8];
+      for (int k0 = 8 * kq; k0 < 8 * kq + 8; k0 += 2) {
+        float2 sa[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sa[i] = *reinterpret_cast<const float2*>(&S.S[uo + 16 * i][k0]);
-      float4 yb[2][2];
+        for (int i = 0; i < 8; ++i)
+          sa[i] = *reinterpret_cast<const float2*>(&S.S[uo + 16 * i][k0]);
+        float4 yb[NKK][2];
 #pragma unroll
-      for (int kk = 0; kk < 2; ++kk)
+        for (int kk = 0; kk < NKK; ++kk)
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
-          yb[kk][h] = *reinterpret_cast<const float4*>(&S.Y[k0 + kk][8 * vo + 4 * h]);
+          for (int h = 0; h < 2; ++h)
+            yb[kk][h] = *reinterpret_cast<const float4*>(&S.Y[k0 + kk][8 * vo + 4 * h]);
 #pragma unroll
-      for (int kk = 0; kk < 2; ++kk) {
-        const float2 bv[4] = {make_float2(yb[kk][0].x, yb[kk][0].y),
-                              make_float2(yb[kk][0].z, yb[kk][0].w),
-                              make_float2(yb[kk][1].x, yb[kk][1].y),
-                              make_float2(yb[kk][1].z, yb[kk][1].w)};
+        for (int kk = 0; kk < NKK; ++kk) {
+          const float2 bv[4] = {make_float2(yb[kk][0].x, yb[kk][0].y),
+                                make_float2(yb[kk][0].z, yb[kk][0].w),
+                                make_float2(yb[kk][1].x, yb[kk][1].y),
+                                make_float2(yb[kk][1].z, yb[kk][1].w)};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float a = kk == 0 ? sa[i].x : sa[i].y;
+          for (int i = 0; i < 8; ++i) {
+            const float a = kk == 0 ? sa[i].x : sa[i].y;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) acc[i][j] = fma2(a, bv[j], acc[i][j]);
+            for (int j = 0; j < 4; ++j) acc[i][j] = fma2(a, bv[j], acc[i][j]);
+          }
         }
       }
+    };
+    if (ej.y == 2) {
+      gemm(std::true_type{});
+    } else {
+      gemm(std::false_type{});
     }
   }
   asm volatile("cp.async.wait_group 0;" ::: "memory");

@@ -178,19 +178,28 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
     issue_xg(pos + 1);
     issue_w(pos + 1, buf ^ 1);
     asm volatile("cp.async.commit_group;" ::: "memory");
-    // dy[(r,b)][v] += sum_u S[u][(r,b)] w[u][v] over this warp's channels
+    // dy[(r,b)][v] += sum_u S[u][(r,b)] w[u][v] over this warp's channels; for a
+    // one-component y_j only the b = 0 entries (even m), whose sums are stored
+    auto gemm = [&](auto two) {
+      constexpr int MS = decltype(two)::value ? 1 : 2;  // m stride
 #pragma unroll 4
-    for (int i = 0; i < kDyU / 8; ++i) {
-      const int u = warp + 8 * i;
-      const float4 a0 = *reinterpret_cast<const float4*>(&S.S[u][8 * ro]);
-      const float4 a1 = *reinterpret_cast<const float4*>(&S.S[u][8 * ro + 4]);
-      const float4 b4 = *reinterpret_cast<const float4*>(&S.wp[buf][u][4 * vq]);
-      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float2 bv[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
+      for (int i = 0; i < kDyU / 8; ++i) {
+        const int u = warp + 8 * i;
+        const float4 a0 = *reinterpret_cast<const float4*>(&S.S[u][8 * ro]);
+        const float4 a1 = *reinterpret_cast<const float4*>(&S.S[u][8 * ro + 4]);
+        const float4 b4 = *reinterpret_cast<const float4*>(&S.wp[buf][u][4 * vq]);
+        const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float2 bv[2] = {make_float2(b4.x, b4.y), make_float2(b4.z, b4.w)};
 #pragma unroll
-      for (int m = 0; m < 8; ++m)
+        for (int m = 0; m < 8; m += MS)
 #pragma unroll
-        for (int k = 0; k < 2; ++k) acc[m][k] = fma2(av[m], bv[k], acc[m][k]);
+          for (int k = 0; k < 2; ++k) acc[m][k] = fma2(av[m], bv[k], acc[m][k]);
+      }
+    };
+    if (ej.y == 2) {
+      gemm(std::true_type{});
+    } else {
+      gemm(std::false_type{});
     }
     const bool last = (rc.w >> 27) & 1;
     if (last) {
