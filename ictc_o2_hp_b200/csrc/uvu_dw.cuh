@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(256, 2) uvu_dw_stage(DwArgs A) {
     // two-component y_j (otherwise its terms are s x 0 and leave dw unchanged)
     auto gemm = [&](auto two) {
       constexpr int NKK = decltype(two)::value ? 2 : 1;
-#pragma unroll 1
+#pragma unroll 2
       for (int k0 = 8 * kq; k0 < 8 * kq + 8; k0 += 2) {
         float2 sa[8];
 #pragma unroll

@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(256, 2) uvu_dy_stage(DyArgs A) {
     // one-component y_j only the b = 0 entries (even m), whose sums are stored
     auto gemm = [&](auto two) {
       constexpr int MS = decltype(two)::value ? 1 : 2;  // m stride
-#pragma unroll 4
+#pragma unroll 8
       for (int i = 0; i < kDyU / 8; ++i) {
         const int u = warp + 8 * i;
         const float4 a0 = *reinterpret_cast<const float4*>(&S.S[u][8 * ro]);

@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(UtShape<UT, NH>::NT, 1) uvu_tile(UvuTileArgs A
     const int kn = A.V - v0 < kUtVC ? A.V - v0 : kUtVC;
     const float* Wb = Wt + st * vc * UT;
     auto gemm = [&]<int D2>() {
-      for (int v = 0; v < kn; ++v) {
+      auto vstep = [&](int v) {
         float2 wv[CW / 2];
 #pragma unroll
         for (int h = 0; h < NH; ++h) {
@@ -215,6 +215,15 @@ __global__ void __launch_bounds__(UtShape<UT, NH>::NT, 1) uvu_tile(UvuTileArgs A
 #pragma unroll
             for (int j = 0; j < CW / 2; ++j) acc[b][i][j] = fma2(av[i], wv[j], acc[b][i][j]);
         }
+      };
+      // a full chunk fully unrolled (the shared-memory loads of later v issue ahead
+      // of the FMAs of earlier ones; 128 registers, no spills); a partial last
+      // chunk one v at a time
+      if (kn == kUtVC) {
+#pragma unroll
+        for (int v = 0; v < kUtVC; ++v) vstep(v);
+      } else {
+        for (int v = 0; v < kn; ++v) vstep(v);
       }
     };
     if (ej.y == 2) gemm.template operator()<2>(); else gemm.template operator()<1>();
