@@ -469,8 +469,15 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
         for (int j = 0; j < CW / 2; ++j) acc[i][j] = fma2(av[i], bv[j], acc[i][j]);
     };
     if (kn == kRtKC) {
+      // the forward unrolls a full chunk completely (no spills at 128 registers); the
+      // dx tile, whose epilogue holds more live values, by 8
+      if constexpr (MODE == kRtFwd) {
+#pragma unroll
+        for (int k = 0; k < kRtKC; ++k) kstep(k);
+      } else {
 #pragma unroll 8
-      for (int k = 0; k < kRtKC; ++k) kstep(k);
+        for (int k = 0; k < kRtKC; ++k) kstep(k);
+      }
     } else {
       for (int k = 0; k < kn; ++k) kstep(k);
     }
