@@ -75,13 +75,19 @@ __global__ void __launch_bounds__(kGemmThreads, A_KMAJOR ? 4 : 3) sgemm_tile(Sge
       }
     }
   };
+  // Transposed into As[k][m ^ swz(k)]: swz(k) = 8 ((k / 4) % 4) puts the four lanes
+  // that share a row m (k quads 0, 4, 8, 12) on different banks, so a warp's stores
+  // are conflict-free (unswizzled: 4-way conflicts).  The swizzle keeps aligned
+  // 4-column groups whole, so the GEMM's float4 reads stay single accesses.
   auto store_a_rows = [&](int buf) {
+    const int sw = (tid & 3) << 3;  // swz(ak + j) for j < 4
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      As[buf][ak + 0][ar + 32 * i] = areg[i].x;
-      As[buf][ak + 1][ar + 32 * i] = areg[i].y;
-      As[buf][ak + 2][ar + 32 * i] = areg[i].z;
-      As[buf][ak + 3][ar + 32 * i] = areg[i].w;
+      const int col = (ar + 32 * i) ^ sw;
+      As[buf][ak + 0][col] = areg[i].x;
+      As[buf][ak + 1][col] = areg[i].y;
+      As[buf][ak + 2][col] = areg[i].z;
+      As[buf][ak + 3][col] = areg[i].w;
     }
   };
   // k-major A [K][M] and B [K][N] tiles by cp.async (zero-filled outside)
@@ -131,8 +137,9 @@ __global__ void __launch_bounds__(kGemmThreads, A_KMAJOR ? 4 : 3) sgemm_tile(Sge
     }
 #pragma unroll
     for (int kk = 0; kk < kGemmBK; ++kk) {
-      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][tm * 4]);
-      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + tm * 4]);
+      const int sw = A_KMAJOR ? 0 : ((kk >> 2) & 3) << 3;  // swz(kk) of the [M][K] variant
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][(tm * 4) ^ sw]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][(64 + tm * 4) ^ sw]);
       const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tn * 4]);
       const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][32 + tn * 4]);
       const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
