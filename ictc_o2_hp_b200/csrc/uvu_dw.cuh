@@ -10,8 +10,9 @@
 // Y[(row, b)][v]; then the GEMM over K = (row, b) accumulates dw_p.  Each thread
 // holds an 8 u x 8 v tile (channels uo + 16 i, v = 8 vo .. 8 vo + 7) over a quarter of
 // each step's 32 (row, b) values; the four quarters are summed in a fixed order at
-// the end.  Chunks are summed in a fixed order afterwards.  Needs U <= 128, V <= 32
-// and 16-byte aligned rows.
+// the end.  Chunks are summed in a fixed order afterwards.  A one-component y_j
+// (scalar second-input entry) has no b = 1 terms: its GEMM runs over the b = 0 half of
+// K only.  Needs U <= 128, V <= 32 and 16-byte aligned rows.
 //
 // This header is included inside the anonymous namespace of uvu_kernels.cu.
 #pragma once

@@ -8,8 +8,9 @@
 // weights w_p[U][V] arrive by cp.async one path ahead; s_p is built from shared
 // memory into S[u][(row, b)] and then contracted over u (GEMM: an 8 (row, b) x 4 v
 // tile per thread; warp w takes the channels u = w + 8 i; the eight warps' sums are
-// added in a fixed order, a three-round tree, when the j group ends).  Needs U <= 128, V <= 32 and 16-byte aligned rows; other shapes use
-// uvu_dy_tile.
+// added in a fixed order, a three-round tree, when the j group ends).  For a
+// one-component y_j the GEMM skips the b = 1 entries, whose sums are never stored.
+// Needs U <= 128, V <= 32 and 16-byte aligned rows; other shapes use uvu_dy_tile.
 //
 // This header is included inside the anonymous namespace of uvu_kernels.cu.
 #pragma once
