@@ -469,9 +469,9 @@ __global__ void __launch_bounds__(RtShape<UT, NH>::NT, 1) radial_tile(RadTileArg
         for (int j = 0; j < CW / 2; ++j) acc[i][j] = fma2(av[i], bv[j], acc[i][j]);
     };
     if (kn == kRtKC) {
-      // the forward unrolls a full chunk completely (no spills at 128 registers); the
-      // dx tile, whose epilogue holds more live values, by 8
-      if constexpr (MODE == kRtFwd) {
+      // the forward and the 512-thread dx tile unroll a full chunk completely; the
+      // 384-thread dx tile by 8 (fully unrolled it was 4 % slower at config 5)
+      if constexpr (MODE == kRtFwd || NH == 1) {
 #pragma unroll
         for (int k = 0; k < kRtKC; ++k) kstep(k);
       } else {
