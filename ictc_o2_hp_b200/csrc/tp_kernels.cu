@@ -750,6 +750,108 @@ __global__ void __launch_bounds__(kWideWarps * 32, 1)
   });
 }
 
+// path_forward for a row pair: the two rows are the halves of float2 values, so each
+// product and output update is one paired FMA, each half rounded exactly as the
+// scalar form (bit-identical per row).
+template <int M, bool FULL, int I>
+__device__ __forceinline__ void path_forward2(const float2* a, const float2* b, float2* o,
+                                              float w) {
+  using P = Paths<M, FULL>;
+  constexpr ChanPath cp = P::table.p[I];
+  float2 s[2];
+  static_for<cp.nt>([&](auto T) {
+    constexpr Term t = P::table.p[I].t[T];
+    mac2<first_term<M, FULL, I, T, 0>(), t.s>(s[t.k], a[P::table.p[I].in1 + t.i],
+                                               b[P::table.p[I].in2 + t.j]);
+  });
+  o[cp.out] = fma2w(w, s[0], o[cp.out]);
+  if constexpr (slot_dim(cp.out) == 2) o[cp.out + 1] = fma2w(w, s[1], o[cp.out + 1]);
+}
+
+// tp_forward_wide on row pairs: each warp takes two rows per stage block (the halves of
+// its float2 operands), half the FMA instructions per row, on CTAs of kWidePairWarps
+// warps (no register cap below 255: the pair state is three float2 rows of slots).
+// A missing second row (odd row count) computes on zeros and stores nothing.
+constexpr int kWidePairWarps = 8;
+
+template <int M, bool FULL, bool CM = false>
+__global__ void __launch_bounds__(kWidePairWarps * 32, 1)
+    tp_forward_wide_paired(const float* __restrict__ x, const float* __restrict__ y,
+                           const float* __restrict__ w, float* __restrict__ out, int64_t rows,
+                           TpLayout L, Mags mags, int groups, int R, int stages) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  using P = Paths<M, FULL>;
+  constexpr int S = 2 * M + 2;
+  const int warp = threadIdx.x >> 5;
+  const int T = groups * 32;
+  const int t = (warp % groups) * 32 + (threadIdx.x & 31);
+  const LaneMap<FULL> lm(warp % groups, threadIdx.x & 31, L.C);
+  float4* wsm = reinterpret_cast<float4*>(smem + kBarrierBytes);
+  if (warp < groups) {
+    static_for<P::chunks>([&](auto k) {
+      float v[4];
+      static_for<4>([&](auto e) {
+        constexpr int pos = 4 * k + e;
+        if constexpr (pos < P::n) {
+          constexpr int I = P::vjp.idx[pos];
+          constexpr ChanPath cp = P::table.p[I];
+          const bool used = lm.active && (!FULL || cp.copied || lm.q == 0);
+          v[e] = used ? __ldg(w + weight_index<M, FULL, I>(L.C, lm.c, lm.q)) * mags.m[cp.cls]
+                      : 0.0f;
+        } else {
+          v[e] = 0.0f;
+        }
+      });
+      wsm[k * T + t] = make_float4(v[0], v[1], v[2], v[3]);
+    });
+  }
+  __syncthreads();
+  const SharedChunks chunks{static_cast<uint32_t>(__cvta_generic_to_shared(wsm + t)),
+                            T * static_cast<int>(sizeof(float4))};
+  const size_t wbytes = static_cast<size_t>(P::chunks) * T * sizeof(float4);
+  const float* src[2] = {x, y};
+  const int64_t W = L.width;
+  const int RB = 2 * R;  // rows per stage block
+  staged_loop<2, false, 2>(smem, smem + wbytes, stages, R, rows, W, src,
+                           [&](const float* stage, int64_t row) {
+    const bool two = row + 1 < rows;
+    float2 a[S], b[S], o[S];
+    auto load_pair = [&](const float* base, float2 (&v)[S]) {
+      float u0[S], u1[S];
+      load_slots<M, FULL, CM>(SharedRow(base), L, lm.c, lm.q, u0);
+      load_slots<M, FULL, CM>(SharedRow(base + W), L, lm.c, lm.q, u1);
+#pragma unroll
+      for (int k = 0; k < S; ++k) v[k] = make_float2(u0[k], two ? u1[k] : 0.f);
+    };
+    load_pair(stage, a);
+    load_pair(stage + RB * W, b);
+#pragma unroll
+    for (int i = 0; i < S; ++i) o[i] = make_float2(0.f, 0.f);
+    float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    auto step = [&](auto K) {
+      constexpr int I = P::vjp.idx[K];
+      if constexpr (K % 4 == 0) w4 = chunks.ld(K / 4);
+      const float wv = K % 4 == 0 ? w4.x : (K % 4 == 1 ? w4.y : (K % 4 == 2 ? w4.z : w4.w));
+      path_forward2<M, FULL, I>(a, b, o, wv);
+    };
+    static_for<P::nfreq>(step);
+    if (!FULL || lm.q == 0) {
+      static_for<P::n - P::nfreq>(
+          [&](auto J) { step(std::integral_constant<int, P::nfreq + J>{}); });
+    }
+    if (lm.active) {
+      float v0[S], v1[S];
+#pragma unroll
+      for (int k = 0; k < S; ++k) {
+        v0[k] = o[k].x;
+        v1[k] = o[k].y;
+      }
+      store_slots<M, FULL, CM>(out + row * W, L, lm.c, lm.q, true, v0);
+      if (two) store_slots<M, FULL, CM>(out + (row + 1) * W, L, lm.c, lm.q, true, v1);
+    }
+  });
+}
+
 // Forward with the group's path weights in shared memory: a CTA of
 // kGroupFwdWarps warps serves ONE channel group and its warps take rows round-
 // robin, so the weights (float4 chunks in Paths::vjp order, built at start from
@@ -1202,6 +1304,7 @@ struct Kernels {
   ForwardGroupedFn fwd_grouped;
   BackwardTiledFn bwd_tiled;
   BackwardStagedFn bwd_paired;  // row pairs through paired f32x2 arithmetic, or null
+  ForwardStagedFn fwd_wide_paired;  // null when the weights do not fit in shared memory
 };
 
 // Row-paired backward where the sweep measured it faster than the scalar staged kernel:
@@ -1225,10 +1328,11 @@ constexpr Kernels kernels_for() {
                    &tp_forward_staged<M, FULL, CM>, &tp_backward_staged<M, FULL, CM>,
                    &prescale_kernel<M, FULL>, Paths<M, FULL>::chunks,
                    &tp_forward_grouped<M, FULL, CM>, &tp_backward_tiled<M, FULL, CM>,
-                   paired_for<M, FULL, CM>()};
+                   paired_for<M, FULL, CM>(),
+                   wide == nullptr ? nullptr : &tp_forward_wide_paired<M, FULL, CM>};
   } else {
     return Kernels{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0, nullptr, nullptr,
-                   nullptr};
+                   nullptr, nullptr};
   }
 }
 
@@ -1587,8 +1691,32 @@ int32_t tp_forward_impl(const float* left, const float* right, const float* weig
   // memory) from m_max = 4 up, where its rows are long enough to keep the bulk
   // copies busy; below that, and when it does not fit, the grouped kernel.
   // Measured over the benchmark sweep (C 32..256, m_max 1..6, both parities).
+  // Row-paired wide forward by default at full parity from m_max = 4 up where its
+  // 8-warp CTA is full (channel groups dividing 8): measured at 65,536 rows after an
+  // L2 flush, C = 128 full m_max 6 / 5 / 4 0.470 -> 0.418 / 0.388 -> 0.361 / 0.321 ->
+  // 0.311 ms, C = 64 and 32 full m_max 6 0.243 -> 0.218 and 0.130 -> 0.118 ms; it lost
+  // at C = 96 full (six groups: 0.373 -> 0.375 ms) and at canonical parity (C = 128
+  // m_max 6: 0.202 -> 0.212 ms), which keep the wide kernel.
+  const int fwd_groups = static_cast<int>(ceil_div(channels, full ? 16 : 32));
+  const bool want_pair =
+      (variant == nullptr && full && m_max >= 4 && kWidePairWarps % fwd_groups == 0) ||
+      (variant != nullptr && strcmp(variant, "widepair") == 0);
+  const StagedPlan pp =
+      (want_pair && k.fwd_wide_paired && al16)
+          ? plan_staged(device, rows, L, full, 2, weight_chunk_bytes(k, channels, full),
+                        kWidePairWarps, 2, true, 1, 2)
+          : StagedPlan{};
+  if (pp.ok) {
+    if ((st = allow_smem(reinterpret_cast<const void*>(k.fwd_wide_paired), pp.smem)) != ICTC_OK)
+      return st;
+    k.fwd_wide_paired<<<static_cast<unsigned>(pp.grid), pp.warps * 32, pp.smem, s>>>(
+        left, right, weight, output, rows, L, mags, pp.groups, pp.R, pp.stages);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? ICTC_OK : cuda_fail(e, "tp_forward launch");
+  }
   const bool want_wide = (variant == nullptr && m_max >= 4) ||
-                         (variant != nullptr && strcmp(variant, "wide") == 0);
+                         (variant != nullptr &&
+                          (strcmp(variant, "wide") == 0 || want_pair));  // also the fallback
   const StagedPlan wp =
       (want_wide && k.fwd_wide && al16)
           ? plan_staged(device, rows, L, full, 2, weight_chunk_bytes(k, channels, full),

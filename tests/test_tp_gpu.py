@@ -248,6 +248,7 @@ def test_tuple_and_component_major_layouts(cuda_device):
     (9, 4, "full", 50, "direct"),      # odd channel count, direct kernels
     (32, 2, "full", 640, "grouped"),
     (256, 3, "full", 200, None),       # channel-tiled backward
+    (128, 6, "full", 1001, "widepair"),  # row-paired wide forward, odd row count
 ])
 def test_component_major_in_place(channels, m_max, parity, rows, variant, cuda_device,
                                   monkeypatch):
@@ -282,7 +283,31 @@ def test_component_major_in_place(channels, m_max, parity, rows, variant, cuda_d
     assert torch.equal(sm[1], sf[1])
 
 
-@pytest.mark.parametrize("variant", ["staged", "wide", "direct", "grouped"])
+@pytest.mark.parametrize("channels,m_max,parity,rows", [
+    (128, 6, "full", 333),       # the benchmark configuration's width, odd row count
+    (32, 4, "canonical", 1001),  # four rows per stage block
+    (96, 5, "full", 64),         # six channel groups
+    (64, 6, "canonical", 4097),
+])
+def test_row_paired_wide_forward_matches_wide(channels, m_max, parity, rows, cuda_device,
+                                              monkeypatch):
+    """The row-paired wide forward (ICTC_TP_FORWARD=widepair: two rows per warp as the
+    halves of paired f32x2 operations) is bit-identical to the wide forward."""
+    from ictc_o2_hp_b200 import TensorProduct, _lib
+    torch.manual_seed(channels + rows)
+    tp = TensorProduct(channels, m_max, parity=parity).to(cuda_device)
+    x = torch.randn(rows, tp.representation_dimension, device=cuda_device)
+    y = torch.randn_like(x)
+    with torch.no_grad():
+        monkeypatch.setenv("ICTC_TP_FORWARD", "wide")
+        ref = tp(x, y)
+        monkeypatch.setenv("ICTC_TP_FORWARD", "widepair")
+        got = tp(x, y)
+    assert torch.equal(got, ref)
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("variant", ["staged", "wide", "direct", "grouped", "widepair"])
 def test_forward_variants_agree(variant, cuda_device, monkeypatch):
     """Every forward kernel selectable with ICTC_TP_FORWARD (staged ring, wide
     staged, register-weight direct, shared-weight grouped) gives the same values
