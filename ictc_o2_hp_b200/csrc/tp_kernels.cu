@@ -673,6 +673,33 @@ __global__ void __launch_bounds__(kStagedWarps * 32, 1)
   });
 }
 
+// The magnitude-scaled path weights of thread t (channel lm.c, world lm.q) as float4
+// chunks in Paths::vjp order, chunk k at wsm[k * T + t] (T threads per row); unused
+// entries (scalar-output paths of world 1, inactive lanes, the last chunk's tail) are 0.
+template <int M, bool FULL>
+__device__ __forceinline__ void build_weight_chunks(const float* __restrict__ w,
+                                                    const TpLayout& L, const Mags& mags,
+                                                    const LaneMap<FULL>& lm, int T, int t,
+                                                    float4* wsm) {
+  using P = Paths<M, FULL>;
+  static_for<P::chunks>([&](auto k) {
+    float v[4];
+    static_for<4>([&](auto e) {
+      constexpr int pos = 4 * k + e;
+      if constexpr (pos < P::n) {
+        constexpr int I = P::vjp.idx[pos];
+        constexpr ChanPath cp = P::table.p[I];
+        const bool used = lm.active && (!FULL || cp.copied || lm.q == 0);
+        v[e] = used ? __ldg(w + weight_index<M, FULL, I>(L.C, lm.c, lm.q)) * mags.m[cp.cls]
+                    : 0.0f;
+      } else {
+        v[e] = 0.0f;
+      }
+    });
+    wsm[k * T + t] = make_float4(v[0], v[1], v[2], v[3]);
+  });
+}
+
 // Forward with the path weights in shared memory instead of registers: with
 // register use capped at 128, CTAs of 16 warps (two rows per stage) fit on an SM,
 // twice the warps of the register-weight variant.  The weights are laid out as
@@ -703,24 +730,7 @@ __global__ void __launch_bounds__(kWideWarps * 32, 1)
   const int t = (warp % groups) * 32 + (threadIdx.x & 31);
   const LaneMap<FULL> lm(warp % groups, threadIdx.x & 31, L.C);
   float4* wsm = reinterpret_cast<float4*>(smem + kBarrierBytes);
-  if (warp < groups) {
-    static_for<P::chunks>([&](auto k) {
-      float v[4];
-      static_for<4>([&](auto e) {
-        constexpr int pos = 4 * k + e;
-        if constexpr (pos < P::n) {
-          constexpr int I = P::vjp.idx[pos];
-          constexpr ChanPath cp = P::table.p[I];
-          const bool used = lm.active && (!FULL || cp.copied || lm.q == 0);
-          v[e] = used ? __ldg(w + weight_index<M, FULL, I>(L.C, lm.c, lm.q)) * mags.m[cp.cls]
-                      : 0.0f;
-        } else {
-          v[e] = 0.0f;
-        }
-      });
-      wsm[k * T + t] = make_float4(v[0], v[1], v[2], v[3]);
-    });
-  }
+  if (warp < groups) build_weight_chunks<M, FULL>(w, L, mags, lm, T, t, wsm);
   __syncthreads();
   const SharedChunks chunks{static_cast<uint32_t>(__cvta_generic_to_shared(wsm + t)),
                             T * static_cast<int>(sizeof(float4))};
@@ -787,24 +797,7 @@ __global__ void __launch_bounds__(kWidePairWarps * 32, 1)
   const int t = (warp % groups) * 32 + (threadIdx.x & 31);
   const LaneMap<FULL> lm(warp % groups, threadIdx.x & 31, L.C);
   float4* wsm = reinterpret_cast<float4*>(smem + kBarrierBytes);
-  if (warp < groups) {
-    static_for<P::chunks>([&](auto k) {
-      float v[4];
-      static_for<4>([&](auto e) {
-        constexpr int pos = 4 * k + e;
-        if constexpr (pos < P::n) {
-          constexpr int I = P::vjp.idx[pos];
-          constexpr ChanPath cp = P::table.p[I];
-          const bool used = lm.active && (!FULL || cp.copied || lm.q == 0);
-          v[e] = used ? __ldg(w + weight_index<M, FULL, I>(L.C, lm.c, lm.q)) * mags.m[cp.cls]
-                      : 0.0f;
-        } else {
-          v[e] = 0.0f;
-        }
-      });
-      wsm[k * T + t] = make_float4(v[0], v[1], v[2], v[3]);
-    });
-  }
+  if (warp < groups) build_weight_chunks<M, FULL>(w, L, mags, lm, T, t, wsm);
   __syncthreads();
   const SharedChunks chunks{static_cast<uint32_t>(__cvta_generic_to_shared(wsm + t)),
                             T * static_cast<int>(sizeof(float4))};
